@@ -1,0 +1,90 @@
+/* exl3b200.h -- the C ABI of libexl3b200.so, the B200 (sm_100a) library of the EXL3 routed-expert ops.
+ *
+ * 1. THE PLUGIN BOUNDARY. The library is a radiance kernel plugin (ABI 17), exporting exactly what the
+ *    reference's device library exports (kernels/exl3r4d/rows.c:524-550) and the reference library's
+ *    schemas (kernels/exl3ref/rows.c:249-258): the engine dlopens it, reads the schemas and the rows, and
+ *    calls a row's `launch(const RadArgs*, RadStream)` with device pointers and a cudaStream_t. The rows
+ *    serve moe_exl3_gate_up, moe_exl3_down, moe_exl3_prep_gu, moe_exl3_gate_up_down and their _mod4 forms
+ *    (include/exl3_abi.h:160-288), every K 2..8 and every codebook.
+ *
+ * 2. DIRECT ENTRY POINTS (plain pointers and sizes) for a caller that holds its operands itself: the
+ *    decode, the relayout, and the routing steps either side of the ops (router, scatter, gather).
+ *
+ * Every entry returns 0 (RAD_OK) or a negative status; nothing is written on a refusal. Device work is
+ * enqueued on `stream` (a cudaStream_t; null = the legacy default stream) and is asynchronous: no entry
+ * point on a launch path allocates, synchronises or reads the environment. */
+#ifndef EXL3B200_H
+#define EXL3B200_H
+
+#include <stdint.h>
+
+#include "rad_abi.h"
+#include "rad_plugin.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ------------------------------------------------------------------ 1. the plugin exports */
+
+/* == RAD_ABI_VERSION (kernels/exl3ref/rows.c:249). */
+uint32_t             rad_plugin_abi_version(void);
+/* {RAD_PLUGIN_KERNEL, "exl3b200", version, description, "sm_100a"} (kernels/exl3r4d/rows.c:528-534). */
+const RadPluginInfo* rad_plugin_info(void);
+/* The eight EXL3 schemas, identical to the reference's (include/exl3_abi.h:366-627;
+ * kernels/exl3ref/rows.c:253-254). */
+int                  rad_kernel_schema_count(void);
+const RadOpSchema*   rad_kernel_schema_at(int i);
+/* The device rows (kernels/exl3r4d/rows.c:369-520 are the rows these replace). */
+int                  rad_kernel_count(void);
+const RadKernelInfo* rad_kernel_at(int i);
+/* Every row may run concurrently with itself: no state survives a launch (kernels/exl3r4d/rows.c:550). */
+int                  rad_kernel_concurrent(int i);
+
+/* ------------------------------------------------------------------ 2. direct entry points */
+
+/* The stored form of a codes plane: the tile-stream record. Replaces the relayout / unrelayout hooks'
+ * conversions (kernels/exl3r4d/layout.c:33-140; common/exl3_layout.h:31-42). Host memory. */
+int exl3b200_codes_to_record(const uint8_t* codes, int64_t row_bytes, int64_t rows, int64_t cols, int bits,
+                             uint16_t* record);
+int exl3b200_record_to_codes(const uint16_t* record, int64_t rows, int64_t cols, int bits, uint8_t* codes,
+                             int64_t row_bytes);
+
+/* W_hat of one [rows, cols] record as fp16 bits, [rows][cols] (radiance's [n][k] view), on the device:
+ * the decode every kernel runs, bit-exact with common/exl3_decode.c exl3_decode_what_rows
+ * (common/exl3_decode.h:157-160). bits 1..8, codebook 0 3inst / 1 mcg / 2 mul1. */
+int exl3b200_decode_what(const void* record, int64_t rows, int64_t cols, int bits, int codebook, void* w_hat,
+                         void* stream);
+
+/* Routing, the steps either side of the ops (the engine's router_topk / moe_scatter / moe_gather, whose
+ * contract include/exl3_abi.h:90-158 states; docs/OPS-exl3.md:195-196 for the gather):
+ *   router_topk:  logits f32 [n_tok, n_expert] -> softmax over all experts, the top_k largest (ties to the
+ *                 lower id) as ids i32 [n_tok, top_k] and their probabilities w f32 [n_tok, top_k], in
+ *                 descending order. n_expert <= 4096, top_k <= 32.
+ *   moe_scatter:  a stable counting sort of the flattened pairs t*top_k + s by expert id - expert_base;
+ *                 ids outside [0, n_expert) dropped; sorted_tok i32 [n_pairs] (-1 past the live count),
+ *                 expert_offset i32 [n_expert + 1]. `work` is caller-provided device memory of
+ *                 exl3b200_moe_scatter_work_bytes() bytes.
+ *   moe_gather:   y f32 [n_tok][width] = sum over slots ascending of w * bf16 row of that slot's sorted row
+ *                 (a dropped slot adds nothing); `rows` bf16 with row pitch `row_pitch` elements. `work` is
+ *                 caller-provided device memory of exl3b200_moe_gather_work_bytes() bytes. */
+int     exl3b200_router_topk(const float* logits, int64_t n_tok, int64_t n_expert, int64_t top_k, int32_t* ids,
+                             float* w, void* stream);
+int64_t exl3b200_moe_scatter_work_bytes(int64_t n_pairs, int64_t n_expert);
+int     exl3b200_moe_scatter(const int32_t* ids, int64_t n_pairs, int64_t n_expert, int64_t expert_base,
+                             int32_t* sorted_tok, int32_t* expert_offset, void* work, void* stream);
+int64_t exl3b200_moe_gather_work_bytes(int64_t n_tok, int64_t top_k);
+int     exl3b200_moe_gather(const uint16_t* rows, int64_t row_pitch, const int32_t* sorted_tok, int64_t n_rows,
+                            const float* w, int64_t n_tok, int64_t top_k, int64_t width, float* y, void* work,
+                            void* stream);
+
+/* The device error word of the current device: nonzero once a bounded wait inside a kernel gave up (the
+ * launch then finished without a valid result). Reading it synchronises the device; `clear` resets it. Not
+ * for a launch path. */
+int exl3b200_read_error(int clear, int32_t* value);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* EXL3B200_H */

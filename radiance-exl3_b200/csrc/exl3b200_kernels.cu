@@ -1,0 +1,797 @@
+// exl3b200_kernels.cu -- the sm_100a kernels of the EXL3 routed-expert path and the extern "C" shim the C
+// host side calls. Hand-written CUDA; no library kernel is on this path.
+//
+//   k_decode_what    record -> W_hat fp16, one warp a 16x16 tile (the bit-exact decode, test vehicle)
+//   k_prep           moe_exl3_prep_gu: xr = f16(had(f16(a[tok] * suh))) | ... suh.1, per sorted row
+//   k_gemm_skinny    the decode band: trellis decode in registers straight into mma.sync B fragments,
+//                    the packed record streamed by a producer warp with cp.async.bulk (TMA) into a
+//                    shared-memory ring, split-K over a thread-block cluster reduced through distributed
+//                    shared memory, and the output rotation / svh / SiLU*up / h_rot epilogue.
+//
+// Semantics are the reference's (docs/OPS-exl3.md:84-153; kernels/exl3ref/ref.c:27-228). The decode is
+// bit-exact against common/exl3_decode.c:47-144: every codebook value is produced by the same single
+// fp16 rounding (HFMA2 / HADD2, round to nearest even) of the same exact operands. The rotations run the
+// butterfly stages h = 1, 2, ..., 64 in f32 in exactly the order of common/exl3_decode.c:172-189, so the
+// prologue's xr matches the reference bit for bit.
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+#include "exl3b200_dev.h"
+
+namespace {
+
+constexpr float kRs = 0.08838834764831844055f;   // (float)(1 / sqrt(128))
+constexpr int kWaitLimit = 1 << 24;               // bounded mbarrier waits (then the error word is set)
+
+// ------------------------------------------------------------------------------------------ small helpers
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ float h2f(uint16_t h) { return __half2float(__ushort_as_half(h)); }
+__device__ __forceinline__ uint16_t f2h(float f) { return __half_as_ushort(__float2half_rn(f)); }
+__device__ __forceinline__ float bf2f(uint16_t h) { return __bfloat162float(__ushort_as_bfloat16(h)); }
+__device__ __forceinline__ uint16_t f2bf(float f) { return __bfloat16_as_ushort(__float2bfloat16_rn(f)); }
+
+// Entry j of a plane table (stacked or pointer table).
+__device__ __forceinline__ const void* tab_entry(const Exl3bTab& t, int64_t j) {
+    if (t.stride_bytes == 0) return reinterpret_cast<const void* const*>(t.base)[j];
+    return static_cast<const uint8_t*>(t.base) + j * t.stride_bytes;
+}
+
+// ------------------------------------------------------------------------------------------ codebooks
+// Two states -> one half2 (low = first). mul1: fp16(1024 + bytesum(s * 0x83DCD12D)) is built exactly as the
+// bits 0x6400 + bytesum (dp4a with that addend), then ONE fp16 FMA by K_INV (0x1EEE) plus K_BIAS (0xC931).
+// mcg / 3inst: (h & 0x8FFF8FFF) ^ 0x3B603B60, the two fp16 halves added once. common/exl3_decode.c:43-67.
+template <int CB>
+__device__ __forceinline__ uint32_t cb_pair(uint32_t s0, uint32_t s1) {
+    if constexpr (CB == 2) {
+        const uint32_t x0 = s0 * 0x83DCD12Du, x1 = s1 * 0x83DCD12Du;
+        const uint32_t u0 = __dp4a(x0, 0x01010101u, 0x6400u);
+        const uint32_t u1 = __dp4a(x1, 0x01010101u, 0x6400u);
+        const uint32_t h = __byte_perm(u0, u1, 0x5410);
+        const __half2 kinv = __halves2half2(__ushort_as_half(0x1EEE), __ushort_as_half(0x1EEE));
+        const __half2 kbias = __halves2half2(__ushort_as_half(0xC931), __ushort_as_half(0xC931));
+        const __half2 r = __hfma2(*reinterpret_cast<const __half2*>(&h), kinv, kbias);
+        return *reinterpret_cast<const uint32_t*>(&r);
+    } else {
+        uint32_t x0, x1;
+        if constexpr (CB == 1) {
+            x0 = s0 * 0xCBAC1FEDu;
+            x1 = s1 * 0xCBAC1FEDu;
+        } else {
+            x0 = s0 * 89226354u + 64248484u;
+            x1 = s1 * 89226354u + 64248484u;
+        }
+        x0 = (x0 & 0x8FFF8FFFu) ^ 0x3B603B60u;
+        x1 = (x1 & 0x8FFF8FFFu) ^ 0x3B603B60u;
+        const uint32_t lo = __byte_perm(x0, x1, 0x5410), hi = __byte_perm(x0, x1, 0x7632);
+        const __half2 r = __hadd2(*reinterpret_cast<const __half2*>(&lo), *reinterpret_cast<const __half2*>(&hi));
+        return *reinterpret_cast<const uint32_t*>(&r);
+    }
+}
+
+// ------------------------------------------------------------------------------------------ one tile, one lane
+// Lane L of a warp decodes trellis positions 8L .. 8L+7 of a 16x16 tile (8K u32 words, one MSB-first stream,
+// circular). Position 8L+j's 16-bit state is the stream window ending at bit (8L+j+1)K. The eight positions
+// are exactly the mma.m16n8k16 B fragments of the tile's two n8 halves (k = 2(L%4) + {0,1,8,9},
+// n = L/4 and L/4 + 8), so the four returned half2 are: b[0], b[1] the first n8 block's fragment registers,
+// b[2], b[3] the second's.
+//
+// The lane's windows all fall in a 64-bit (K <= 4) or 96-bit (K >= 5) span that starts on a 16-bit
+// boundary with its first window at offset 16..31; each state is then one clamped funnel shift.
+template <int BITS, int CB>
+__device__ __forceinline__ void decode_lane(const uint32_t* __restrict__ w, int lane, uint32_t b[4]) {
+    constexpr int NW = 8 * BITS;                           // words in the tile
+    constexpr int NB = 256 * BITS;                         // bits in the tile
+    uint32_t st[8];
+    if constexpr (BITS == 4) {
+        // window of position 8L+j at offset 20 + 4j of (word L-1 : word L)
+        const uint32_t hi = w[(lane + NW - 1) % NW], lo = w[lane];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) st[j] = __funnelshift_r(lo, hi, 28 - 4 * j) & 0xFFFFu;
+    } else {
+        const int base = ((8 * lane + 1) * BITS - 16 + NB) % NB;   // first window's start bit
+        const int a = base >> 5, off = base & 31;
+        const int sh16 = off < 16 ? 16 : 0;                        // realign so the first window sits at 16..31
+        const int offp = off + sh16;
+        const uint32_t wm1 = w[(a + NW - 1) % NW], wa = w[a], wb = w[(a + 1) % NW];
+        const uint32_t h = __funnelshift_r(wa, wm1, sh16);         // stream bits [32a - sh16, +32)
+        const uint32_t m = __funnelshift_r(wb, wa, sh16);          // the next 32
+        if constexpr (BITS <= 4) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) st[j] = __funnelshift_rc(m, h, 48 - offp - j * BITS) & 0xFFFFu;
+        } else {
+            const uint32_t wc = w[(a + 2) % NW];
+            const uint32_t l = __funnelshift_r(wc, wb, sh16);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const int q = offp + j * BITS;
+                const uint32_t v0 = __funnelshift_rc(m, h, 48 - q);
+                const uint32_t v1 = __funnelshift_rc(l, m, 80 - q);
+                st[j] = (q <= 48 ? v0 : v1) & 0xFFFFu;
+            }
+        }
+    }
+    b[0] = cb_pair<CB>(st[0], st[1]);
+    b[1] = cb_pair<CB>(st[2], st[3]);
+    b[2] = cb_pair<CB>(st[4], st[5]);
+    b[3] = cb_pair<CB>(st[6], st[7]);
+}
+
+// ------------------------------------------------------------------------------------------ 128-point rotation
+// A warp holds one 128-vector, lane l the elements 4l .. 4l+3. Stages h = 1, 2 inside the lane, h = 4 .. 64
+// across lanes; a+b stays low, a-b goes high, exactly as common/exl3_decode.c:179-185; then x (float)(1/sqrt(128)).
+__device__ __forceinline__ void had128_warp(float v[4], int lane) {
+    float a, b;
+    a = v[0]; b = v[1]; v[0] = __fadd_rn(a, b); v[1] = __fsub_rn(a, b);
+    a = v[2]; b = v[3]; v[2] = __fadd_rn(a, b); v[3] = __fsub_rn(a, b);
+    a = v[0]; b = v[2]; v[0] = __fadd_rn(a, b); v[2] = __fsub_rn(a, b);
+    a = v[1]; b = v[3]; v[1] = __fadd_rn(a, b); v[3] = __fsub_rn(a, b);
+#pragma unroll
+    for (int m = 1; m < 32; m <<= 1) {
+        const bool high = (lane & m) != 0;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float p = __shfl_xor_sync(0xFFFFFFFFu, v[i], m);
+            v[i] = high ? __fsub_rn(p, v[i]) : __fadd_rn(v[i], p);
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) v[i] = __fmul_rn(v[i], kRs);
+}
+
+// f16(had(f16(x * s))) of one 128-block held as above (kernels/exl3ref/ref.c:27-32).
+__device__ __forceinline__ void prologue_warp(float v[4], const uint16_t* __restrict__ s, int lane) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) v[i] = h2f(f2h(__fmul_rn(v[i], h2f(s[4 * lane + i]))));
+    had128_warp(v, lane);
+}
+
+// ------------------------------------------------------------------------------------------ mbarrier / TMA
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+// Bounded wait for the phase of `parity`; false (and the error word set) when it never completed.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int32_t* err) {
+    const uint32_t a = smem_u32(bar);
+    for (int i = 0; i < kWaitLimit; ++i) {
+        uint32_t done;
+        asm volatile(
+            "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+            : "=r"(done)
+            : "r"(a), "r"(parity)
+            : "memory");
+        if (done) return true;
+    }
+    if (err) atomicOr(err, 1);
+    return false;
+}
+// One bulk (non-tensor) TMA copy global -> this CTA's shared memory, completing on `bar`. 16-byte aligned
+// addresses and a size that is a multiple of 16 (the host refuses weights that are not).
+__device__ __forceinline__ void tma_bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ float4 ld_dsmem_f4(const float* local, uint32_t rank) {
+    uint32_t remote;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_u32(local)), "r"(rank));
+    float4 v;
+    asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "r"(remote)
+                 : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void ldmatrix_x4(uint32_t r[4], const void* p) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(smem_u32(p)));
+}
+__device__ __forceinline__ void mma16816(float c[4], const uint32_t a[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %2, %3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// ------------------------------------------------------------------------------------------ the decode (test vehicle)
+template <int BITS, int CB>
+__global__ void k_decode_what(const uint32_t* __restrict__ record, int64_t rows, int64_t cols,
+                              uint16_t* __restrict__ out) {
+    const int lane = threadIdx.x & 31;
+    const int64_t nt = rows / 16, kt = cols / 16;
+    const int64_t tile = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+    if (tile >= nt * kt) return;
+    const int64_t tk = tile / nt, tn = tile % nt;
+    uint32_t b[4];
+    decode_lane<BITS, CB>(record + tile * 8 * BITS, lane, b);
+    const int g = lane >> 2, t = lane & 3;
+    // b[0]: (n = g, k = 2t, 2t+1); b[1]: (n = g, k = 2t+8, +9); b[2], b[3]: n + 8
+    const int64_t n0 = tn * 16 + g, k0 = tk * 16 + 2 * t;
+    uint32_t* o = reinterpret_cast<uint32_t*>(out);
+    o[(n0 * cols + k0) / 2] = b[0];
+    o[(n0 * cols + k0 + 8) / 2] = b[1];
+    o[((n0 + 8) * cols + k0) / 2] = b[2];
+    o[((n0 + 8) * cols + k0 + 8) / 2] = b[3];
+}
+
+// ------------------------------------------------------------------------------------------ expert lookups
+struct ExpertView {
+    int c;
+    int64_t j, R, C;
+};
+__device__ __forceinline__ ExpertView expert_view(const Exl3bOp& op, int64_t e) {
+    ExpertView v;
+    v.c = (int)(e % op.n_class);
+    v.j = e / op.n_class;
+    v.R = op.cls[v.c].rows;
+    v.C = op.cls[v.c].cols;
+    return v;
+}
+__device__ __forceinline__ bool row_live(const Exl3bOp& op, int64_t i) {
+    return i >= op.expert_offset[0] && i < op.expert_offset[op.n_expert] && op.sorted_tok[i] >= 0;
+}
+
+// ------------------------------------------------------------------------------------------ prep_gu
+// One warp a (sorted row, 128-block of the class's input width); both halves. Rows outside the runs are not
+// written; a row whose sorted_tok is negative is zero across 2C (docs/OPS-exl3.md:128-142).
+__global__ void k_prep(const Exl3bOp op) {
+    const int lane = threadIdx.x & 31;
+    const int64_t nblk = op.x_cols / 128;
+    const int64_t task = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+    const int64_t i = task / nblk, blk = task % nblk;
+    if (i >= op.T) return;
+    const int64_t lo = op.expert_offset[0], hi = op.expert_offset[op.n_expert];
+    if (i < lo || i >= hi) return;
+    // the owner: largest e with off[e] <= i
+    int64_t a = 0, b = op.n_expert;
+    while (b - a > 1) {
+        const int64_t mid = (a + b) / 2;
+        if (op.expert_offset[mid] <= i) a = mid; else b = mid;
+    }
+    const ExpertView ev = expert_view(op, a);
+    if (blk * 128 >= ev.C) return;
+    uint16_t* y = static_cast<uint16_t*>(op.y) + i * op.y_pitch;
+    const int32_t tok = op.sorted_tok[i];
+    for (int half = 0; half < 2; ++half) {
+        uint16_t* dst = y + half * ev.C + blk * 128 + 4 * lane;
+        if (tok < 0) {
+#pragma unroll
+            for (int q = 0; q < 4; ++q) dst[q] = 0;
+            continue;
+        }
+        const uint16_t* src = static_cast<const uint16_t*>(op.x) + (int64_t)(tok / op.top_k) * op.x_pitch + blk * 128;
+        float v[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) v[q] = op.x_bf16 ? bf2f(src[4 * lane + q]) : h2f(src[4 * lane + q]);
+        const Exl3bTab& st = half ? op.cls[ev.c].suh1 : op.cls[ev.c].suh;
+        prologue_warp(v, static_cast<const uint16_t*>(tab_entry(st, ev.j)) + blk * 128, lane);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) dst[q] = f2h(v[q]);
+    }
+}
+
+// ------------------------------------------------------------------------------------------ the decode-band GEMM
+//
+// Unit = (expert e, row group g of up to 16*MCH of its rows, output block b of 128 columns). A cluster of
+// `ksplit` CTAs runs one unit, CTA r taking 128-column chunks [r*nch/S, (r+1)*nch/S) of the class's input
+// width; the partial sums meet in the cluster leader's shared memory (in rank order: deterministic).
+// Persistent: the clusters walk the unit list, which every CTA derives from expert_offset the same way.
+//
+// Warps 0..7 decode and multiply; warp 8 is the producer (cp.async.bulk of each k-tile row of the block's
+// eight tiles, per matrix, into an NST-stage ring). For gate_up, warp w owns the gate tile w and the up tile
+// w of the block (matrices 0 and 1); for down, tile w.
+constexpr int kConsumerWarps = 8;
+constexpr int kThreads = (kConsumerWarps + 1) * 32;
+constexpr int kNst = 8;      // ring stages
+constexpr int kTks = 4;      // k-tile rows a stage
+
+template <int BITS, bool GU>
+struct SkinnyCfg {
+    static constexpr int MATS = GU ? 2 : 1;
+    static constexpr int TILE_WORDS = 8 * BITS;
+    static constexpr int COPY_BYTES = 8 * TILE_WORDS * 4;          // the block's 8 tiles of one k row
+    static constexpr int STAGE_BYTES = kTks * MATS * COPY_BYTES;
+    static constexpr int RED_COLS = MATS * 128 + 4;                 // f32 partial sums a row (padded)
+};
+
+// Shared-memory layout (bytes): [bars 256][unit prefix (n_expert+1) u32, 16-aligned][ring][xr / red]
+__host__ __device__ inline int64_t skinny_prefix_bytes(int64_t n_expert) { return ((n_expert + 1) * 4 + 15) / 16 * 16; }
+
+template <int BITS, int CB, bool GU, int MCH>
+__global__ void __launch_bounds__(kThreads, 1) k_gemm_skinny(const Exl3bOp op, int ksplit, int kc_max, int n_blocks) {
+    using Cfg = SkinnyCfg<BITS, GU>;
+    constexpr int MMAX = 16 * MCH;
+    constexpr int MATS = Cfg::MATS;
+    extern __shared__ __align__(128) uint8_t smem[];
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+    uint64_t* empty = full + kNst;
+    int* s_misc = reinterpret_cast<int*>(smem + 2 * kNst * 8);           // [0] n_units
+    uint32_t* prefix = reinterpret_cast<uint32_t*>(smem + 256);
+    uint8_t* ring = smem + 256 + skinny_prefix_bytes(op.n_expert);
+    uint8_t* xr_raw = ring + kNst * Cfg::STAGE_BYTES;
+    const int xr_stride = kc_max + 8;                                     // halves a row (+16 B: no ldmatrix conflicts)
+    uint16_t* xr = reinterpret_cast<uint16_t*>(xr_raw);                   // [MATS][MMAX][xr_stride]
+    float* red = reinterpret_cast<float*>(xr_raw);                        // [MMAX][RED_COLS] (aliases xr)
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int S = ksplit;
+    const uint32_t rank = S > 1 ? cluster_rank() : 0;
+    const int64_t cluster_id = blockIdx.y, n_clusters = gridDim.y;
+    const int64_t n_exp = op.n_expert;
+
+    if (tid == 0) {
+        for (int s = 0; s < kNst; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kConsumerWarps);
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    // ---- the unit list: units of expert e = ceil(rows_e / MMAX) * n_blocks (block-scan of the counts)
+    {
+        __shared__ uint32_t part[kThreads];
+        const int64_t per = (n_exp + kThreads - 1) / kThreads;
+        const int64_t e0 = tid * per, e1 = e0 + per < n_exp ? e0 + per : n_exp;
+        uint32_t sum = 0;
+        for (int64_t e = e0; e < e1; ++e) {
+            const int64_t r = op.expert_offset[e + 1] - op.expert_offset[e];
+            sum += r > 0 ? (uint32_t)(((r + MMAX - 1) / MMAX) * n_blocks) : 0u;
+        }
+        part[tid] = sum;
+        __syncthreads();
+        if (tid == 0) {
+            uint32_t acc = 0;
+            for (int t = 0; t < kThreads; ++t) {
+                const uint32_t v = part[t];
+                part[t] = acc;
+                acc += v;
+            }
+            s_misc[0] = (int)acc;
+        }
+        __syncthreads();
+        uint32_t acc = part[tid];
+        for (int64_t e = e0; e < e1; ++e) {
+            prefix[e] = acc;
+            const int64_t r = op.expert_offset[e + 1] - op.expert_offset[e];
+            acc += r > 0 ? (uint32_t)(((r + MMAX - 1) / MMAX) * n_blocks) : 0u;
+        }
+        if (tid == 0) prefix[n_exp] = (uint32_t)s_misc[0];
+    }
+    __syncthreads();
+    if (S > 1) cluster_sync_all();
+    const int64_t n_units = s_misc[0];
+
+    // ---- rows no unit writes: zero (outside the runs, or a dropped slot), across the whole width
+    {
+        const int64_t gcta = cluster_id * S + rank, ncta = n_clusters * S;
+        for (int64_t i = gcta; i < op.T; i += ncta) {
+            if (row_live(op, i)) continue;
+            if (GU) {
+                uint16_t* y = static_cast<uint16_t*>(op.y) + i * op.y_pitch;
+                for (int64_t c = tid; c < op.y_cols; c += kThreads) y[c] = 0;
+            } else {
+                uint16_t* y = static_cast<uint16_t*>(op.y) + i * op.y_pitch;
+                for (int64_t c = tid; c < op.y_cols; c += kThreads) y[c] = 0;
+            }
+        }
+    }
+
+    uint32_t it = 0;   // ring position, advanced identically by producer and consumers
+    for (int64_t unit = cluster_id; unit < n_units; unit += n_clusters) {
+        // which expert: the last e with prefix[e] <= unit
+        int64_t lo = 0, hi = n_exp;
+        while (hi - lo > 1) {
+            const int64_t mid = (lo + hi) / 2;
+            if ((int64_t)prefix[mid] <= unit) lo = mid; else hi = mid;
+        }
+        const int64_t e = lo;
+        const int64_t local = unit - prefix[e];
+        const int64_t grp = local / n_blocks, blk = local % n_blocks;
+        const ExpertView ev = expert_view(op, e);
+        const Exl3bClass& cl = op.cls[ev.c];
+        const int64_t r0 = op.expert_offset[e] + grp * MMAX;
+        const int64_t rend = op.expert_offset[e + 1];
+        const int nr = (int)(rend - r0 < MMAX ? rend - r0 : MMAX);
+        const int64_t width = GU ? ev.R / 2 : ev.R;                       // output columns of this class
+        if (blk * 128 >= width) {
+            // a narrower class: its rows are zero past its own width
+            if (rank == 0 && warp < kConsumerWarps)
+                for (int m = warp; m < nr; m += kConsumerWarps) {
+                    const int64_t i = r0 + m;
+                    if (!row_live(op, i)) continue;
+                    uint16_t* y = static_cast<uint16_t*>(op.y) + i * op.y_pitch + blk * 128;
+                    for (int q = lane; q < 128; q += 32) y[q] = 0;
+                }
+            continue;
+        }
+        const int64_t nch = ev.C / 128;
+        const int64_t ch0 = nch * rank / S, ch1 = nch * (rank + 1) / S;
+        const int64_t k0 = ch0 * 128;
+        const int ntk = (int)((ch1 - ch0) * 8);
+        const int nstages = (ntk + kTks - 1) / kTks;
+
+        if (warp == kConsumerWarps) {
+            // ------------------------------------------------ producer
+            if (lane == 0) {
+                const uint16_t* rec = static_cast<const uint16_t*>(tab_entry(cl.codes, ev.j));
+                const int64_t wrows = GU ? ev.R / 2 : ev.R;                  // rows of one record
+                const int64_t mat_elems = (ev.C / 16) * (wrows / 16) * 16 * BITS;
+                for (int sidx = 0; sidx < nstages; ++sidx, ++it) {
+                    const uint32_t s = it % kNst, ph = (it / kNst) & 1;
+                    mbar_wait(&empty[s], ph ^ 1, op.err);
+                    const int tk_first = sidx * kTks;
+                    const int n_in = ntk - tk_first < kTks ? ntk - tk_first : kTks;
+                    mbar_expect_tx(&full[s], (uint32_t)(n_in * MATS * Cfg::COPY_BYTES));
+                    for (int q = 0; q < n_in; ++q) {
+                        const int64_t tk = ch0 * 8 + tk_first + q;
+                        for (int mat = 0; mat < MATS; ++mat) {
+                            const uint16_t* src = rec + mat * mat_elems + (tk * (wrows / 16) + blk * 8) * 16 * BITS;
+                            tma_bulk_g2s(ring + s * Cfg::STAGE_BYTES + (q * MATS + mat) * Cfg::COPY_BYTES, src,
+                                         Cfg::COPY_BYTES, &full[s]);
+                        }
+                    }
+                }
+            } else {
+                it += nstages;
+            }
+            __syncwarp();
+        } else {
+            // ------------------------------------------------ consumers: the rotated input rows into xr
+            const int nchl = (int)(ch1 - ch0);
+            for (int task = warp; task < MATS * MMAX * nchl; task += kConsumerWarps) {
+                const int mat = task / (MMAX * nchl);
+                const int m = (task / nchl) % MMAX;
+                const int chl = task % nchl;
+                uint16_t* dst = xr + ((int64_t)mat * MMAX + m) * xr_stride + chl * 128 + 4 * lane;
+                const int64_t i = r0 + m;
+                const int32_t tok = m < nr ? op.sorted_tok[i] : -1;
+                float v[4] = { 0.f, 0.f, 0.f, 0.f };
+                if (tok >= 0) {
+                    const int64_t kk = k0 + chl * 128 + 4 * lane;
+                    const uint16_t* xs;
+                    bool rotate;
+                    const uint16_t* s = nullptr;
+                    if (GU) {
+                        if (op.a_rot) {
+                            xs = static_cast<const uint16_t*>(op.x) + i * op.x_pitch + mat * ev.C + kk;
+                            rotate = false;
+                        } else {
+                            xs = static_cast<const uint16_t*>(op.x) + (int64_t)(tok / op.top_k) * op.x_pitch + kk;
+                            rotate = true;
+                            s = static_cast<const uint16_t*>(tab_entry(mat ? cl.suh1 : cl.suh, ev.j)) + k0 + chl * 128;
+                        }
+                    } else {
+                        xs = static_cast<const uint16_t*>(op.x) + i * op.x_pitch + kk;
+                        rotate = !op.h_rot;
+                        if (rotate) s = static_cast<const uint16_t*>(tab_entry(cl.suh, ev.j)) + k0 + chl * 128;
+                    }
+                    const bool bf = GU && !op.a_rot && op.x_bf16;
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) v[q] = bf ? bf2f(xs[q]) : h2f(xs[q]);
+                    if (rotate) {
+                        prologue_warp(v, s, lane);
+                    }
+                }
+#pragma unroll
+                for (int q = 0; q < 4; ++q) dst[q] = f2h(v[q]);
+            }
+            asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");
+
+            // ------------------------------------------------ main loop
+            float acc[MATS][MCH][2][4];
+#pragma unroll
+            for (int mt = 0; mt < MATS; ++mt)
+#pragma unroll
+                for (int mc = 0; mc < MCH; ++mc)
+#pragma unroll
+                    for (int nb = 0; nb < 2; ++nb)
+#pragma unroll
+                        for (int q = 0; q < 4; ++q) acc[mt][mc][nb][q] = 0.f;
+            const int arow = (lane & 7) + 8 * ((lane >> 3) & 1), acol = 8 * (lane >> 4);
+            for (int sidx = 0; sidx < nstages; ++sidx, ++it) {
+                const uint32_t s = it % kNst, ph = (it / kNst) & 1;
+                mbar_wait(&full[s], ph, op.err);
+                const int tk_first = sidx * kTks;
+                const int n_in = ntk - tk_first < kTks ? ntk - tk_first : kTks;
+                for (int q = 0; q < n_in; ++q) {
+                    const int tkl = tk_first + q;                       // k-tile index inside this CTA's range
+#pragma unroll
+                    for (int mat = 0; mat < MATS; ++mat) {
+                        const uint32_t* words = reinterpret_cast<const uint32_t*>(
+                            ring + s * Cfg::STAGE_BYTES + (q * MATS + mat) * Cfg::COPY_BYTES) + warp * Cfg::TILE_WORDS;
+                        uint32_t b[4];
+                        decode_lane<BITS, CB>(words, lane, b);
+#pragma unroll
+                        for (int mc = 0; mc < MCH; ++mc) {
+                            uint32_t a[4];
+                            ldmatrix_x4(a, xr + ((int64_t)mat * MMAX + mc * 16 + arow) * xr_stride + tkl * 16 + acol);
+                            mma16816(acc[mat][mc][0], a, b[0], b[1]);
+                            mma16816(acc[mat][mc][1], a, b[2], b[3]);
+                        }
+                    }
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&empty[s]);
+            }
+            // partial sums -> red (aliases xr: every consumer warp must be done reading it)
+            asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");
+            const int g = lane >> 2, t = lane & 3;
+#pragma unroll
+            for (int mat = 0; mat < MATS; ++mat)
+#pragma unroll
+                for (int mc = 0; mc < MCH; ++mc)
+#pragma unroll
+                    for (int nb = 0; nb < 2; ++nb) {
+                        const int col = mat * 128 + warp * 16 + nb * 8 + 2 * t;
+                        float* r0p = red + (mc * 16 + g) * Cfg::RED_COLS + col;
+                        float* r1p = red + (mc * 16 + g + 8) * Cfg::RED_COLS + col;
+                        r0p[0] = acc[mat][mc][nb][0];
+                        r0p[1] = acc[mat][mc][nb][1];
+                        r1p[0] = acc[mat][mc][nb][2];
+                        r1p[1] = acc[mat][mc][nb][3];
+                    }
+        }
+        if (S > 1) cluster_sync_all(); else __syncthreads();
+
+        // ---------------------------------------------------- epilogue in the leader
+        if (rank == 0 && warp < kConsumerWarps) {
+            for (int m = warp; m < nr; m += kConsumerWarps) {
+                const int64_t i = r0 + m;
+                if (op.sorted_tok[i] < 0) continue;
+                float v[MATS][4];
+#pragma unroll
+                for (int mat = 0; mat < MATS; ++mat) {
+                    const float* src = red + m * Cfg::RED_COLS + mat * 128 + 4 * lane;
+                    float4 sum = *reinterpret_cast<const float4*>(src);
+                    for (int r = 1; r < S; ++r) {
+                        const float4 p = ld_dsmem_f4(src, (uint32_t)r);
+                        sum.x = __fadd_rn(sum.x, p.x);
+                        sum.y = __fadd_rn(sum.y, p.y);
+                        sum.z = __fadd_rn(sum.z, p.z);
+                        sum.w = __fadd_rn(sum.w, p.w);
+                    }
+                    v[mat][0] = sum.x; v[mat][1] = sum.y; v[mat][2] = sum.z; v[mat][3] = sum.w;
+                    had128_warp(v[mat], lane);
+                }
+                const uint16_t* svh = static_cast<const uint16_t*>(tab_entry(cl.svh, ev.j));
+                if (GU) {
+                    const int64_t W = ev.R / 2;
+                    const int64_t n0 = blk * 128 + 4 * lane;
+                    float h[4];
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        const float gte = __fmul_rn(v[0][q], h2f(svh[n0 + q]));
+                        const float up = __fmul_rn(v[MATS - 1][q], h2f(svh[W + n0 + q]));
+                        const float sg = __fmul_rn(gte, __frcp_rn(__fadd_rn(1.0f, expf(-gte))));
+                        h[q] = __fmul_rn(sg, up);
+                    }
+                    uint16_t* y = static_cast<uint16_t*>(op.y) + i * op.y_pitch + n0;
+                    if (op.h_rot) {
+                        const uint16_t* dn = static_cast<const uint16_t*>(tab_entry(cl.dn_suh, ev.j)) + blk * 128;
+#pragma unroll
+                        for (int q = 0; q < 4; ++q) h[q] = h2f(f2h(h[q]));
+                        prologue_warp(h, dn, lane);
+                    }
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) y[q] = f2h(h[q]);
+                } else {
+                    const int64_t n0 = blk * 128 + 4 * lane;
+                    uint16_t* y = static_cast<uint16_t*>(op.y) + i * op.y_pitch + n0;
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) y[q] = f2bf(__fmul_rn(v[0][q], h2f(svh[n0 + q])));
+                }
+            }
+        }
+        if (S > 1) cluster_sync_all(); else __syncthreads();
+    }
+}
+
+// Shared memory a skinny launch needs.
+int64_t skinny_smem(int bits, int gu, int mch, int64_t kc_max, int64_t n_expert) {
+    const int mats = gu ? 2 : 1, mmax = 16 * mch;
+    const int64_t stage = (int64_t)kTks * mats * 8 * 8 * bits * 4;
+    const int64_t xr = (int64_t)mats * mmax * (kc_max + 8) * 2;
+    const int64_t red = (int64_t)mmax * (mats * 128 + 4) * 4;
+    return 256 + skinny_prefix_bytes(n_expert) + kNst * stage + (xr > red ? xr : red);
+}
+
+template <int BITS, int CB, bool GU, int MCH>
+int launch_skinny_t(const Exl3bOp* op, const Exl3bPlan* p, int kc_max, int n_blocks, cudaStream_t st) {
+    auto kern = k_gemm_skinny<BITS, CB, GU, MCH>;
+    const int smem = p->smem_bytes;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) return -6;
+    if (p->ksplit > 1 &&
+        cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess)
+        return -6;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)p->ksplit, (unsigned)p->clusters, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = (size_t)smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = (unsigned)p->ksplit;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, *op, p->ksplit, kc_max, n_blocks);
+    return e == cudaSuccess ? 0 : -6;
+}
+
+template <int BITS, bool GU, int MCH>
+int launch_skinny_cb(const Exl3bOp* op, const Exl3bPlan* p, int kc_max, int n_blocks, cudaStream_t st) {
+    switch (op->codebook) {
+    case 0: return launch_skinny_t<BITS, 0, GU, MCH>(op, p, kc_max, n_blocks, st);
+    case 1: return launch_skinny_t<BITS, 1, GU, MCH>(op, p, kc_max, n_blocks, st);
+    case 2: return launch_skinny_t<BITS, 2, GU, MCH>(op, p, kc_max, n_blocks, st);
+    default: return -1;
+    }
+}
+
+template <int BITS, bool GU>
+int launch_skinny_m(const Exl3bOp* op, const Exl3bPlan* p, int kc_max, int n_blocks, cudaStream_t st) {
+    switch (p->mch) {
+    case 1: return launch_skinny_cb<BITS, GU, 1>(op, p, kc_max, n_blocks, st);
+    case 2: return launch_skinny_cb<BITS, GU, 2>(op, p, kc_max, n_blocks, st);
+    case 4: return launch_skinny_cb<BITS, GU, 4>(op, p, kc_max, n_blocks, st);
+    default: return -1;
+    }
+}
+
+template <bool GU>
+int launch_skinny_b(const Exl3bOp* op, const Exl3bPlan* p, int kc_max, int n_blocks, cudaStream_t st) {
+    switch (op->bits) {
+    case 2: return launch_skinny_m<2, GU>(op, p, kc_max, n_blocks, st);
+    case 3: return launch_skinny_m<3, GU>(op, p, kc_max, n_blocks, st);
+    case 4: return launch_skinny_m<4, GU>(op, p, kc_max, n_blocks, st);
+    case 5: return launch_skinny_m<5, GU>(op, p, kc_max, n_blocks, st);
+    case 6: return launch_skinny_m<6, GU>(op, p, kc_max, n_blocks, st);
+    case 7: return launch_skinny_m<7, GU>(op, p, kc_max, n_blocks, st);
+    case 8: return launch_skinny_m<8, GU>(op, p, kc_max, n_blocks, st);
+    default: return -1;
+    }
+}
+
+}  // namespace
+
+// ============================================================================================ the C shim
+extern "C" {
+
+static inline cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
+
+int exl3b_cuda_decode_what(const void* record, int64_t rows, int64_t cols, int bits, int codebook, void* out,
+                           void* stream) {
+    if (!record || !out || rows <= 0 || cols <= 0 || rows % 16 || cols % 16) return -1;
+    const int64_t tiles = (rows / 16) * (cols / 16);
+    const int wpb = 8;
+    const dim3 grid((unsigned)((tiles + wpb - 1) / wpb)), block(wpb * 32);
+    const uint32_t* r = static_cast<const uint32_t*>(record);
+    uint16_t* o = static_cast<uint16_t*>(out);
+    cudaStream_t st = as_stream(stream);
+#define EXL3B_DW(B, C) k_decode_what<B, C><<<grid, block, 0, st>>>(r, rows, cols, o)
+#define EXL3B_DW_CB(B)                    \
+    switch (codebook) {                   \
+    case 0: EXL3B_DW(B, 0); break;        \
+    case 1: EXL3B_DW(B, 1); break;        \
+    case 2: EXL3B_DW(B, 2); break;        \
+    default: return -1;                   \
+    }
+    switch (bits) {
+    case 1: EXL3B_DW_CB(1); break;
+    case 2: EXL3B_DW_CB(2); break;
+    case 3: EXL3B_DW_CB(3); break;
+    case 4: EXL3B_DW_CB(4); break;
+    case 5: EXL3B_DW_CB(5); break;
+    case 6: EXL3B_DW_CB(6); break;
+    case 7: EXL3B_DW_CB(7); break;
+    case 8: EXL3B_DW_CB(8); break;
+    default: return -1;
+    }
+#undef EXL3B_DW_CB
+#undef EXL3B_DW
+    return cudaGetLastError() == cudaSuccess ? 0 : -6;
+}
+
+int exl3b_cuda_prep(const Exl3bOp* op, void* stream) {
+    if (op->T <= 0) return 0;
+    const int64_t tasks = op->T * (op->x_cols / 128);
+    const int wpb = 8;
+    k_prep<<<(unsigned)((tasks + wpb - 1) / wpb), wpb * 32, 0, as_stream(stream)>>>(*op);
+    return cudaGetLastError() == cudaSuccess ? 0 : -6;
+}
+
+// Plan a decode-band launch: the rows a unit holds, the K split and the persistent grid. `sm_count` and the
+// occupancy come from the device the caller queried once (no query on the launch path).
+int exl3b_plan_skinny(const Exl3bOp* op, int sm_count, Exl3bPlan* p) {
+    const int gu = op->op == EXL3B_OP_GATE_UP;
+    int64_t cmin = op->cls[0].cols, wmax = 0;
+    for (int c = 0; c < op->n_class; ++c) {
+        if (op->cls[c].cols < cmin) cmin = op->cls[c].cols;
+        const int64_t w = gu ? op->cls[c].rows / 2 : op->cls[c].rows;
+        if (w > wmax) wmax = w;
+    }
+    const int64_t n_blocks = wmax / 128;
+    const int64_t live = op->n_expert < op->T ? op->n_expert : op->T;
+    const int64_t rows_per = live > 0 ? (op->T + live - 1) / live : 1;
+    int mch = rows_per <= 16 ? 1 : rows_per <= 32 ? 2 : 4;
+    const int64_t mmax = 16 * mch;
+    const int64_t units = (live + op->T / mmax + 1) * n_blocks;
+    // split K until the units fill the machine twice over (a power of two, at most 8, at most the chunks)
+    int S = 1;
+    const int64_t nch_min = cmin / 128;
+    while (S < 8 && units * S < 2 * sm_count && 2 * S <= nch_min) S *= 2;
+    int64_t kc_max = 0;
+    for (int c = 0; c < op->n_class; ++c) {
+        const int64_t nch = op->cls[c].cols / 128;
+        const int64_t per = (nch + S - 1) / S * 128;
+        if (per > kc_max) kc_max = per;
+    }
+    int64_t smem = skinny_smem(op->bits, gu, mch, kc_max, op->n_expert);
+    while (smem > 220 * 1024 && mch > 1) {           // keep one CTA an SM possible
+        mch /= 2;
+        smem = skinny_smem(op->bits, gu, mch, kc_max, op->n_expert);
+    }
+    while (smem > 220 * 1024 && S < 8 && 2 * S <= nch_min) {
+        S *= 2;
+        kc_max = 0;
+        for (int c = 0; c < op->n_class; ++c) {
+            const int64_t nch = op->cls[c].cols / 128;
+            const int64_t per = (nch + S - 1) / S * 128;
+            if (per > kc_max) kc_max = per;
+        }
+        smem = skinny_smem(op->bits, gu, mch, kc_max, op->n_expert);
+    }
+    if (smem > 227 * 1024) return -1;
+    const int64_t per_sm = smem <= 56 * 1024 ? 4 : smem <= 75 * 1024 ? 3 : smem <= 113 * 1024 ? 2 : 1;
+    int64_t clusters = sm_count * per_sm / S;
+    const int64_t units_max = (live + op->T / (16 * mch) + 1) * n_blocks;
+    if (clusters > units_max) clusters = units_max;
+    if (clusters < 1) clusters = 1;
+    p->ksplit = S;
+    p->mch = mch;
+    p->clusters = (int)clusters;
+    p->smem_bytes = (int)smem;
+    return 0;
+}
+
+int exl3b_cuda_gemm_skinny(const Exl3bOp* op, const Exl3bPlan* p, void* stream) {
+    const int gu = op->op == EXL3B_OP_GATE_UP;
+    int64_t wmax = 0, kc_max = 0;
+    for (int c = 0; c < op->n_class; ++c) {
+        const int64_t w = gu ? op->cls[c].rows / 2 : op->cls[c].rows;
+        if (w > wmax) wmax = w;
+        const int64_t nch = op->cls[c].cols / 128;
+        const int64_t per = (nch + p->ksplit - 1) / p->ksplit * 128;
+        if (per > kc_max) kc_max = per;
+    }
+    cudaStream_t st = as_stream(stream);
+    return gu ? launch_skinny_b<true>(op, p, (int)kc_max, (int)(wmax / 128), st)
+              : launch_skinny_b<false>(op, p, (int)kc_max, (int)(wmax / 128), st);
+}
+
+}  // extern "C"

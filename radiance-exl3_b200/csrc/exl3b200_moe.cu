@@ -1,0 +1,294 @@
+// exl3b200_moe.cu -- the routing steps on either side of the routed-expert ops, and the device bookkeeping the
+// host side needs (SM count, the error word). sm_100a CUDA, extern "C" shim.
+//
+//   k_router_topk     softmax over all experts, top-k (ties to the lower id), one warp a token
+//   k_scatter_*       a STABLE counting sort of the flattened (token, slot) pairs by expert: the routing
+//                     contract of include/exl3_abi.h:96-158 (sorted_tok, expert_offset, -1 past the live count)
+//   k_gather          y[t] = sum over slots ascending of w[t,s] * row of (t,s), f32 (docs/OPS-exl3.md:195-196)
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+#include "exl3b200_dev.h"
+
+namespace {
+
+__device__ int32_t g_err_word;   // set by a kernel whose bounded wait gave up
+
+constexpr int kScatterChunk = 1024;   // pairs a block of the large-sort path
+constexpr int kSmallPairs = 8192;     // at most this many pairs: one block does the whole sort
+
+// ------------------------------------------------------------------------------------------ router
+// One warp a token: softmax over n_expert logits (max, then sum of exp in lane-strided order reduced by a
+// butterfly), then top_k rounds of a warp argmax (larger logit first, lower id on a tie).
+__global__ void k_router_topk(const float* __restrict__ logits, int64_t n_tok, int n_expert, int top_k,
+                              int32_t* __restrict__ ids, float* __restrict__ w) {
+    const int lane = threadIdx.x & 31;
+    const int64_t t = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+    if (t >= n_tok) return;
+    const float* l = logits + t * n_expert;
+    float mx = -INFINITY;
+    for (int e = lane; e < n_expert; e += 32) mx = fmaxf(mx, l[e]);
+    for (int m = 16; m; m >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, m));
+    float s = 0.f;
+    for (int e = lane; e < n_expert; e += 32) s += expf(l[e] - mx);
+    for (int m = 16; m; m >>= 1) s += __shfl_xor_sync(0xFFFFFFFFu, s, m);
+    uint32_t taken[4] = { 0u, 0u, 0u, 0u };   // lane's experts e = lane + 32 * q, q < 128 (n_expert <= 4096)
+    for (int r = 0; r < top_k; ++r) {
+        float best = -INFINITY;
+        int bid = 0x7FFFFFFF;
+        for (int q = 0, e = lane; e < n_expert; ++q, e += 32) {
+            if ((taken[q >> 5] >> (q & 31)) & 1u) continue;
+            const float v = l[e];
+            if (v > best || (v == best && e < bid)) { best = v; bid = e; }
+        }
+        for (int m = 16; m; m >>= 1) {
+            const float ov = __shfl_xor_sync(0xFFFFFFFFu, best, m);
+            const int oid = __shfl_xor_sync(0xFFFFFFFFu, bid, m);
+            if (ov > best || (ov == best && oid < bid)) { best = ov; bid = oid; }
+        }
+        if (bid != 0x7FFFFFFF && (bid & 31) == lane) {
+            const int q = bid >> 5;
+            taken[q >> 5] |= 1u << (q & 31);
+        }
+        if (lane == 0) {
+            ids[t * top_k + r] = bid == 0x7FFFFFFF ? -1 : bid;
+            w[t * top_k + r] = bid == 0x7FFFFFFF ? 0.f : expf(best - mx) / s;
+        }
+    }
+}
+
+// ------------------------------------------------------------------------------------------ scatter
+__device__ __forceinline__ int local_expert(int32_t id, int64_t base, int n_expert) {
+    const int64_t e = (int64_t)id - base;
+    return e >= 0 && e < n_expert ? (int)e : -1;
+}
+
+// Stable placement of one chunk of up to 1024 pairs (one a thread, in order), the running per-expert
+// positions in `run` (shared). Warps go one after another, so pairs of one expert land in flat order.
+__device__ __forceinline__ void place_chunk(const int32_t* ids, int64_t c0, int64_t n_pairs, int64_t base, int n_expert,
+                                            int* run, int32_t* sorted_tok) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
+    const int64_t f = c0 + tid;
+    const int e = f < n_pairs ? local_expert(ids[f], base, n_expert) : -1;
+    const unsigned peers = __match_any_sync(0xFFFFFFFFu, e);
+    const int rank = __popc(peers & ((1u << lane) - 1u));
+    const int leader = __ffs(peers) - 1;
+    for (int w = 0; w < nw; ++w) {
+        if (warp == w && e >= 0) {
+            sorted_tok[run[e] + rank] = (int32_t)f;
+            __syncwarp(peers);
+            if (lane == leader) run[e] += __popc(peers);
+        }
+        __syncthreads();
+    }
+}
+
+// The whole sort in one block (few pairs): histogram, scan, stable placement, tail of -1.
+__global__ void k_scatter_small(const int32_t* __restrict__ ids, int64_t n_pairs, int n_expert, int64_t base,
+                                int32_t* __restrict__ sorted_tok, int32_t* __restrict__ off) {
+    extern __shared__ int sm[];
+    int* cnt = sm;                 // [n_expert + 1]
+    const int tid = threadIdx.x;
+    for (int e = tid; e <= n_expert; e += blockDim.x) cnt[e] = 0;
+    __syncthreads();
+    for (int64_t f = tid; f < n_pairs; f += blockDim.x) {
+        const int e = local_expert(ids[f], base, n_expert);
+        if (e >= 0) atomicAdd(&cnt[e], 1);
+    }
+    __syncthreads();
+    if (tid == 0) {
+        int acc = 0;
+        for (int e = 0; e < n_expert; ++e) {
+            const int v = cnt[e];
+            cnt[e] = acc;
+            off[e] = acc;
+            acc += v;
+        }
+        off[n_expert] = acc;
+        cnt[n_expert] = acc;
+    }
+    __syncthreads();
+    const int live = cnt[n_expert];
+    for (int64_t f = live + tid; f < n_pairs; f += blockDim.x) sorted_tok[f] = -1;
+    for (int64_t c0 = 0; c0 < n_pairs; c0 += blockDim.x) place_chunk(ids, c0, n_pairs, base, n_expert, cnt, sorted_tok);
+}
+
+// Large path, step 1: per-chunk histograms hist[b][e].
+__global__ void k_scatter_hist(const int32_t* __restrict__ ids, int64_t n_pairs, int n_expert, int64_t base,
+                               int32_t* __restrict__ hist) {
+    extern __shared__ int sm[];
+    const int tid = threadIdx.x;
+    for (int e = tid; e < n_expert; e += blockDim.x) sm[e] = 0;
+    __syncthreads();
+    const int64_t f = (int64_t)blockIdx.x * kScatterChunk + tid;
+    if (f < n_pairs) {
+        const int e = local_expert(ids[f], base, n_expert);
+        if (e >= 0) atomicAdd(&sm[e], 1);
+    }
+    __syncthreads();
+    for (int e = tid; e < n_expert; e += blockDim.x) hist[(int64_t)blockIdx.x * n_expert + e] = sm[e];
+}
+
+// Step 2 (one block): expert_offset, and hist[b][e] turned into chunk b's first position for expert e.
+__global__ void k_scatter_scan(int32_t* __restrict__ hist, int nb, int n_expert, int32_t* __restrict__ off) {
+    extern __shared__ int sm[];   // [n_expert] totals
+    const int tid = threadIdx.x;
+    for (int e = tid; e < n_expert; e += blockDim.x) {
+        int acc = 0;
+        for (int b = 0; b < nb; ++b) {
+            const int v = hist[(int64_t)b * n_expert + e];
+            hist[(int64_t)b * n_expert + e] = acc;
+            acc += v;
+        }
+        sm[e] = acc;
+    }
+    __syncthreads();
+    if (tid == 0) {
+        int acc = 0;
+        for (int e = 0; e < n_expert; ++e) {
+            const int v = sm[e];
+            sm[e] = acc;
+            off[e] = acc;
+            acc += v;
+        }
+        off[n_expert] = acc;
+    }
+    __syncthreads();
+    for (int e = tid; e < n_expert; e += blockDim.x)
+        for (int b = 0; b < nb; ++b) hist[(int64_t)b * n_expert + e] += sm[e];
+}
+
+// Step 3: stable placement of each chunk from its first positions; the tail of -1.
+__global__ void k_scatter_place(const int32_t* __restrict__ ids, int64_t n_pairs, int n_expert, int64_t base,
+                                const int32_t* __restrict__ hist, const int32_t* __restrict__ off,
+                                int32_t* __restrict__ sorted_tok) {
+    extern __shared__ int sm[];
+    const int tid = threadIdx.x;
+    for (int e = tid; e < n_expert; e += blockDim.x) sm[e] = hist[(int64_t)blockIdx.x * n_expert + e];
+    __syncthreads();
+    place_chunk(ids, (int64_t)blockIdx.x * kScatterChunk, n_pairs, base, n_expert, sm, sorted_tok);
+    const int64_t live = off[n_expert];
+    const int64_t f = (int64_t)blockIdx.x * kScatterChunk + tid;
+    if (f >= live && f < n_pairs) sorted_tok[f] = -1;
+}
+
+// ------------------------------------------------------------------------------------------ gather
+__global__ void k_invert(const int32_t* __restrict__ sorted_tok, int64_t n_rows, int64_t n_pairs,
+                         int32_t* __restrict__ pos) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n_rows) return;
+    const int32_t f = sorted_tok[i];
+    if (f >= 0 && f < n_pairs) pos[f] = (int32_t)i;
+}
+
+// One block a token; thread columns 4 at a time; slots in ascending order.
+__global__ void k_gather(const uint16_t* __restrict__ rows, int64_t pitch, const int32_t* __restrict__ pos,
+                         const float* __restrict__ w, int top_k, int64_t width, float* __restrict__ y) {
+    const int64_t t = blockIdx.x;
+    for (int64_t n = 4 * (int64_t)threadIdx.x; n < width; n += 4 * (int64_t)blockDim.x) {
+        float acc[4] = { 0.f, 0.f, 0.f, 0.f };
+        for (int s = 0; s < top_k; ++s) {
+            const int32_t i = pos[t * top_k + s];
+            if (i < 0) continue;
+            const float ws = w[t * top_k + s];
+            const uint16_t* r = rows + (int64_t)i * pitch + n;
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+                if (n + q < width) acc[q] = __fadd_rn(acc[q], __fmul_rn(ws, __bfloat162float(__ushort_as_bfloat16(r[q]))));
+        }
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+            if (n + q < width) y[t * width + n + q] = acc[q];
+    }
+}
+
+}  // namespace
+
+extern "C" {
+
+static inline cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
+
+// SM count and the error word of the current device, cached per device (no synchronisation).
+int exl3b_cuda_device_info(int* sm_count, int32_t** err_word) {
+    static int s_sm[64];
+    static int32_t* s_err[64];
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return -1;
+    if (!s_sm[dev]) {
+        int sm = 0;
+        void* p = nullptr;
+        if (cudaDeviceGetAttribute(&sm, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return -1;
+        if (cudaGetSymbolAddress(&p, g_err_word) != cudaSuccess) return -1;
+        s_err[dev] = static_cast<int32_t*>(p);
+        s_sm[dev] = sm;
+    }
+    *sm_count = s_sm[dev];
+    *err_word = s_err[dev];
+    return 0;
+}
+
+int exl3b_cuda_read_error(int clear, int32_t* value) {
+    int32_t v = 0;
+    if (cudaMemcpyFromSymbol(&v, g_err_word, sizeof v) != cudaSuccess) return -1;
+    if (value) *value = v;
+    if (clear) {
+        const int32_t z = 0;
+        if (cudaMemcpyToSymbol(g_err_word, &z, sizeof z) != cudaSuccess) return -1;
+    }
+    return 0;
+}
+
+int exl3b200_router_topk(const float* logits, int64_t n_tok, int64_t n_expert, int64_t top_k, int32_t* ids, float* w,
+                         void* stream) {
+    if (!logits || !ids || !w || n_tok < 0 || n_expert < 1 || n_expert > 4096 || top_k < 1 || top_k > 32 ||
+        top_k > n_expert)
+        return -12;
+    if (n_tok == 0) return 0;
+    const int wpb = 8;
+    k_router_topk<<<(unsigned)((n_tok + wpb - 1) / wpb), wpb * 32, 0, as_stream(stream)>>>(
+        logits, n_tok, (int)n_expert, (int)top_k, ids, w);
+    return cudaGetLastError() == cudaSuccess ? 0 : -6;
+}
+
+int64_t exl3b200_moe_scatter_work_bytes(int64_t n_pairs, int64_t n_expert) {
+    const int64_t nb = (n_pairs + kScatterChunk - 1) / kScatterChunk;
+    return (nb > 0 ? nb : 1) * n_expert * 4;
+}
+
+int exl3b200_moe_scatter(const int32_t* ids, int64_t n_pairs, int64_t n_expert, int64_t expert_base,
+                         int32_t* sorted_tok, int32_t* expert_offset, void* work, void* stream) {
+    if (!ids || !sorted_tok || !expert_offset || n_pairs < 0 || n_expert < 1 || n_expert > 16384) return -12;
+    cudaStream_t st = as_stream(stream);
+    const size_t smem = (size_t)(n_expert + 1) * 4;
+    if (n_pairs <= kSmallPairs) {
+        k_scatter_small<<<1, 1024, smem, st>>>(ids, n_pairs, (int)n_expert, expert_base, sorted_tok, expert_offset);
+        return cudaGetLastError() == cudaSuccess ? 0 : -6;
+    }
+    if (!work) return -5;
+    const int nb = (int)((n_pairs + kScatterChunk - 1) / kScatterChunk);
+    int32_t* hist = static_cast<int32_t*>(work);
+    k_scatter_hist<<<nb, kScatterChunk, smem, st>>>(ids, n_pairs, (int)n_expert, expert_base, hist);
+    k_scatter_scan<<<1, 1024, smem, st>>>(hist, nb, (int)n_expert, expert_offset);
+    k_scatter_place<<<nb, kScatterChunk, smem, st>>>(ids, n_pairs, (int)n_expert, expert_base, hist, expert_offset,
+                                                     sorted_tok);
+    return cudaGetLastError() == cudaSuccess ? 0 : -6;
+}
+
+int64_t exl3b200_moe_gather_work_bytes(int64_t n_tok, int64_t top_k) { return (n_tok * top_k > 0 ? n_tok * top_k : 1) * 4; }
+
+int exl3b200_moe_gather(const uint16_t* rows, int64_t row_pitch, const int32_t* sorted_tok, int64_t n_rows,
+                        const float* w, int64_t n_tok, int64_t top_k, int64_t width, float* y, void* work,
+                        void* stream) {
+    if (!rows || !sorted_tok || !w || !y || !work || n_tok < 0 || top_k < 1 || width < 1) return -12;
+    if (n_tok == 0) return 0;
+    cudaStream_t st = as_stream(stream);
+    int32_t* pos = static_cast<int32_t*>(work);
+    if (cudaMemsetAsync(pos, 0xFF, (size_t)(n_tok * top_k) * 4, st) != cudaSuccess) return -6;
+    if (n_rows > 0)
+        k_invert<<<(unsigned)((n_rows + 255) / 256), 256, 0, st>>>(sorted_tok, n_rows, n_tok * top_k, pos);
+    k_gather<<<(unsigned)n_tok, 256, 0, st>>>(rows, row_pitch, pos, w, (int)top_k, width, y);
+    return cudaGetLastError() == cudaSuccess ? 0 : -6;
+}
+
+}  // extern "C"
