@@ -1,0 +1,180 @@
+"""layer.py -- one routed-MoE layer on the B200 library: router -> scatter -> moe_exl3_gate_up -> moe_exl3_down ->
+gather, every step a kernel of libexl3b200.so, the two expert ops called through the plugin rows exactly as the
+engine calls them (RadArgs, RadStream; rad_block_moe_exl3.h's pass issues the same sequence).
+
+Weights are synthetic and resident in HBM: each expert's codes as its stored tile-stream record (uniform random
+u16 words: every symbol sequence is a valid trellis, so a uniform record is a uniform canonical plane), suh / suh.1
+random +-1 fp16, svh +-|N(0,1)| * 0.02 fp16 (the per-channel scale lives in svh). h crosses
+between the two ops rotated (h_rot = 1, docs/OPS-exl3.md "EPI 1").
+
+Expert parallelism: `expert_base` / `n_local` select the experts this rank holds ([base, base + n_local)); the
+layer then serves rows whose expert is local (the dispatch in bench.py's multi-GPU path sends them here)."""
+import ctypes as C
+
+import numpy as np
+
+from . import cases as X
+from . import rad
+from .native import Native
+
+
+class MoeLayer:
+    def __init__(self, plugin, *, n_expert=512, hidden=2048, width=512, top_k=10, bits_gu=3, bits_dn=4,
+                 codebook="mul1", max_tokens=2048, seed=0, device="cuda", n_local=None, expert_base=0,
+                 max_rows=None):
+        import torch
+        self.torch = torch
+        self.plugin, self.native = plugin, Native(plugin.path)
+        self.E, self.H, self.W, self.k = n_expert, hidden, width, top_k
+        self.n_local = n_local or n_expert
+        self.base = expert_base
+        self.bits_gu, self.bits_dn, self.codebook = bits_gu, bits_dn, codebook
+        self.max_tokens = max_tokens
+        self.max_rows = max_rows or max_tokens * top_k
+        dev = self.dev = torch.device(device)
+        g = torch.Generator(device=dev)
+        g.manual_seed(seed)
+        E, H, W = self.n_local, hidden, width
+        # ---- weights: records and scales, resident
+        self.gu_bytes = 2 * W * H * bits_gu // 8          # stacked gate + up record
+        self.dn_bytes = H * W * bits_dn // 8
+        self.gu_rec = torch.randint(-32768, 32768, (E, self.gu_bytes // 2), generator=g, device=dev,
+                                    dtype=torch.int32).to(torch.int16)
+        self.dn_rec = torch.randint(-32768, 32768, (E, self.dn_bytes // 2), generator=g, device=dev,
+                                    dtype=torch.int32).to(torch.int16)
+
+        def sign(*shape):
+            return (torch.randint(0, 2, shape, generator=g, device=dev) * 2 - 1).to(torch.float16)
+
+        def svh(*shape):
+            return (sign(*shape).float() * torch.randn(shape, generator=g, device=dev).abs() * 0.02).to(torch.float16)
+
+        self.suh, self.suh1 = sign(E, 1, H), sign(E, 1, H)
+        self.svh_gu = svh(E, 2 * W, 1)
+        self.dn_suh = sign(E, 1, W)
+        self.svh_dn = svh(E, H, 1)
+        self.gu_tab = torch.tensor([self.gu_rec[e].data_ptr() for e in range(E)], dtype=torch.int64, device=dev)
+        self.dn_tab = torch.tensor([self.dn_rec[e].data_ptr() for e in range(E)], dtype=torch.int64, device=dev)
+        # ---- activations and routing buffers (the largest pass)
+        T, R = max_tokens, self.max_rows
+        self.x = torch.empty((T, H), dtype=torch.float16, device=dev)
+        self.logits = torch.empty((T, n_expert), dtype=torch.float32, device=dev)
+        self.ids = torch.empty((T, top_k), dtype=torch.int32, device=dev)
+        self.w = torch.empty((T, top_k), dtype=torch.float32, device=dev)
+        self.sorted_tok = torch.empty(R, dtype=torch.int32, device=dev)
+        self.offset = torch.empty(self.n_local + 1, dtype=torch.int32, device=dev)
+        self.scatter_work = torch.empty(max(16, self.native.scatter_work_bytes(R, self.n_local)), dtype=torch.uint8,
+                                        device=dev)
+        self.h = torch.empty((R, W), dtype=torch.float16, device=dev)
+        self.y_rows = torch.empty((R, H), dtype=torch.bfloat16, device=dev)
+        self.out = torch.empty((T, H), dtype=torch.float32, device=dev)
+        self.gather_work = torch.empty(max(16, self.native.gather_work_bytes(T, top_k)), dtype=torch.uint8,
+                                       device=dev)
+        self.rec_dtype = self._stored_dtype()
+        self._args = {}
+
+    # ------------------------------------------------------------------ the stored codes dtype
+    def _stored_dtype(self):
+        """Ask the gate_up row's layout hook what it stores a codes plane as (its RadLayout dtype)."""
+        row = self.plugin.row("moe_exl3_gate_up")
+        params = self._params_gu(self.max_tokens)
+        P, nP, keep = rad.make_params(params)
+        enc = X.encoding(self.bits_gu, self.codebook, stacked=True)
+        sel = C.c_int(0)
+        pt = rad.tensor(0, rad.DT_UK[self.bits_gu], [2 * self.W, self.H])
+        L = rad.RadLayout()
+        rc = row.layout(P, nP, 1, C.byref(enc), C.byref(sel), C.byref(pt), 1, C.byref(L))
+        if rc != 0 or L.bytes != self.gu_bytes:
+            raise RuntimeError(f"layout hook: rc {rc}, bytes {L.bytes} (expected {self.gu_bytes})")
+        return int(L.dtype)
+
+    def _params_gu(self, M):
+        return {"M": M, "N": 2 * self.W, "K": self.H, "n_expert": self.n_local, "top_k": self.k,
+                "dtype": f"exl3k{self.bits_gu}", "codebook": self.codebook, "h_rot": 1, "a_rot": 0}
+
+    def _params_dn(self, M):
+        return {"M": M, "N": self.H, "K": self.W, "n_expert": self.n_local, "top_k": self.k,
+                "dtype": f"exl3k{self.bits_dn}", "codebook": self.codebook, "h_rot": 1}
+
+    # ------------------------------------------------------------------ the RadArgs of one pass size
+    def _build(self, T, rows, x_ptr=None, top_k=None, M=None):
+        """RadArgs of gate_up and down for a pass of `rows` sorted rows over `T` input rows."""
+        key = (T, rows, x_ptr, top_k, M)
+        if key in self._args:
+            return self._args[key]
+        k = top_k or self.k
+        E, H, W = self.n_local, self.H, self.W
+        keep = []
+        M = M or T
+
+        def args(params, tensors):
+            P, nP, kp = rad.make_params(params)
+            arr = (rad.RadTensor * len(tensors))(*tensors)
+            a = rad.RadArgs()
+            a.t, a.n_t, a.p, a.n_p, a.world_size = arr, len(tensors), P, nP, 1
+            keep.extend([P, kp, arr])
+            return a
+
+        absent = rad.RadTensor()
+        xp = x_ptr or self.x.data_ptr()
+        pg = self._params_gu(M)
+        pg["top_k"] = k
+        gu_t = [rad.tensor(xp, rad.DT["f16"], [T, H]),
+                rad.tensor(self.gu_tab.data_ptr(), self.rec_dtype, [E, 2 * W, H], [0, H, 1]),
+                rad.tensor(self.suh.data_ptr(), rad.DT["f16"], [E, 1, H]),
+                rad.tensor(self.suh1.data_ptr(), rad.DT["f16"], [E, 1, H]),
+                rad.tensor(self.svh_gu.data_ptr(), rad.DT["f16"], [E, 2 * W, 1]),
+                rad.tensor(self.dn_suh.data_ptr(), rad.DT["f16"], [E, 1, W]),
+                rad.tensor(self.sorted_tok.data_ptr(), rad.DT["i32"], [rows]),
+                rad.tensor(self.offset.data_ptr(), rad.DT["i32"], [E + 1]),
+                absent, absent, absent, absent, absent,
+                rad.tensor(self.h.data_ptr(), rad.DT["f16"], [rows, W])]
+        pd = self._params_dn(M)
+        pd["top_k"] = k
+        dn_t = [rad.tensor(self.h.data_ptr(), rad.DT["f16"], [rows, W]),
+                rad.tensor(self.dn_tab.data_ptr(), self.rec_dtype, [E, H, W], [0, W, 1]),
+                rad.tensor(self.dn_suh.data_ptr(), rad.DT["f16"], [E, 1, W]),
+                rad.tensor(self.svh_dn.data_ptr(), rad.DT["f16"], [E, H, 1]),
+                rad.tensor(self.sorted_tok.data_ptr(), rad.DT["i32"], [rows]),
+                rad.tensor(self.offset.data_ptr(), rad.DT["i32"], [E + 1]),
+                absent, absent, absent,
+                rad.tensor(self.y_rows.data_ptr(), rad.DT["bf16"], [rows, H])]
+        res = (args(pg, gu_t), args(pd, dn_t), keep)
+        self._args[key] = res
+        return res
+
+    # ------------------------------------------------------------------ one pass
+    def experts(self, T, rows, stream, x_ptr=None, top_k=None, M=None):
+        """gate_up then down over the sorted rows already in sorted_tok / offset."""
+        a_gu, a_dn, _ = self._build(T, rows, x_ptr, top_k, M)
+        rc = self.plugin.row("moe_exl3_gate_up").launch(C.byref(a_gu), stream)
+        if rc != 0:
+            raise RuntimeError(f"moe_exl3_gate_up launch: {rc}")
+        rc = self.plugin.row("moe_exl3_down").launch(C.byref(a_dn), stream)
+        if rc != 0:
+            raise RuntimeError(f"moe_exl3_down launch: {rc}")
+
+    def forward(self, T, stream):
+        """The whole layer over the first T tokens of self.x / self.logits into self.out (f32 [T, H])."""
+        nat, rows = self.native, T * self.k
+        nat.router_topk(self.logits.data_ptr(), T, self.E, self.k, self.ids.data_ptr(), self.w.data_ptr(), stream)
+        nat.moe_scatter(self.ids.data_ptr(), rows, self.n_local, self.base, self.sorted_tok.data_ptr(),
+                        self.offset.data_ptr(), self.scatter_work.data_ptr(), stream)
+        self.experts(T, rows, stream)
+        nat.moe_gather(self.y_rows.data_ptr(), self.H, self.sorted_tok.data_ptr(), rows, self.w.data_ptr(), T, self.k,
+                       self.H, self.out.data_ptr(), self.gather_work.data_ptr(), stream)
+
+    # ------------------------------------------------------------------ accounting
+    def expert_bytes(self):
+        """Algorithmic bytes of one expert: both records plus every scale vector the pass reads."""
+        H, W = self.H, self.W
+        gu = self.gu_bytes + 2 * H * 2 + 2 * W * 2 + W * 2       # record, suh + suh.1, svh, dn_suh
+        dn = self.dn_bytes + H * 2                                # record, svh (suh not read at h_rot 1)
+        return gu, dn
+
+    def expert_flops(self, rows):
+        return 2 * rows * (2 * self.W * self.H + self.H * self.W)
+
+    def live_experts(self):
+        off = self.offset.cpu().numpy()
+        return int((np.diff(off) > 0).sum())

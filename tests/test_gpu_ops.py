@@ -1,0 +1,247 @@
+"""The B200 library on a GPU, through its C ABI, against the oracle.
+
+- the decode: bit-exact with the restatement (itself pinned to the reference and the vllm-exl3 golden) for every K
+  1..8 and every codebook, on enough tiles to meet nearly every 16-bit state;
+- every op through the plugin rows (layout hooks, redzones, NaN-prefilled outputs) against the reference library
+  built from the reference sources, within the stated tolerance: max |got - want| / max |want| <= 1e-2 and cosine
+  >= 0.9999, rows the reference leaves zero exactly zero;
+- the chain identities inside this library, to the bit: gate_up(h_rot 1) -> down(h_rot 1) equals the h_rot 0
+  pair; prep_gu -> gate_up(a_rot 1) equals gate_up(a_rot 0); gate_up_down equals its pair;
+- the routing kernels: router top-k against numpy, the scatter to the bit against the stable contract, the gather
+  against the restatement."""
+import os
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+from oracle_bind import REF_SO, Oracle, compare  # noqa: E402
+from exl3b200 import cases as X  # noqa: E402
+from exl3b200 import load_plugin  # noqa: E402
+from exl3b200.native import Native  # noqa: E402
+from exl3b200.rad import Plugin  # noqa: E402
+
+REL_TOL, COS_TOL = 1e-2, 0.9999
+
+
+@pytest.fixture(scope="module")
+def dev():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    return torch.device("cuda:0")
+
+
+@pytest.fixture(scope="module")
+def plugin(dev):
+    return load_plugin()
+
+
+@pytest.fixture(scope="module")
+def native(dev):
+    return Native()
+
+
+@pytest.fixture(scope="module")
+def orc():
+    return Oracle()
+
+
+@pytest.fixture(scope="module")
+def ref_plugin():
+    if not REF_SO.exists():
+        pytest.skip("oracle/_ref/libexl3ref.so not present")
+    return Plugin(REF_SO)
+
+
+@pytest.mark.parametrize("bits", range(1, 9))
+@pytest.mark.parametrize("cb", ["3inst", "mcg", "mul1"])
+def test_decode_is_bit_exact(dev, native, orc, bits, cb):
+    rng = np.random.default_rng(1000 + 10 * bits + len(cb))
+    rows, cols = (1024, 2048) if bits == 8 else (256, 512)
+    rec = rng.integers(0, 1 << 16, size=rows * cols * bits // 16, dtype=np.uint64).astype(np.uint16)
+    want = orc.record_decode(rec, rows, cols, bits, cb)
+    rec_d = torch.from_numpy(rec.view(np.int16)).to(dev)
+    out = torch.zeros(rows * cols, dtype=torch.int16, device=dev)
+    native.decode_what(rec_d.data_ptr(), rows, cols, bits, {"3inst": 0, "mcg": 1, "mul1": 2}[cb], out.data_ptr())
+    torch.cuda.synchronize()
+    got = out.cpu().numpy().view(np.uint16).reshape(rows, cols)
+    assert np.array_equal(got, want), f"{(got != want).sum()} of {got.size} values differ"
+
+
+def test_device_relayout_equals_oracle(orc, native):
+    rng = np.random.default_rng(5)
+    for bits in range(1, 9):
+        sym = rng.integers(0, 1 << bits, size=(48, 256), dtype=np.uint32)
+        codes = X.pack_codes(sym, bits)
+        rec = np.zeros(48 * 256 * bits // 16, np.uint16)
+        native.codes_to_record(codes.ctypes.data, codes.shape[1], 48, 256, bits, rec.ctypes.data)
+        assert np.array_equal(rec, orc.codes_to_record(codes, 48, 256, bits))
+        back = np.zeros_like(codes)
+        native.record_to_codes(rec.ctypes.data, 48, 256, bits, back.ctypes.data, codes.shape[1])
+        assert np.array_equal(back, codes)
+
+
+# ---------------------------------------------------------------------------------------------- ops
+OPS = [
+    dict(op="moe_exl3_down", M=4, top_k=2, n_expert=5, geom=[(256, 128)], bits=4, codebook="mul1", drop=0.2),
+    dict(op="moe_exl3_down", M=3, top_k=2, n_expert=4, geom=[(256, 256), (128, 128)], bits=3, codebook="mcg",
+         n_protect=1, pitch_extra=8),
+    dict(op="moe_exl3_down", M=16, top_k=1, n_expert=1, geom=[(512, 2048)], bits=4, codebook="mul1"),   # config 1
+    dict(op="moe_exl3_gate_up", M=4, top_k=2, n_expert=5, geom=[(256, 256)], bits=4, codebook="mul1", drop=0.2),
+    dict(op="moe_exl3_gate_up", M=3, top_k=2, n_expert=4, geom=[(512, 128), (256, 256)], bits=2, codebook="3inst",
+         h_rot=1, x_dtype="bf16"),
+    dict(op="moe_exl3_gate_up", M=4, top_k=2, n_expert=4, geom=[(256, 128)], bits=5, codebook="mcg", a_rot=1),
+    dict(op="moe_exl3_gate_up", M=40, top_k=2, n_expert=3, geom=[(256, 256)], bits=3, codebook="mul1"),  # > 64 rows
+    dict(op="moe_exl3_gate_up", M=8, top_k=1, n_expert=1, geom=[(1024, 2048)], bits=4, codebook="mul1"),  # config 2
+    dict(op="moe_exl3_prep_gu", M=4, top_k=2, n_expert=3, geom=[(256, 256), (256, 128)], bits=4, drop=0.25),
+    dict(op="moe_exl3_gate_up_down", M=3, top_k=2, n_expert=4, geom=[(256, 128)], bits=4, codebook="mul1"),
+    dict(op="moe_exl3_gate_up_down", M=32, top_k=1, n_expert=1, geom=[(1024, 2048)], bits=4, codebook="mul1"),
+    dict(op="moe_exl3_down_mod4", M=4, top_k=2, n_expert=6, geom=[(128, 128), (256, 128), (128, 256), (128, 128)],
+         bits=6, codebook="mul1"),
+    dict(op="moe_exl3_gate_up_mod4", M=4, top_k=2, n_expert=6,
+         geom=[(256, 128), (512, 128), (256, 256), (256, 128)], bits=7, codebook="mcg", h_rot=1),
+    dict(op="moe_exl3_down", M=8, top_k=10, n_expert=64, geom=[(2048, 512)], bits=4, codebook="mul1",
+         table_form="stacked"),
+    dict(op="moe_exl3_gate_up", M=8, top_k=10, n_expert=64, geom=[(1024, 2048)], bits=3, codebook="mul1"),
+    dict(op="moe_exl3_down", M=2, top_k=2, n_expert=3, geom=[(256, 128)], bits=8, codebook="3inst"),
+]
+
+
+def _case(spec, seed=4321):
+    spec = dict(spec)
+    return X.Case(spec.pop("op"), seed, **spec)
+
+
+def _want(case, orc, ref_plugin):
+    """The reference library itself for small cases; the restatement (pinned to it bit for bit on the CPU, see
+    tests/test_oracle.py) with threads for the large ones."""
+    if case.n_expert <= 8 and case.x_cols * max(r for r, _ in case.geom) <= 1 << 20:
+        r = case.run(ref_plugin, device=False)
+        assert r["rc"] == 0
+        return r["y"]
+    prefill = np.full((case.T, case.y_cols), 0xFFFF, np.uint16)
+    return orc.run_case(case, n_threads=os.cpu_count() or 4, prefill=prefill)
+
+
+@pytest.mark.parametrize("spec", OPS, ids=lambda s: f"{s['op']}-M{s['M']}-K{s['bits']}-{s.get('codebook', '')}")
+def test_op_matches_the_reference(dev, plugin, orc, ref_plugin, spec):
+    case = _case(spec)
+    got = case.run(plugin, device=True)
+    assert got["rc"] == 0, got["rc"]
+    assert got["redzone_ok"], "a write outside an operand"
+    assert got["inputs_ok"], "an input changed"
+    assert got["unrelayout_ok"], "the layout hooks do not round-trip"
+    want = _want(case, orc, ref_plugin)
+    if case.base == "moe_exl3_prep_gu":
+        # prep_gu is the rotation alone: to the bit, including the rows it must not write
+        assert np.array_equal(got["y"], want)
+        return
+    ok, detail = compare(got["y"], want, case.out_dtype(), REL_TOL, COS_TOL)
+    assert ok, detail
+    assert np.array_equal(got["y_pitch_tail"], np.full_like(got["y_pitch_tail"], 0xFFFF)), "wrote past the width"
+    assert Native().read_error() == 0
+
+
+def test_h_rot_pair_is_bit_identical(dev, plugin):
+    base = dict(M=6, top_k=2, n_expert=5, geom=[(512, 256)], bits=4, codebook="mul1", drop=0.1)
+    gu1 = X.Case("moe_exl3_gate_up", 77, h_rot=1, **base)
+    gu0 = X.Case("moe_exl3_gate_up", 0, h_rot=0, planes=gu1.planes, x=gu1.x, sorted_tok=gu1.sorted_tok,
+                 expert_offset=gu1.expert_offset, **{k: v for k, v in base.items() if k != "drop"})
+    h0 = gu0.run(plugin, device=True)["y"]
+    h1 = gu1.run(plugin, device=True)["y"]
+    dgeom = [(256, 256)]
+    dplanes = []
+    for p in gu1.planes:
+        rng = np.random.default_rng(len(dplanes))
+        d = X.random_planes(rng, 256, 256, 4, False)
+        d["suh"] = p["dn_suh"]
+        dplanes.append(d)
+    common = dict(M=6, top_k=2, n_expert=5, geom=dgeom, bits=4, codebook="mul1", planes=dplanes,
+                  sorted_tok=gu1.sorted_tok, expert_offset=gu1.expert_offset)
+    y0 = X.Case("moe_exl3_down", 0, h_rot=0, x=h0, **common).run(plugin, device=True)["y"]
+    y1 = X.Case("moe_exl3_down", 0, h_rot=1, x=h1, **common).run(plugin, device=True)["y"]
+    assert np.array_equal(y0, y1)
+    assert not np.array_equal(h0, h1)     # control: the flag moves gate_up's output
+
+
+def test_prep_then_a_rot_is_bit_identical(dev, plugin):
+    base = dict(M=5, top_k=2, n_expert=4, geom=[(256, 256), (512, 128)], bits=3, codebook="mcg", drop=0.1)
+    gu0 = X.Case("moe_exl3_gate_up", 91, **base)
+    pg = X.Case("moe_exl3_prep_gu", 0, planes=gu0.planes, x=gu0.x, sorted_tok=gu0.sorted_tok,
+                expert_offset=gu0.expert_offset, **{k: v for k, v in base.items() if k != "drop"})
+    xr = pg.run(plugin, device=True)["y"]
+    xr = np.where(xr == 0xFFFF, 0, xr).astype(np.uint16)     # rows prep_gu does not write: gate_up ignores them
+    gu1 = X.Case("moe_exl3_gate_up", 0, a_rot=1, planes=gu0.planes, x=xr, sorted_tok=gu0.sorted_tok,
+                 expert_offset=gu0.expert_offset, **{k: v for k, v in base.items() if k != "drop"})
+    assert np.array_equal(gu0.run(plugin, device=True)["y"], gu1.run(plugin, device=True)["y"])
+
+
+def test_gate_up_down_equals_its_pair(dev, plugin):
+    gd = X.Case("moe_exl3_gate_up_down", 5, M=5, top_k=2, n_expert=4, geom=[(512, 256)], bits=4, codebook="mul1",
+                drop=0.1)
+    y = gd.run(plugin, device=True)["y"]
+    gu = X.Case("moe_exl3_gate_up", 0, M=5, top_k=2, n_expert=4, geom=[(512, 256)], bits=4, codebook="mul1",
+                h_rot=1, planes=gd.planes, x=gd.x, sorted_tok=gd.sorted_tok, expert_offset=gd.expert_offset)
+    h = gu.run(plugin, device=True)["y"]
+    dplanes = [{"codes": p["dn_codes"], "suh": p["dn_suh"], "svh": p["dn_svh"]} for p in gd.planes]
+    dn = X.Case("moe_exl3_down", 0, M=5, top_k=2, n_expert=4, geom=[(256, 256)], bits=4, codebook="mul1", h_rot=1,
+                planes=dplanes, x=h, sorted_tok=gd.sorted_tok, expert_offset=gd.expert_offset)
+    assert np.array_equal(y, dn.run(plugin, device=True)["y"])
+
+
+def test_refusals_write_nothing(dev, plugin):
+    case = _case(OPS[0])
+    case.bits = 9          # a dtype no row serves
+    with pytest.raises(Exception):
+        case.run(plugin, device=True)
+
+
+# ---------------------------------------------------------------------------------------------- routing
+@pytest.mark.parametrize("T,E,k", [(1, 512, 10), (64, 512, 10), (2048, 512, 10), (33, 100, 3)])
+def test_router_and_scatter(dev, native, T, E, k):
+    rng = np.random.default_rng(T + E)
+    logits = rng.standard_normal((T, E)).astype(np.float32)
+    lg = torch.from_numpy(logits).to(dev)
+    ids = torch.empty((T, k), dtype=torch.int32, device=dev)
+    w = torch.empty((T, k), dtype=torch.float32, device=dev)
+    native.router_topk(lg.data_ptr(), T, E, k, ids.data_ptr(), w.data_ptr())
+    torch.cuda.synchronize()
+    want_ids = np.argsort(-logits, axis=1, kind="stable")[:, :k]
+    assert np.array_equal(ids.cpu().numpy(), want_ids)
+    p = np.exp(logits.astype(np.float64) - logits.max(1, keepdims=True))
+    p /= p.sum(1, keepdims=True)
+    assert np.allclose(w.cpu().numpy(), np.take_along_axis(p, want_ids, 1), rtol=1e-5, atol=1e-7)
+    # the stable counting sort, to the bit (with some slots dropped)
+    idn = want_ids.astype(np.int32).copy()
+    idn[rng.random(idn.shape) < 0.05] = -1
+    st_want, off_want = X.stable_scatter(idn, E)
+    ids_d = torch.from_numpy(idn).to(dev)
+    st = torch.empty(T * k, dtype=torch.int32, device=dev)
+    off = torch.empty(E + 1, dtype=torch.int32, device=dev)
+    work = torch.empty(max(1, native.scatter_work_bytes(T * k, E)), dtype=torch.uint8, device=dev)
+    native.moe_scatter(ids_d.data_ptr(), T * k, E, 0, st.data_ptr(), off.data_ptr(), work.data_ptr())
+    torch.cuda.synchronize()
+    assert np.array_equal(off.cpu().numpy(), off_want)
+    assert np.array_equal(st.cpu().numpy(), st_want)
+
+
+def test_gather(dev, native, orc):
+    rng = np.random.default_rng(9)
+    T, k, E, width = 37, 4, 16, 256
+    ids = np.stack([rng.permutation(E)[:k] for _ in range(T)]).astype(np.int32)
+    ids[rng.random(ids.shape) < 0.1] = -1
+    st, off = X.stable_scatter(ids, E)
+    rows = X.bf16_bits(rng.standard_normal((T * k, width)).astype(np.float32))
+    w = rng.random((T, k)).astype(np.float32)
+    want = orc.gather(rows, st, w, T, k, width)
+    r_d = torch.from_numpy(rows.view(np.int16)).to(dev)
+    st_d = torch.from_numpy(st).to(dev)
+    w_d = torch.from_numpy(w).to(dev)
+    y = torch.empty((T, width), dtype=torch.float32, device=dev)
+    work = torch.empty(native.gather_work_bytes(T, k), dtype=torch.uint8, device=dev)
+    native.moe_gather(r_d.data_ptr(), width, st_d.data_ptr(), T * k, w_d.data_ptr(), T, k, width, y.data_ptr(),
+                      work.data_ptr())
+    torch.cuda.synchronize()
+    assert np.array_equal(y.cpu().numpy(), want)
