@@ -1,0 +1,417 @@
+"""bench.py -- the routed-MoE layer on B200: tokens/s and packed-weight HBM GB/s per chip.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--tokens T] [--impl ours|reference]
+
+Workload ("config 3"): one routed-MoE layer -- 512 experts of hidden 2048 / width 512,
+gate_up at K=3 and down at K=4 (mul1 codebook), top-10 softmax routing of seeded N(0,1) logits -- over T tokens
+(default 2048) of N(0,1) fp16 activations. A step is the whole layer: router -> stable scatter -> moe_exl3_gate_up
+(h_rot 1) -> moe_exl3_down (h_rot 1) -> weighted gather, each a kernel of libexl3b200.so, the expert ops called
+through the plugin rows. Weights are synthetic and resident (679 MB > the 126 MB L2, so every step streams them
+from HBM; no flush is needed). N > 1: expert parallelism -- each rank holds 512/N experts and its own T tokens
+(weak scaling), a dispatch and a combine all-to-all over NCCL carry the token rows.
+
+--impl reference: the reference's own CPU implementation of the path (kernels/exl3ref built from its sources,
+oracle/_ref) timed on this box's host cores, every thread running a bounded sample of the same workload.
+Prints ONE JSON line (rank 0)."""
+import argparse
+import ctypes as C
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO / "radiance-exl3_b200"))
+sys.path.insert(0, str(REPO / "tests"))
+
+METRIC = "routed-MoE layer tokens/s and packed-weight HBM GB/s/chip at batch 1-2048, 1/2/4/8 B200"
+E, H, W, TOPK, KGU, KDN, CB = 512, 2048, 512, 10, 3, 4, "mul1"
+WORKLOAD = (f"config 3: routed-MoE layer, {E} experts of [hidden {H}, width {W}], top-{TOPK} softmax routing, "
+            f"gate_up K={KGU} / down K={KDN} {CB}, h_rot 1")
+
+
+def peaks():
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d["hbm_gbs"], d["bf16_tflops"], "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+# ------------------------------------------------------------------------------------------ clocks
+class Clocks:
+    """nvidia-smi sampling of SM clocks and throttle reasons while the GPU works."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
+        self.proc.terminate()
+        out, _ = self.proc.communicate(timeout=10)
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx.append(float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ------------------------------------------------------------------------------------------ the reference sample
+def reference_sample_setup(T=2048, n_experts=4, seed=7):
+    """A bounded sample of the workload for the reference's host library: the first `n_experts` experts of a
+    T-token top-10 routing (all of their rows, so the per-row decode amortisation is the workload's), their
+    canonical planes, and the token rows. Returns (launch callables, tokens the sample stands for)."""
+    from exl3b200 import cases as X
+    from exl3b200 import rad
+    from oracle_bind import REF_SO
+    rng = np.random.default_rng(seed)
+    logits = rng.standard_normal((T, E)).astype(np.float32)
+    ids = np.argsort(-logits, axis=1, kind="stable")[:, :TOPK].astype(np.int32)
+    st, off = X.stable_scatter(ids, E)
+    rows = int(off[n_experts])
+    st_s = np.ascontiguousarray(st[:rows])
+    off_s = np.ascontiguousarray(off[:n_experts + 1])
+    x = X.bits_f16(X.f16(rng.standard_normal((T, H)).astype(np.float32)))
+    gu = [X.random_planes(rng, 2 * W, H, KGU, True) for _ in range(n_experts)]
+    dn = [X.random_planes(rng, H, W, KDN, False) for _ in range(n_experts)]
+    dn_suh = [X.f16((rng.integers(0, 2, W) * 2 - 1).astype(np.float32)) for _ in range(n_experts)]
+    plugin = rad.Plugin(REF_SO)
+    row_gu, row_dn = plugin.row("moe_exl3_gate_up"), plugin.row("moe_exl3_down")
+
+    def stack(arrs):
+        return np.ascontiguousarray(np.stack([np.ascontiguousarray(a).view(np.uint8).reshape(-1) for a in arrs]))
+
+    keep = []
+
+    def T_(arr, dt, shape, stride=None):
+        keep.append(arr)
+        return rad.tensor(arr.ctypes.data, dt, shape, stride)
+
+    n = n_experts
+    gcodes, gsuh, gsuh1, gsvh = stack([p["codes"] for p in gu]), stack([p["suh"] for p in gu]), \
+        stack([p["suh1"] for p in gu]), stack([p["svh"] for p in gu])
+    dsuh, dcodes, dsvh = stack(dn_suh), stack([p["codes"] for p in dn]), stack([p["svh"] for p in dn])
+
+    def make():
+        h = np.zeros((rows, W), np.uint16)
+        y = np.zeros((rows, H), np.uint16)
+        absent = rad.RadTensor()
+        gu_t = [T_(x, rad.DT["f16"], [T, H]), T_(gcodes, rad.DT_UK[KGU], [n, 2 * W, H]),
+                T_(gsuh, rad.DT["f16"], [n, 1, H]), T_(gsuh1, rad.DT["f16"], [n, 1, H]),
+                T_(gsvh, rad.DT["f16"], [n, 2 * W, 1]), T_(dsuh, rad.DT["f16"], [n, 1, W]),
+                T_(st_s, rad.DT["i32"], [rows]), T_(off_s, rad.DT["i32"], [n + 1]),
+                absent, absent, absent, absent, absent, T_(h, rad.DT["f16"], [rows, W])]
+        dn_t = [T_(h, rad.DT["f16"], [rows, W]), T_(dcodes, rad.DT_UK[KDN], [n, H, W]),
+                T_(dsuh, rad.DT["f16"], [n, 1, W]), T_(dsvh, rad.DT["f16"], [n, H, 1]),
+                T_(st_s, rad.DT["i32"], [rows]), T_(off_s, rad.DT["i32"], [n + 1]),
+                absent, absent, absent, T_(y, rad.DT["bf16"], [rows, H])]
+        out = []
+        for params, ts in (({"M": T, "N": 2 * W, "K": H, "n_expert": n, "top_k": TOPK, "dtype": f"exl3k{KGU}",
+                             "codebook": CB, "h_rot": 1, "a_rot": 0}, gu_t),
+                           ({"M": T, "N": H, "K": W, "n_expert": n, "top_k": TOPK, "dtype": f"exl3k{KDN}",
+                             "codebook": CB, "h_rot": 1}, dn_t)):
+            P, nP, kp = rad.make_params(params)
+            arr = (rad.RadTensor * len(ts))(*ts)
+            a = rad.RadArgs()
+            a.t, a.n_t, a.p, a.n_p, a.world_size = arr, len(ts), P, nP, 1
+            keep.extend([P, kp, arr, a])
+            out.append(a)
+        return out
+
+    def run(args_pair):
+        a_gu, a_dn = args_pair
+        rc = row_gu.launch(C.byref(a_gu), None)
+        rc = rc or row_dn.launch(C.byref(a_dn), None)
+        if rc:
+            raise RuntimeError(f"exl3ref launch: {rc}")
+
+    return make, run, rows / TOPK, keep
+
+
+def time_reference(threads, steps, warmup, n_experts=4, T=2048):
+    """Every thread runs the same bounded sample concurrently (ctypes releases the GIL); a step is one sample on
+    every thread. Returns (tokens/s aggregate, seconds a step, sample description)."""
+    make, run, tokens, keep = reference_sample_setup(T, n_experts)
+    arg_sets = [make() for _ in range(threads)]
+    times = []
+    for it in range(warmup + steps):
+        ths = [threading.Thread(target=run, args=(arg_sets[i],)) for i in range(threads)]
+        t0 = time.perf_counter()
+        for t in ths:
+            t.start()
+        for t in ths:
+            t.join()
+        dt = time.perf_counter() - t0
+        if it >= warmup:
+            times.append(dt)
+    step = float(np.mean(times))
+    sample = (f"kernels/exl3ref (unmodified, -O2 -ffp-contract=off) gate_up(K={KGU}, h_rot 1) + down(K={KDN}, h_rot 1) "
+              f"over the first {n_experts} experts of a T={T} top-{TOPK} routing ({int(tokens * TOPK)} sorted rows = "
+              f"{tokens:.1f} tokens' worth), {threads} thread(s) each running it; router/scatter/gather not included")
+    return threads * tokens / step, step, sample
+
+
+# ------------------------------------------------------------------------------------------ our arm
+def bench_ours(args, rank, world, local_rank):
+    import torch
+    torch.cuda.set_device(local_rank)
+    from exl3b200 import load_plugin
+    from exl3b200.layer import MoeLayer
+    dev = torch.device("cuda", local_rank)
+    plugin = load_plugin()
+    T = args.tokens
+    if world > 1:
+        from exl3b200.ep import EpLayer
+        layer = EpLayer(plugin, rank=rank, world=world, n_expert=E, hidden=H, width=W, top_k=TOPK, bits_gu=KGU,
+                        bits_dn=KDN, codebook=CB, max_tokens=T, seed=1 + rank)
+    else:
+        layer = MoeLayer(plugin, n_expert=E, hidden=H, width=W, top_k=TOPK, bits_gu=KGU, bits_dn=KDN, codebook=CB,
+                         max_tokens=T, seed=1)
+    g = torch.Generator(device=dev)
+    g.manual_seed(1000 + rank)
+    layer.x.copy_(torch.randn(layer.x.shape, generator=g, device=dev).to(torch.float16))
+    layer.logits.copy_(torch.randn(layer.logits.shape, generator=g, device=dev))
+    stream = torch.cuda.current_stream()
+    sh = stream.cuda_stream
+    hbm, tflops, peak_kind = peaks()
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize()
+
+    # ---- warm-up, then a clock soak of about a second, then EXACTLY K timed steps
+    clocks = Clocks(local_rank)
+    for _ in range(args.warmup):
+        layer.forward(T, sh)
+    barrier()
+    clocks.start()
+    soak_t0 = time.perf_counter()
+    while not args.profile and time.perf_counter() - soak_t0 < 1.0:
+        layer.forward(T, sh)
+    torch.cuda.synchronize()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    kev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    barrier()
+    wall0 = time.perf_counter()
+    ev[0].record(stream)
+    for s in range(args.steps):
+        layer.forward(T, sh, events=kev[s])
+    ev[1].record(stream)
+    barrier()
+    wall = time.perf_counter() - wall0
+    clk = clocks.stop()
+    ms = ev[0].elapsed_time(ev[1]) / args.steps
+    gu_ms = float(np.mean([k[0].elapsed_time(k[1]) for k in kev]))
+    dn_ms = float(np.mean([k[1].elapsed_time(k[2]) for k in kev]))
+    if world > 1:
+        t = torch.tensor([ms, gu_ms, dn_ms], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms, gu_ms, dn_ms = (float(v) for v in t.cpu())
+    live = layer.live_experts()
+    gu_b, dn_b = layer.expert_bytes()
+    tokens_total = T * world
+    value = tokens_total / (ms / 1e3)
+    step_bytes = live * (gu_b + dn_b)
+    # the dominant kernel's roofline (bytes it must read once / its measured duration)
+    dom = "gate_up" if gu_ms >= dn_ms else "down"
+    dom_ms = gu_ms if dom == "gate_up" else dn_ms
+    dom_bytes = live * (gu_b if dom == "gate_up" else dn_b)
+    achieved = dom_bytes / (dom_ms / 1e3) / 1e9
+    launches_per_step = layer.launches_per_step(T)
+
+    # ---- end to end: pinned host inputs in, the layer, the output back, every step
+    e2e = None
+    if not args.no_e2e:
+        hx = torch.empty(layer.x[:T].shape, dtype=layer.x.dtype, pin_memory=True)
+        hl = torch.empty(layer.logits[:T].shape, dtype=layer.logits.dtype, pin_memory=True)
+        hx.copy_(layer.x[:T].cpu())
+        hl.copy_(layer.logits[:T].cpu())
+        ho = torch.empty(layer.out[:T].shape, dtype=layer.out.dtype, pin_memory=True)
+        for _ in range(args.warmup):
+            layer.x[:T].copy_(hx, non_blocking=True)
+            layer.logits[:T].copy_(hl, non_blocking=True)
+            layer.forward(T, sh)
+            ho.copy_(layer.out[:T], non_blocking=True)
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            layer.x[:T].copy_(hx, non_blocking=True)
+            layer.logits[:T].copy_(hl, non_blocking=True)
+            layer.forward(T, sh)
+            ho.copy_(layer.out[:T], non_blocking=True)
+        e1.record(stream)
+        barrier()
+        e_ms = e0.elapsed_time(e1) / args.steps
+        if world > 1:
+            t = torch.tensor([e_ms], device=dev)
+            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+            e_ms = float(t.item())
+        e2e = {"value": tokens_total / (e_ms / 1e3), "unit": "tokens/s", "ms_per_step": e_ms,
+               "h2d_bytes_per_step": int(hx.numel() * 2 + hl.numel() * 4),
+               "d2h_bytes_per_step": int(ho.numel() * 4),
+               "path": "pinned host x + logits -> router/scatter kernels -> plugin rows moe_exl3_gate_up, "
+                       "moe_exl3_down (RadArgs launch) -> gather kernel -> pinned host y"}
+
+    # ---- the batch sweep (1 GPU): each T captured in a CUDA graph
+    sweep = None
+    if world == 1 and not args.no_sweep:
+        sweep = {}
+        for Ts in (1, 8, 64, 512, 2048):
+            if Ts > T:
+                continue
+            for _ in range(3):
+                layer.forward(Ts, sh)
+            torch.cuda.synchronize()
+            graph_ok = True
+            try:
+                gph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(gph):
+                    layer.forward(Ts, torch.cuda.current_stream().cuda_stream)
+                run = gph.replay
+            except Exception:
+                graph_ok = False
+                run = lambda: layer.forward(Ts, sh)  # noqa: E731
+            for _ in range(3):
+                run()
+            torch.cuda.synchronize()
+            n = max(args.steps, 20)
+            a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a0.record()
+            for _ in range(n):
+                run()
+            a1.record()
+            torch.cuda.synchronize()
+            sms = a0.elapsed_time(a1) / n
+            lv = layer.live_experts()
+            sweep[str(Ts)] = {"ms": round(sms, 4), "tokens_per_s": round(Ts / (sms / 1e3), 1),
+                              "live_experts": lv, "weight_gbs": round(lv * (gu_b + dn_b) / (sms / 1e3) / 1e9, 1),
+                              "frac_hbm": round(lv * (gu_b + dn_b) / (sms / 1e3) / 1e9 / hbm, 3),
+                              "graph": graph_ok}
+            del run
+            if graph_ok:
+                del gph
+
+    # ---- the CPU baseline (rank 0, one GPU): the reference library on a bounded sample
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        try:
+            v, step, sample = time_reference(threads=1, steps=1, warmup=0, n_experts=32)
+            cpu = {"value": round(v, 3), "unit": "tokens/s", "cores": 1, "kind": "reference",
+                   "sample": sample, "seconds": round(step, 2), "host_cores_available": os.cpu_count()}
+        except Exception as exc:  # the reference library is absent on this box
+            cpu = {"value": None, "unit": "tokens/s", "cores": 0, "kind": "reference", "sample": f"unavailable: {exc}"}
+
+    if rank != 0:
+        return None
+    flops = layer.expert_flops(T * TOPK) * world
+    line = {
+        "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "fp16 operands (decoded trellis), f32 accumulate", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "tokens_per_gpu": T, "n_expert": E, "hidden": H, "width": W, "top_k": TOPK,
+                   "bits": {"gate_up": KGU, "down": KDN}, "codebook": CB,
+                   "parallelism": f"ep{world}" if world > 1 else "single",
+                   "l2": "no flush: the packed weights (679 MB) exceed the 126 MB L2 and stream every step",
+                   "inputs": "codes uniform random record words, suh +-1, svh +-|N(0,1)|*0.02, x and logits N(0,1)"},
+        "hbm_gbs_per_chip": round(step_bytes / (ms / 1e3) / 1e9, 1),
+        "tflops": round(flops / (ms / 1e3) / 1e12, 2),
+        "roofline": {"bound": "hbm", "kernel": f"k_gemm_skinny ({dom})", "achieved": round(achieved, 1),
+                     "peak": hbm, "unit": "GB/s", "frac": round(achieved / hbm, 4),
+                     "peak_source": f"{peak_kind} hbm_gbs (MEASURED_PEAKS.json)",
+                     "bytes_per_launch": int(dom_bytes), "ms_per_launch": round(dom_ms, 4), "traffic": None,
+                     "other": {"gate_up_ms": round(gu_ms, 4), "down_ms": round(dn_ms, 4)}},
+        "clocks": clk, "gpu_launches": int(launches_per_step * args.steps),
+        "e2e": e2e, "cpu_baseline": cpu, "sweep": sweep, "wall_s": round(wall, 3),
+    }
+    return line
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--tokens", type=int, default=2048)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-sweep", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile", action="store_true",
+                    help="for a profiler run: no clock soak, sweep, end-to-end leg or CPU baseline")
+    args = ap.parse_args()
+    args.warmup = max(3, args.warmup)
+    if args.profile:
+        args.no_sweep = args.no_e2e = args.no_cpu_baseline = True
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    local_rank = int(os.environ.get("LOCAL_RANK", 0))
+
+    if args.impl == "reference":
+        if rank != 0:
+            return 0
+        threads = max(1, min(os.cpu_count() or 1, 64))
+        v, step, sample = time_reference(threads, args.steps, args.warmup, n_experts=2)
+        line = {"metric": METRIC, "impl": "reference", "value": round(v, 3), "unit": "tokens/s", "n_gpus": args.gpus,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(step * 1e3, 2),
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32 host",
+                "data": "synthetic",
+                "config": {"workload": WORKLOAD, "tokens_per_gpu": args.tokens, "n_expert": E, "top_k": TOPK},
+                "cpu_baseline": {"value": round(v, 3), "unit": "tokens/s", "cores": threads, "kind": "reference",
+                                 "sample": sample},
+                "e2e": {"value": round(v, 3), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return 0
+
+    if world > 1:
+        import datetime
+
+        import torch
+        torch.cuda.set_device(local_rank)
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                             device_id=torch.device("cuda", local_rank))
+    try:
+        line = bench_ours(args, rank, world, local_rank)
+    finally:
+        if world > 1:
+            import torch
+            torch.distributed.barrier()
+            torch.distributed.destroy_process_group()
+    if rank == 0 and line is not None:
+        print(json.dumps(line), flush=True)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -144,23 +144,35 @@ class MoeLayer:
         return res
 
     # ------------------------------------------------------------------ one pass
-    def experts(self, T, rows, stream, x_ptr=None, top_k=None, M=None):
-        """gate_up then down over the sorted rows already in sorted_tok / offset."""
+    def experts(self, T, rows, stream, x_ptr=None, top_k=None, M=None, events=None):
+        """gate_up then down over the sorted rows already in sorted_tok / offset. `events`: three
+        torch.cuda.Event recorded before gate_up, between the two and after down (on the current stream)."""
         a_gu, a_dn, _ = self._build(T, rows, x_ptr, top_k, M)
+        if events:
+            events[0].record()
         rc = self.plugin.row("moe_exl3_gate_up").launch(C.byref(a_gu), stream)
         if rc != 0:
             raise RuntimeError(f"moe_exl3_gate_up launch: {rc}")
+        if events:
+            events[1].record()
         rc = self.plugin.row("moe_exl3_down").launch(C.byref(a_dn), stream)
         if rc != 0:
             raise RuntimeError(f"moe_exl3_down launch: {rc}")
+        if events:
+            events[2].record()
 
-    def forward(self, T, stream):
+    def launches_per_step(self, T):
+        """Kernels of this library one forward launches: router, scatter (1 small / 3 large), gate_up, down,
+        the gather's inverse map and the gather."""
+        return 1 + (1 if T * self.k <= 8192 else 3) + 2 + 2
+
+    def forward(self, T, stream, events=None):
         """The whole layer over the first T tokens of self.x / self.logits into self.out (f32 [T, H])."""
         nat, rows = self.native, T * self.k
         nat.router_topk(self.logits.data_ptr(), T, self.E, self.k, self.ids.data_ptr(), self.w.data_ptr(), stream)
         nat.moe_scatter(self.ids.data_ptr(), rows, self.n_local, self.base, self.sorted_tok.data_ptr(),
                         self.offset.data_ptr(), self.scatter_work.data_ptr(), stream)
-        self.experts(T, rows, stream)
+        self.experts(T, rows, stream, events=events)
         nat.moe_gather(self.y_rows.data_ptr(), self.H, self.sorted_tok.data_ptr(), rows, self.w.data_ptr(), T, self.k,
                        self.H, self.out.data_ptr(), self.gather_work.data_ptr(), stream)
 
