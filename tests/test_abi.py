@@ -1,0 +1,178 @@
+"""The drop-in boundary on the CPU (no GPU needed): libexl3b200.so loads, exports every symbol include/exl3b200.h
+declares, reports ABI 17, exports schemas identical field for field to the reference library's (the engine refuses
+a second library whose schemas differ, include/exl3_abi.h:5-9), describes operands as the reference does, lays
+codes out and back losslessly, and refuses what the reference refuses -- before touching the device."""
+import ctypes as C
+import re
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+from oracle_bind import REF_SO
+from exl3b200 import cases as X
+from exl3b200 import load_plugin, library_path
+from exl3b200 import rad
+from exl3b200.rad import Plugin
+
+REPO = Path(__file__).resolve().parent.parent
+
+
+@pytest.fixture(scope="module")
+def plugin():
+    return load_plugin()
+
+
+@pytest.fixture(scope="module")
+def ref_plugin():
+    if not REF_SO.exists():
+        pytest.skip("oracle/_ref/libexl3ref.so not built")
+    return Plugin(REF_SO)
+
+
+def declared_functions():
+    text = (REPO / "include" / "exl3b200.h").read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b((?:rad|exl3b200)_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_every_declared_symbol_is_exported():
+    lib = C.CDLL(str(library_path()))
+    names = declared_functions()
+    assert len(names) >= 15
+    for n in names:
+        assert hasattr(lib, n), n
+
+
+def test_identity(plugin):
+    assert plugin.lib.rad_plugin_abi_version() == 17
+    info = plugin.info
+    assert info["name"] == "exl3b200" and info["target"] == "sm_100a" and info["kind"] == 1
+
+
+def test_schemas_equal_the_reference_library(plugin, ref_plugin):
+    assert plugin.schemas() == ref_plugin.schemas()
+
+
+def test_rows_cover_every_op_on_the_device(plugin):
+    ops = {r.op.decode() for r in plugin.rows()}
+    assert ops == {s["op"] for s in plugin.schemas()}
+    assert all(r.domain == rad.DOMAIN_DEVICE for r in plugin.rows())
+    assert all(plugin.lib.rad_kernel_concurrent(i) == 1 for i in range(len(plugin.rows())))
+
+
+SHAPE_PARAMS = [
+    ("moe_exl3_gate_up", {"M": (1, 16), "N": 1024, "K": 2048, "n_expert": 512, "top_k": 10, "dtype": "exl3k3",
+                          "codebook": "mul1", "h_rot": 1, "a_rot": 0}),
+    ("moe_exl3_down", {"M": (1, 2048), "N": 2048, "K": 512, "n_expert": 512, "top_k": 10, "dtype": "exl3k4",
+                       "codebook": "mul1", "h_rot": 0, "N_odd": 2048, "K_odd": 384}),
+    ("moe_exl3_prep_gu", {"M": 4, "K": 256, "n_expert": 3, "top_k": 2, "dtype": "exl3k4", "K_odd": 128}),
+    ("moe_exl3_gate_up_down", {"M": 3, "N": 512, "K": 256, "n_expert": 4, "top_k": 2, "dtype": "exl3k5",
+                               "codebook": "mcg"}),
+    ("moe_exl3_gate_up_mod4", {"M": 4, "N": 512, "K": 256, "n_expert": 7, "top_k": 2, "dtype": "exl3k2",
+                               "codebook": "3inst", "N_2": 256, "K_3": 128, "h_rot": 1, "a_rot": 1}),
+    ("moe_exl3_down_mod4", {"M": 4, "N": 256, "K": 256, "n_expert": 7, "top_k": 2, "dtype": "exl3k8",
+                            "codebook": "mul1", "N_1": 128, "h_rot": 0}),
+    ("moe_exl3_prep_gu_mod4", {"M": 4, "K": 256, "n_expert": 6, "top_k": 2, "dtype": "exl3k4", "K_2": 128}),
+    ("moe_exl3_gate_up_down_mod4", {"M": 2, "N": 512, "K": 256, "n_expert": 8, "top_k": 2, "dtype": "exl3k4",
+                                    "codebook": "mul1", "N_3": 256}),
+]
+
+
+@pytest.mark.parametrize("op,params", SHAPE_PARAMS, ids=[o for o, _ in SHAPE_PARAMS])
+def test_shape_hook_equals_the_reference(plugin, ref_plugin, op, params):
+    mine, theirs = plugin.row(op), ref_plugin.row(op)
+    P, nP, keep = rad.make_params(params)
+    n_opd = next(s for s in plugin.schemas() if s["op"] == op)["operands"]
+    for i in range(len(n_opd)):
+        a, b = rad.RadOpdDesc(), rad.RadOpdDesc()
+        ra = mine.opd_shape(P, nP, i, C.byref(a))
+        rb = theirs.opd_shape(P, nP, i, C.byref(b))
+        assert ra == rb, (op, i)
+        assert bytes(a) == bytes(b), (op, i)
+
+
+def test_constraints_select_every_bitrate_and_codebook(plugin):
+    row = plugin.row("moe_exl3_gate_up")
+    cons = [row.constraints[k] for k in range(row.n_constraints)]
+    for bits in range(2, 9):
+        for cb in ("mul1", "mcg", "3inst"):
+            p = {"M": 8, "N": 1024, "K": 2048, "n_expert": 512, "top_k": 10, "dtype": f"exl3k{bits}",
+                 "codebook": cb, "h_rot": 1, "a_rot": 0}
+            assert all(rad.constraint_holds(c, p) for c in cons)
+    bad = {"M": 8, "N": 1024, "K": 2000, "n_expert": 512, "top_k": 10, "dtype": "exl3k4", "codebook": "mul1",
+           "h_rot": 1, "a_rot": 0}
+    assert not all(rad.constraint_holds(c, bad) for c in cons)
+
+
+@pytest.mark.parametrize("op", ["moe_exl3_gate_up", "moe_exl3_down", "moe_exl3_gate_up_down"])
+def test_layout_hook_round_trips(plugin, op):
+    case = X.Case(op, 3, M=2, top_k=1, n_expert=2, geom=[(512, 256)], bits=3, codebook="mcg", h_rot=1)
+    row = plugin.row(op)
+    P, nP, keep = rad.make_params(case.params())
+    enc = X.encoding(3, "mcg", stacked=op != "moe_exl3_down")
+    sel = C.c_int(0)
+    R, Cc = case.geom[0]
+    codes = np.ascontiguousarray(case.planes[0]["codes"])
+    pt = rad.tensor(codes.ctypes.data, rad.DT_UK[3], [R, Cc])
+    L = rad.RadLayout()
+    assert row.layout(P, nP, 1, C.byref(enc), C.byref(sel), C.byref(pt), 1, C.byref(L)) == 0
+    assert L.bytes == R * Cc * 3 // 8 and L.align >= 16
+    rec = np.zeros(L.bytes, np.uint8)
+    assert row.relayout(P, nP, 1, C.byref(enc), C.byref(sel), C.byref(pt), 1, rec.ctypes.data, L.bytes) == 0
+    back = np.zeros_like(codes)
+    bt = rad.tensor(back.ctypes.data, rad.DT_UK[3], [R, Cc])
+    assert row.unrelayout(P, nP, 1, C.byref(enc), C.byref(sel), rec.ctypes.data, L.bytes, C.byref(bt), 1) == 0
+    assert np.array_equal(back, codes)
+    # a scale plane is stored as it is
+    sel.value = 1
+    st = rad.tensor(0, rad.DT["f16"], [1, Cc])
+    assert row.layout(P, nP, 2, C.byref(enc), C.byref(sel), C.byref(st), 1, C.byref(L)) == rad.RAD["UNSUPPORTED"]
+    # a codebook the encoding does not name is refused by the hook
+    enc2 = X.encoding(3, "mul1", stacked=op != "moe_exl3_down")
+    sel.value = 0
+    assert row.layout(P, nP, 1, C.byref(enc2), C.byref(sel), C.byref(pt), 1, C.byref(L)) == rad.RAD["DTYPE"]
+
+
+def _launch(plugin, op, params, tensors):
+    row = plugin.row(op)
+    P, nP, keep = rad.make_params(params)
+    arr = (rad.RadTensor * len(tensors))(*tensors)
+    a = rad.RadArgs()
+    a.t, a.n_t, a.p, a.n_p, a.world_size = arr, len(tensors), P, nP, 1
+    return row.launch(C.byref(a), None)
+
+
+def test_refusals_come_before_any_device_work(plugin):
+    """The reference's refusal codes (docs/OPS-exl3.md:292-301), returned by the host side with no GPU present."""
+    p = {"M": 2, "N": 256, "K": 128, "n_expert": 2, "top_k": 1, "dtype": "exl3k4", "codebook": "mul1", "h_rot": 0}
+    x = np.zeros((2, 128), np.uint16)
+    y = np.zeros((2, 256), np.uint16)
+    st = np.zeros(2, np.int32)
+    off = np.array([0, 1, 2], np.int32)
+    codes = np.zeros(8, np.uint64)
+    sc = np.zeros((2, 1, 256), np.uint16)
+
+    def tens(xdt=rad.DT["f16"], ydt=rad.DT["bf16"], ycols=256, codes_dt=1970):
+        return [rad.tensor(x.ctypes.data, xdt, [2, 128]),
+                rad.tensor(codes.ctypes.data, codes_dt, [2, 256, 128], [0, 128, 1]),
+                rad.tensor(sc.ctypes.data, rad.DT["f16"], [2, 1, 128]),
+                rad.tensor(sc.ctypes.data, rad.DT["f16"], [2, 256, 1]),
+                rad.tensor(st.ctypes.data, rad.DT["i32"], [2]),
+                rad.tensor(off.ctypes.data, rad.DT["i32"], [3]),
+                rad.RadTensor(), rad.RadTensor(), rad.RadTensor(),
+                rad.tensor(y.ctypes.data, ydt, [2, ycols])]
+
+    op = "moe_exl3_down"
+    assert _launch(plugin, op, dict(p, dtype="exl3k9"), tens()) == rad.RAD["DTYPE"]
+    assert _launch(plugin, op, dict(p, codebook="nope"), tens()) == rad.RAD["DTYPE"]
+    assert _launch(plugin, op, dict(p, h_rot=2), tens()) == rad.RAD["INVAL"]
+    assert _launch(plugin, op, {k: v for k, v in p.items() if k != "h_rot"}, tens()) == rad.RAD["SCHEMA"]
+    assert _launch(plugin, op, dict(p, K=100), tens()) == rad.RAD["SHAPE"]
+    assert _launch(plugin, op, p, tens(ydt=rad.DT["f16"])) == rad.RAD["DTYPE"]
+    assert _launch(plugin, op, p, tens(ycols=128)) == rad.RAD["SHAPE"]
+    assert _launch(plugin, op, p, tens(codes_dt=rad.DT_UK[4])) == rad.RAD["DTYPE"]   # not laid out
+    t = tens()
+    t[6] = rad.tensor(codes.ctypes.data, 1970, [1, 256, 128], [0, 128, 1])     # odd tables partly present
+    assert _launch(plugin, op, p, t) == rad.RAD["INVAL"]
+    assert (y == 0).all()
