@@ -78,6 +78,20 @@ int     exl3b200_moe_gather(const uint16_t* rows, int64_t row_pitch, const int32
                             const float* w, int64_t n_tok, int64_t top_k, int64_t width, float* y, void* work,
                             void* stream);
 
+/* moe_gather for a caller that cannot allocate device memory -- one whose memory is fixed up front (a serving
+ * engine that owns a preallocated pool and forbids cudaMalloc on its launch path, a process running under a
+ * strict device-memory budget, code that must not grow the CUDA allocator's footprint). No counterpart in the
+ * reference: it is this library's own addition. Same arguments and result as exl3b200_moe_gather without `work`:
+ * the inverse pair -> row map lives in a fixed 1 MiB device array inside this library, so n_tok * top_k must be at
+ * most 262,144 (RAD_E_SHAPE beyond, nothing enqueued). The first call on each device looks up the array's device
+ * address (cudaGetSymbolAddress) with that device current; make that first call before any stream capture. The
+ * call allocates nothing (no cudaMalloc, no cudaFree, no allocating library routine). Every call shares the one
+ * array per device: calls that overlap on the GPU (two streams, or two threads) race and must be serialised by
+ * the caller. */
+int     exl3b200_moe_gather_noalloc(const uint16_t* rows, int64_t row_pitch, const int32_t* sorted_tok,
+                                    int64_t n_rows, const float* w, int64_t n_tok, int64_t top_k, int64_t width,
+                                    float* y, void* stream);
+
 /* The device error word of the current device: nonzero once a bounded wait inside a kernel gave up (the
  * launch then finished without a valid result). Reading it synchronises the device; `clear` resets it. Not
  * for a launch path. */

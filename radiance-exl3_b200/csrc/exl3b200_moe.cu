@@ -291,4 +291,37 @@ int exl3b200_moe_gather(const uint16_t* rows, int64_t row_pitch, const int32_t* 
     return cudaGetLastError() == cudaSuccess ? 0 : -6;
 }
 
+// ------------------------------------------------------------------------------------------ the gather, allocating nothing
+// The gather's one piece of scratch -- the inverse map from a (token, slot) pair to its sorted row -- lives in this
+// fixed device array instead of memory the caller provides, for callers that cannot allocate device memory at all.
+// At most kNoAllocMaxPairs pairs a call (1 MiB of int32). Every GPU that loads this library holds the array until
+// the process exits.
+constexpr int64_t kNoAllocMaxPairs = 1 << 18;
+static __device__ __align__(256) int32_t g_noalloc_pos[kNoAllocMaxPairs];
+
+int exl3b200_moe_gather_noalloc(const uint16_t* rows, int64_t row_pitch, const int32_t* sorted_tok, int64_t n_rows,
+                                const float* w, int64_t n_tok, int64_t top_k, int64_t width, float* y, void* stream) {
+    if (!rows || !sorted_tok || !w || !y || n_tok < 0 || top_k < 1 || width < 1 || n_rows < 0) return -12;
+    if (n_tok * top_k > kNoAllocMaxPairs) return -1;   // past the fixed array: refused before anything is enqueued
+    if (n_tok == 0) return 0;
+    // Set-up, once per device, with that device current: the array's device address. The host-side name of a
+    // __device__ array is not a device address; only cudaGetSymbolAddress gives one.
+    static int32_t* s_pos[64];
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return -6;
+    if (!s_pos[dev]) {
+        void* p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_noalloc_pos) != cudaSuccess || !p) return -6;
+        s_pos[dev] = static_cast<int32_t*>(p);
+    }
+    int32_t* pos = s_pos[dev];
+    cudaStream_t st = as_stream(stream);
+    // the map starts as "no row" (-1) for every pair of this call; the array keeps the last call's contents
+    if (cudaMemsetAsync(pos, 0xFF, (size_t)(n_tok * top_k) * 4, st) != cudaSuccess) return -6;
+    if (n_rows > 0)
+        k_invert<<<(unsigned)((n_rows + 255) / 256), 256, 0, st>>>(sorted_tok, n_rows, n_tok * top_k, pos);
+    k_gather<<<(unsigned)n_tok, 256, 0, st>>>(rows, row_pitch, pos, w, (int)top_k, width, y);
+    return cudaGetLastError() == cudaSuccess ? 0 : -6;
+}
+
 }  // extern "C"
