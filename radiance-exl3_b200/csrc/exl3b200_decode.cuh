@@ -1,0 +1,216 @@
+// exl3b200_decode.cuh -- device code shared by the sm_100a kernels of libexl3b200.so: the bit-exact trellis decode
+// of one lane's eight positions, the 128-point rotation in the reference's stage order, the mbarrier / TMA bulk-copy
+// helpers with bounded waits, and the expert lookups of the routing contract. Included by each .cu file (every
+// function is internal to the including translation unit).
+#pragma once
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+#include "exl3b200_dev.h"
+
+namespace {
+
+constexpr float kRs = 0.08838834764831844055f;   // (float)(1 / sqrt(128))
+constexpr int kWaitLimit = 1 << 24;               // bounded mbarrier waits (then the error word is set)
+
+// ------------------------------------------------------------------------------------------ small helpers
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ float h2f(uint16_t h) { return __half2float(__ushort_as_half(h)); }
+__device__ __forceinline__ uint16_t f2h(float f) { return __half_as_ushort(__float2half_rn(f)); }
+__device__ __forceinline__ float bf2f(uint16_t h) { return __bfloat162float(__ushort_as_bfloat16(h)); }
+__device__ __forceinline__ uint16_t f2bf(float f) { return __bfloat16_as_ushort(__float2bfloat16_rn(f)); }
+
+// Entry j of a plane table (stacked or pointer table).
+__device__ __forceinline__ const void* tab_entry(const Exl3bTab& t, int64_t j) {
+    if (t.stride_bytes == 0) return reinterpret_cast<const void* const*>(t.base)[j];
+    return static_cast<const uint8_t*>(t.base) + j * t.stride_bytes;
+}
+
+// ------------------------------------------------------------------------------------------ codebooks
+// Two states -> one half2 (low = first). mul1: fp16(1024 + bytesum(s * 0x83DCD12D)) is built exactly as the
+// bits 0x6400 + bytesum (dp4a with that addend), then ONE fp16 FMA by K_INV (0x1EEE) plus K_BIAS (0xC931).
+// mcg / 3inst: (h & 0x8FFF8FFF) ^ 0x3B603B60, the two fp16 halves added once. common/exl3_decode.c:43-67.
+template <int CB>
+__device__ __forceinline__ uint32_t cb_pair(uint32_t s0, uint32_t s1) {
+    if constexpr (CB == 2) {
+        const uint32_t x0 = s0 * 0x83DCD12Du, x1 = s1 * 0x83DCD12Du;
+        const uint32_t u0 = __dp4a(x0, 0x01010101u, 0x6400u);
+        const uint32_t u1 = __dp4a(x1, 0x01010101u, 0x6400u);
+        const uint32_t h = __byte_perm(u0, u1, 0x5410);
+        const __half2 kinv = __halves2half2(__ushort_as_half(0x1EEE), __ushort_as_half(0x1EEE));
+        const __half2 kbias = __halves2half2(__ushort_as_half(0xC931), __ushort_as_half(0xC931));
+        const __half2 r = __hfma2(*reinterpret_cast<const __half2*>(&h), kinv, kbias);
+        return *reinterpret_cast<const uint32_t*>(&r);
+    } else {
+        uint32_t x0, x1;
+        if constexpr (CB == 1) {
+            x0 = s0 * 0xCBAC1FEDu;
+            x1 = s1 * 0xCBAC1FEDu;
+        } else {
+            x0 = s0 * 89226354u + 64248484u;
+            x1 = s1 * 89226354u + 64248484u;
+        }
+        x0 = (x0 & 0x8FFF8FFFu) ^ 0x3B603B60u;
+        x1 = (x1 & 0x8FFF8FFFu) ^ 0x3B603B60u;
+        const uint32_t lo = __byte_perm(x0, x1, 0x5410), hi = __byte_perm(x0, x1, 0x7632);
+        const __half2 r = __hadd2(*reinterpret_cast<const __half2*>(&lo), *reinterpret_cast<const __half2*>(&hi));
+        return *reinterpret_cast<const uint32_t*>(&r);
+    }
+}
+
+// ------------------------------------------------------------------------------------------ one tile, one lane
+// Lane L of a warp decodes trellis positions 8L .. 8L+7 of a 16x16 tile (8K u32 words, one MSB-first stream,
+// circular). Position 8L+j's 16-bit state is the stream window ending at bit (8L+j+1)K. The eight positions
+// are exactly the mma.m16n8k16 B fragments of the tile's two n8 halves (k = 2(L%4) + {0,1,8,9},
+// n = L/4 and L/4 + 8), so the four returned half2 are: b[0], b[1] the first n8 block's fragment registers,
+// b[2], b[3] the second's.
+//
+// The lane's windows all fall in a 64-bit (K <= 4) or 96-bit (K >= 5) span that starts on a 16-bit
+// boundary with its first window at offset 16..31; each state is then one clamped funnel shift.
+template <int BITS, int CB>
+__device__ __forceinline__ void decode_lane(const uint32_t* __restrict__ w, int lane, uint32_t b[4]) {
+    constexpr int NW = 8 * BITS;                           // words in the tile
+    constexpr int NB = 256 * BITS;                         // bits in the tile
+    uint32_t st[8];
+    if constexpr (BITS == 4) {
+        // window of position 8L+j at offset 20 + 4j of (word L-1 : word L)
+        const uint32_t hi = w[(lane + NW - 1) % NW], lo = w[lane];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) st[j] = __funnelshift_r(lo, hi, 28 - 4 * j) & 0xFFFFu;
+    } else {
+        const int base = ((8 * lane + 1) * BITS - 16 + NB) % NB;   // first window's start bit
+        const int a = base >> 5, off = base & 31;
+        const int sh16 = off < 16 ? 16 : 0;                        // realign so the first window sits at 16..31
+        const int offp = off + sh16;
+        const uint32_t wm1 = w[(a + NW - 1) % NW], wa = w[a], wb = w[(a + 1) % NW];
+        const uint32_t h = __funnelshift_r(wa, wm1, sh16);         // stream bits [32a - sh16, +32)
+        const uint32_t m = __funnelshift_r(wb, wa, sh16);          // the next 32
+        if constexpr (BITS <= 4) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) st[j] = __funnelshift_rc(m, h, 48 - offp - j * BITS) & 0xFFFFu;
+        } else {
+            const uint32_t wc = w[(a + 2) % NW];
+            const uint32_t l = __funnelshift_r(wc, wb, sh16);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const int q = offp + j * BITS;
+                const uint32_t v0 = __funnelshift_rc(m, h, 48 - q);
+                const uint32_t v1 = __funnelshift_rc(l, m, 80 - q);
+                st[j] = (q <= 48 ? v0 : v1) & 0xFFFFu;
+            }
+        }
+    }
+    b[0] = cb_pair<CB>(st[0], st[1]);
+    b[1] = cb_pair<CB>(st[2], st[3]);
+    b[2] = cb_pair<CB>(st[4], st[5]);
+    b[3] = cb_pair<CB>(st[6], st[7]);
+}
+
+// ------------------------------------------------------------------------------------------ 128-point rotation
+// A warp holds one 128-vector, lane l the elements 4l .. 4l+3. Stages h = 1, 2 inside the lane, h = 4 .. 64
+// across lanes; a+b stays low, a-b goes high, exactly as common/exl3_decode.c:179-185; then x (float)(1/sqrt(128)).
+__device__ __forceinline__ void had128_warp(float v[4], int lane) {
+    float a, b;
+    a = v[0]; b = v[1]; v[0] = __fadd_rn(a, b); v[1] = __fsub_rn(a, b);
+    a = v[2]; b = v[3]; v[2] = __fadd_rn(a, b); v[3] = __fsub_rn(a, b);
+    a = v[0]; b = v[2]; v[0] = __fadd_rn(a, b); v[2] = __fsub_rn(a, b);
+    a = v[1]; b = v[3]; v[1] = __fadd_rn(a, b); v[3] = __fsub_rn(a, b);
+#pragma unroll
+    for (int m = 1; m < 32; m <<= 1) {
+        const bool high = (lane & m) != 0;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float p = __shfl_xor_sync(0xFFFFFFFFu, v[i], m);
+            v[i] = high ? __fsub_rn(p, v[i]) : __fadd_rn(v[i], p);
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) v[i] = __fmul_rn(v[i], kRs);
+}
+
+// f16(had(f16(x * s))) of one 128-block held as above (kernels/exl3ref/ref.c:27-32).
+__device__ __forceinline__ void prologue_warp(float v[4], const uint16_t* __restrict__ s, int lane) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) v[i] = h2f(f2h(__fmul_rn(v[i], h2f(s[4 * lane + i]))));
+    had128_warp(v, lane);
+}
+
+// ------------------------------------------------------------------------------------------ mbarrier / TMA
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+// Bounded wait for the phase of `parity`; false (and the error word set) when it never completed.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int32_t* err) {
+    const uint32_t a = smem_u32(bar);
+    for (int i = 0; i < kWaitLimit; ++i) {
+        uint32_t done;
+        asm volatile(
+            "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+            : "=r"(done)
+            : "r"(a), "r"(parity)
+            : "memory");
+        if (done) return true;
+    }
+    if (err) atomicOr(err, 1);
+    return false;
+}
+// One bulk (non-tensor) TMA copy global -> this CTA's shared memory, completing on `bar`. 16-byte aligned
+// addresses and a size that is a multiple of 16 (the host refuses weights that are not).
+__device__ __forceinline__ void tma_bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ float4 ld_dsmem_f4(const float* local, uint32_t rank) {
+    uint32_t remote;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_u32(local)), "r"(rank));
+    float4 v;
+    asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "r"(remote)
+                 : "memory");
+    return v;
+}
+
+
+// ------------------------------------------------------------------------------------------ expert lookups
+struct ExpertView {
+    int c;
+    int64_t j, R, C;
+};
+__device__ __forceinline__ ExpertView expert_view(const Exl3bOp& op, int64_t e) {
+    ExpertView v;
+    v.c = (int)(e % op.n_class);
+    v.j = e / op.n_class;
+    v.R = op.cls[v.c].rows;
+    v.C = op.cls[v.c].cols;
+    return v;
+}
+__device__ __forceinline__ bool row_live(const Exl3bOp& op, int64_t i) {
+    return i >= op.expert_offset[0] && i < op.expert_offset[op.n_expert] && op.sorted_tok[i] >= 0;
+}
+
+}  // namespace

@@ -18,7 +18,8 @@
 /* The CUDA side (exl3b200_kernels.cu, exl3b200_moe.cu). */
 int     exl3b_cuda_decode_what(const void* record, int64_t rows, int64_t cols, int bits, int codebook, void* out,
                                void* stream);
-int     exl3b_cuda_prep(const Exl3bOp* op, void* stream);
+int     exl3b_cuda_prep(const Exl3bOp* op, void* dst, int64_t dst_pitch, void* stream);
+int     exl3b_cuda_gemm_tc(const Exl3bOp* op, const void* xin, int64_t xin_pitch, int sm_count, void* stream);
 int     exl3b_plan_skinny(const Exl3bOp* op, int sm_count, Exl3bPlan* p);
 int     exl3b_cuda_gemm_skinny(const Exl3bOp* op, const Exl3bPlan* p, void* stream);
 int     exl3b_cuda_device_info(int* sm_count, int32_t** err_word);
@@ -149,13 +150,56 @@ static int build_op(const RadArgs* a, int op, Exl3bGeom* g, Exl3bOp* k) {
     return RAD_OK;
 }
 
-static int run_op(Exl3bOp* k, void* stream) {
+/* The band choice. The tensor-core path decodes each expert's weights once for up to 64 of its rows and pays its
+ * input-rotation pass (the prep kernel into scratch) once per row; the decode-band path re-rotates per output block
+ * and holds at most 64 rows in registers. The tensor-core path is taken when the live experts average at least
+ * EXL3B_TC_MIN_ROWS rows, every class's output is a whole number of 256-row unit pairs, and its input rows can be
+ * read by a 16-byte-aligned tensor map (else the decode-band path serves the launch, with the same result). */
+#ifndef EXL3B_TC_MIN_ROWS
+#define EXL3B_TC_MIN_ROWS 16
+#endif
+static int tc_band(const Exl3bOp* k) {
+    if (k->op == EXL3B_OP_PREP_GU || k->T <= 0) return 0;
+    const int64_t live = k->n_expert < k->T ? k->n_expert : k->T;
+    if (live <= 0 || k->T / live < EXL3B_TC_MIN_ROWS) return 0;
+    for (int c = 0; c < k->n_class; ++c) {
+        if (k->cls[c].cols % 64) return 0;
+        if (k->op == EXL3B_OP_DOWN && k->cls[c].rows % 256) return 0;
+    }
+    if ((k->n_expert + 1) * 4 > 16384) return 0;
+    return 1;
+}
+
+/* Scratch the tensor-core path needs: the rotated input rows when the op's input is not already rotated. */
+static int64_t tc_scratch_bytes(const Exl3bOp* k) {
+    if (!tc_band(k)) return 0;
+    if (k->op == EXL3B_OP_GATE_UP && !k->a_rot) return (k->T * 2 * k->x_cols * 2 + 255) / 256 * 256;
+    if (k->op == EXL3B_OP_DOWN && !k->h_rot) return (k->T * k->x_cols * 2 + 255) / 256 * 256;
+    return 0;
+}
+
+static int run_op(Exl3bOp* k, void* scratch, int64_t scratch_bytes, void* stream) {
     int sm = 0;
     int32_t* err = 0;
     if (exl3b_cuda_device_info(&sm, &err) != 0) return RAD_E_DEVICE;
     k->err = err;
-    if (k->op == EXL3B_OP_PREP_GU) return exl3b_cuda_prep(k, stream) == 0 ? RAD_OK : RAD_E_DEVICE;
+    if (k->op == EXL3B_OP_PREP_GU) return exl3b_cuda_prep(k, k->y, k->y_pitch, stream) == 0 ? RAD_OK : RAD_E_DEVICE;
     if (k->T == 0) return RAD_OK;
+    if (tc_band(k)) {
+        const int64_t need = tc_scratch_bytes(k);
+        const void* xin = 0;
+        int64_t pitch = 0;
+        if (need == 0) {
+            xin = k->x;
+            pitch = k->x_pitch;
+            if (!rad_ptr_aligned(xin, 16) || (pitch * 2) % 16) xin = 0;
+        } else if (scratch && scratch_bytes >= need && rad_ptr_aligned(scratch, 256)) {
+            pitch = k->op == EXL3B_OP_GATE_UP ? 2 * k->x_cols : k->x_cols;
+            if (exl3b_cuda_prep(k, scratch, pitch, stream) != 0) return RAD_E_DEVICE;
+            xin = scratch;
+        }
+        if (xin) return exl3b_cuda_gemm_tc(k, xin, pitch, sm, stream) == 0 ? RAD_OK : RAD_E_DEVICE;
+    }
     Exl3bPlan plan;
     if (exl3b_plan_skinny(k, sm, &plan) != 0) return RAD_E_SHAPE;
     return exl3b_cuda_gemm_skinny(k, &plan, stream) == 0 ? RAD_OK : RAD_E_DEVICE;
@@ -166,7 +210,14 @@ static int launch_op(const RadArgs* a, RadStream s, int op) {
     Exl3bOp k;
     const int rc = build_op(a, op, &g, &k);
     if (rc != RAD_OK) return rc;
-    return run_op(&k, s);
+    return run_op(&k, a->scratch, a->scratch_bytes, s);
+}
+
+static int64_t op_scratch(const RadArgs* a, int op) {
+    Exl3bGeom g;
+    Exl3bOp k;
+    if (build_op(a, op, &g, &k) != RAD_OK) return 0;
+    return tc_scratch_bytes(&k);
 }
 
 /* gate_up_down: its two halves, h in the launch's scratch (docs/OPS-exl3.md:177-191). */
@@ -189,35 +240,30 @@ static int64_t gd_h_bytes(const RadArgs* a, int mod4) {
     return T > 0 && W > 0 ? (T * W * 2 + 255) / 256 * 256 : 0;
 }
 
-static int launch_gd(const RadArgs* a, RadStream s, int mod4) {
+/* Build the two halves' argument records; h at `h_data` (the launch's scratch, or a placeholder for sizing). */
+static int gd_halves(const RadArgs* a, int mod4, void* h_data, Exl3bOp* k1, Exl3bOp* k2) {
     const Exl3bPositions* gd = exl3b_positions(mod4 ? EXL3B_GU_DN4 : EXL3B_GU_DN);
     if (a->n_t < gd->n_opd || !rad_arg_in(a, gd->y)) return RAD_E_INVAL;
     RadParam pg[16], pd[16];
     int ng = 0, nd = 0;
     exl3b_gd_params(a->p, a->n_p, mod4, pg, &ng, pd, &nd);
     const int64_t T = rad_tensor_rows(rad_arg_in(a, gd->y));
-    const int64_t need = gd_h_bytes(a, mod4);
-    if (T < 0 || need <= 0) return RAD_E_SHAPE;
-    if (!a->scratch || a->scratch_bytes < need) return RAD_E_SCRATCH;
+    static const char* const nq[4] = { "N", "N_1", "N_2", "N_3" };
+    const int64_t N = rad_param_geti(a->p, a->n_p, "N", 0);
+    int64_t W = 0;
+    for (int c = 0; c < (mod4 ? 4 : 2); ++c) {
+        const int64_t n = (mod4 ? rad_param_geti(a->p, a->n_p, nq[c], N)
+                                : (c ? rad_param_geti(a->p, a->n_p, "N_odd", N) : N)) / 2;
+        if (n > W) W = n;
+    }
+    if (T < 0 || W <= 0) return RAD_E_SHAPE;
     RadTensor h;
     memset(&h, 0, sizeof h);
-    h.data = a->scratch;
+    h.data = h_data;
     h.dtype = RAD_F16;
     h.rank = 2;
     h.shape[0] = T;
-    h.shape[1] = need / 2 / (T > 0 ? T : 1);
-    {
-        /* the exact width: the widest class's N / 2 */
-        static const char* const nq[4] = { "N", "N_1", "N_2", "N_3" };
-        const int64_t N = rad_param_geti(a->p, a->n_p, "N", 0);
-        int64_t W = 0;
-        for (int c = 0; c < (mod4 ? 4 : 2); ++c) {
-            const int64_t n = (mod4 ? rad_param_geti(a->p, a->n_p, nq[c], N)
-                                    : (c ? rad_param_geti(a->p, a->n_p, "N_odd", N) : N)) / 2;
-            if (n > W) W = n;
-        }
-        h.shape[1] = W;
-    }
+    h.shape[1] = W;
     rad_tensor_pack(&h);
     RadTensor tg[24], td[16];
     exl3b_gd_operands(a->t, &h, mod4, tg, td);
@@ -230,20 +276,42 @@ static int launch_gd(const RadArgs* a, RadStream s, int mod4) {
     ad.n_t = exl3b_positions(mod4 ? EXL3B_DOWN4 : EXL3B_DOWN)->n_opd;
     ad.p = pd;
     ad.n_p = nd;
-    /* both halves are checked before either is launched: a refusal writes nothing */
     Exl3bGeom g1, g2;
-    Exl3bOp k1, k2;
-    int rc = build_op(&ag, mod4 ? EXL3B_GATE_UP4 : EXL3B_GATE_UP, &g1, &k1);
+    int rc = build_op(&ag, mod4 ? EXL3B_GATE_UP4 : EXL3B_GATE_UP, &g1, k1);
     if (rc != RAD_OK) return rc;
-    rc = build_op(&ad, mod4 ? EXL3B_DOWN4 : EXL3B_DOWN, &g2, &k2);
-    if (rc != RAD_OK) return rc;
-    rc = run_op(&k1, s);
-    if (rc != RAD_OK) return rc;
-    return run_op(&k2, s);
+    return build_op(&ad, mod4 ? EXL3B_DOWN4 : EXL3B_DOWN, &g2, k2);
 }
 
-static int64_t gd_scratch(const RadArgs* a) { return gd_h_bytes(a, 0); }
-static int64_t gd4_scratch(const RadArgs* a) { return gd_h_bytes(a, 1); }
+static int launch_gd(const RadArgs* a, RadStream s, int mod4) {
+    const Exl3bPositions* gd = exl3b_positions(mod4 ? EXL3B_GU_DN4 : EXL3B_GU_DN);
+    if (a->n_t < gd->n_opd || !rad_arg_in(a, gd->y)) return RAD_E_INVAL;
+    const int64_t need = gd_h_bytes(a, mod4);
+    if (need <= 0) return RAD_E_SHAPE;
+    if (!a->scratch || a->scratch_bytes < need) return RAD_E_SCRATCH;
+    /* both halves are checked before either is launched: a refusal writes nothing */
+    Exl3bOp k1, k2;
+    const int rc = gd_halves(a, mod4, a->scratch, &k1, &k2);
+    if (rc != RAD_OK) return rc;
+    uint8_t* rest = (uint8_t*)a->scratch + need;
+    const int r1 = run_op(&k1, rest, a->scratch_bytes - need, s);
+    if (r1 != RAD_OK) return r1;
+    return run_op(&k2, 0, 0, s);
+}
+
+static int64_t gd_scratch_of(const RadArgs* a, int mod4) {
+    const int64_t h = gd_h_bytes(a, mod4);
+    Exl3bOp k1, k2;
+    static uint16_t placeholder[8];
+    if (h <= 0 || gd_halves(a, mod4, placeholder, &k1, &k2) != RAD_OK) return h;
+    return h + tc_scratch_bytes(&k1);
+}
+
+static int64_t gd_scratch(const RadArgs* a) { return gd_scratch_of(a, 0); }
+static int64_t gd4_scratch(const RadArgs* a) { return gd_scratch_of(a, 1); }
+static int64_t gu_scratch(const RadArgs* a) { return op_scratch(a, EXL3B_GATE_UP); }
+static int64_t dn_scratch(const RadArgs* a) { return op_scratch(a, EXL3B_DOWN); }
+static int64_t gu4_scratch(const RadArgs* a) { return op_scratch(a, EXL3B_GATE_UP4); }
+static int64_t dn4_scratch(const RadArgs* a) { return op_scratch(a, EXL3B_DOWN4); }
 
 static int gu_launch(const RadArgs* a, RadStream s)  { return launch_op(a, s, EXL3B_GATE_UP); }
 static int dn_launch(const RadArgs* a, RadStream s)  { return launch_op(a, s, EXL3B_DOWN); }
@@ -484,13 +552,13 @@ static const RadKernelInfo k_rows[] = {
       "h_rot's down rotation (sm_100a)",
       "any M; K % 128, N % 256 (each class); up to four classes in one grid",
       "exl3k2..exl3k8; mul1, mcg, 3inst; a f16 or bf16; h f16", RAD_DOMAIN_DEVICE, 10, c_gu, N_OF(c_gu),
-      gu_launch, gu_shape, 0, 0, 0, gu_layout, gu_relayout, gu_unrelayout },
+      gu_launch, gu_shape, gu_scratch, 0, 0, gu_layout, gu_relayout, gu_unrelayout },
     { "exl3b200_moe_down", "moe_exl3_down", "moe",
       "EXL3 routed experts, down, bf16 y: input rotation (h_rot 0), trellis decode in registers into tensor-core "
       "fragments, the output rotation and svh (sm_100a)",
       "any M; K % 128, N % 128 (each class); up to four classes in one grid",
       "exl3k2..exl3k8; mul1, mcg, 3inst; h f16; y bf16", RAD_DOMAIN_DEVICE, 10, c_dn, N_OF(c_dn),
-      dn_launch, dn_shape, 0, 0, 0, dn_layout, dn_relayout, dn_unrelayout },
+      dn_launch, dn_shape, dn_scratch, 0, 0, dn_layout, dn_relayout, dn_unrelayout },
     { "exl3b200_moe_prep_gu", "moe_exl3_prep_gu", "moe",
       "EXL3 routed experts, gate_up's input rotation as an op: every sorted row of every run, a[token] x suh and "
       "x suh.1, each 128-block Hadamard-rotated, side by side in xr (sm_100a)",
@@ -506,12 +574,12 @@ static const RadKernelInfo k_rows[] = {
       "EXL3 routed experts, gate and up, four classes by number mod 4: the gate_up kernels (sm_100a)",
       "any M; K % 128, N % 256 (each class); four classes in one grid",
       "exl3k2..exl3k8; mul1, mcg, 3inst; a f16 or bf16; h f16", RAD_DOMAIN_DEVICE, 10, c_gu, N_OF(c_gu),
-      gu4_launch, gu4_shape, 0, 0, 0, gu4_layout, gu4_relayout, gu4_unrelayout },
+      gu4_launch, gu4_shape, gu4_scratch, 0, 0, gu4_layout, gu4_relayout, gu4_unrelayout },
     { "exl3b200_moe_down_mod4", "moe_exl3_down_mod4", "moe",
       "EXL3 routed experts, down, four classes by number mod 4: the down kernels (sm_100a)",
       "any M; K % 128, N % 128 (each class); four classes in one grid",
       "exl3k2..exl3k8; mul1, mcg, 3inst; h f16; y bf16", RAD_DOMAIN_DEVICE, 10, c_dn, N_OF(c_dn),
-      dn4_launch, dn4_shape, 0, 0, 0, dn4_layout, dn4_relayout, dn4_unrelayout },
+      dn4_launch, dn4_shape, dn4_scratch, 0, 0, dn4_layout, dn4_relayout, dn4_unrelayout },
     { "exl3b200_moe_prep_gu_mod4", "moe_exl3_prep_gu_mod4", "moe",
       "EXL3 routed experts, gate_up's input rotation as an op, four classes by number mod 4 (sm_100a)",
       "any M; K % 128 (each class)", "exl3k2..exl3k8; a f16 or bf16; xr f16", RAD_DOMAIN_DEVICE, 10, c_pg,

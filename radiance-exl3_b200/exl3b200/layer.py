@@ -139,7 +139,16 @@ class MoeLayer:
                 rad.tensor(self.offset.data_ptr(), rad.DT["i32"], [E + 1]),
                 absent, absent, absent,
                 rad.tensor(self.y_rows.data_ptr(), rad.DT["bf16"], [rows, H])]
-        res = (args(pg, gu_t), args(pd, dn_t), keep)
+        a_gu, a_dn = args(pg, gu_t), args(pd, dn_t)
+        # the scratch each row's hook asks for (the tensor-core band's rotated input rows), allocated once per shape
+        for row_name, a in (("moe_exl3_gate_up", a_gu), ("moe_exl3_down", a_dn)):
+            row = self.plugin.row(row_name)
+            need = int(row.scratch(C.byref(a))) if row.scratch else 0
+            if need > 0:
+                buf = self.torch.empty(need, dtype=self.torch.uint8, device=self.dev)
+                keep.append(buf)
+                a.scratch, a.scratch_bytes = buf.data_ptr(), need
+        res = (a_gu, a_dn, keep)
         self._args[key] = res
         return res
 

@@ -106,6 +106,19 @@ OPS = [
          table_form="stacked"),
     dict(op="moe_exl3_gate_up", M=8, top_k=10, n_expert=64, geom=[(1024, 2048)], bits=3, codebook="mul1"),
     dict(op="moe_exl3_down", M=2, top_k=2, n_expert=3, geom=[(256, 128)], bits=8, codebook="3inst"),
+    # the tensor-core band (live experts averaging >= 16 rows)
+    dict(op="moe_exl3_down", M=100, top_k=2, n_expert=4, geom=[(512, 256)], bits=4, codebook="mul1", h_rot=1),
+    dict(op="moe_exl3_gate_up", M=64, top_k=2, n_expert=4, geom=[(512, 256), (256, 128)], bits=2, codebook="3inst",
+         drop=0.1),
+    dict(op="moe_exl3_gate_up", M=48, top_k=1, n_expert=2, geom=[(1024, 512)], bits=5, codebook="mcg", a_rot=1),
+    dict(op="moe_exl3_down", M=70, top_k=1, n_expert=1, geom=[(256, 128)], bits=8, codebook="mul1"),
+    dict(op="moe_exl3_gate_up", M=33, top_k=2, n_expert=2, geom=[(256, 256)], bits=6, codebook="mul1", h_rot=1,
+         x_dtype="bf16"),
+    dict(op="moe_exl3_gate_up", M=200, top_k=10, n_expert=64, geom=[(1024, 2048)], bits=3, codebook="mul1",
+         h_rot=1),
+    dict(op="moe_exl3_down", M=200, top_k=10, n_expert=64, geom=[(2048, 512)], bits=4, codebook="mul1", h_rot=1),
+    dict(op="moe_exl3_down_mod4", M=64, top_k=2, n_expert=8, geom=[(256, 128), (512, 128), (256, 256), (256, 128)],
+         bits=7, codebook="mcg"),
 ]
 
 
