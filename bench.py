@@ -346,7 +346,7 @@ def bench_ours(args, rank, world, local_rank):
                    "inputs": "codes uniform random record words, suh +-1, svh +-|N(0,1)|*0.02, x and logits N(0,1)"},
         "hbm_gbs_per_chip": round(step_bytes / (ms / 1e3) / 1e9, 1),
         "tflops": round(flops / (ms / 1e3) / 1e12, 2),
-        "roofline": {"bound": "hbm", "kernel": f"k_gemm_skinny ({dom})", "achieved": round(achieved, 1),
+        "roofline": {"bound": "hbm", "kernel": layer.band_name(dom, T), "achieved": round(achieved, 1),
                      "peak": hbm, "unit": "GB/s", "frac": round(achieved / hbm, 4),
                      "peak_source": f"{peak_kind} hbm_gbs (MEASURED_PEAKS.json)",
                      "bytes_per_launch": int(dom_bytes), "ms_per_launch": round(dom_ms, 4), "traffic": None,

@@ -13,7 +13,8 @@
 namespace {
 
 constexpr float kRs = 0.08838834764831844055f;   // (float)(1 / sqrt(128))
-constexpr int kWaitLimit = 1 << 24;               // bounded mbarrier waits (then the error word is set)
+constexpr uint64_t kWaitLimitNs = 2000000000ull;  // a bounded mbarrier wait gives up after 2 s (error word set)
+constexpr uint32_t kSuspendNs = 100000u;          // a waiting thread sleeps in hardware up to this long a try
 
 // ------------------------------------------------------------------------------------------ small helpers
 
@@ -73,33 +74,63 @@ __device__ __forceinline__ uint32_t cb_pair(uint32_t s0, uint32_t s1) {
 //
 // The lane's windows all fall in a 64-bit (K <= 4) or 96-bit (K >= 5) span that starts on a 16-bit
 // boundary with its first window at offset 16..31; each state is then one clamped funnel shift.
-template <int BITS, int CB>
-__device__ __forceinline__ void decode_lane(const uint32_t* __restrict__ w, int lane, uint32_t b[4]) {
-    constexpr int NW = 8 * BITS;                           // words in the tile
-    constexpr int NB = 256 * BITS;                         // bits in the tile
-    uint32_t st[8];
+// What a lane needs to find its eight windows in any tile of a given K: the byte offsets of the three or four
+// stream words they span, the 16-bit realignment and the first window's offset. Computed once a kernel.
+template <int BITS>
+struct LaneDec {
+    uint32_t o0, o1, o2, o3;   // byte offsets of words a-1, a, a+1, a+2 (circular in the tile)
+    uint32_t sh16;             // 0 or 16
+    int offp;                  // the first window's offset, 16..31
+};
+
+template <int BITS>
+__device__ __forceinline__ LaneDec<BITS> lane_dec(int lane) {
+    constexpr int NW = 8 * BITS;
+    constexpr int NB = 256 * BITS;
+    LaneDec<BITS> d;
     if constexpr (BITS == 4) {
-        // window of position 8L+j at offset 20 + 4j of (word L-1 : word L)
-        const uint32_t hi = w[(lane + NW - 1) % NW], lo = w[lane];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) st[j] = __funnelshift_r(lo, hi, 28 - 4 * j) & 0xFFFFu;
+        d.o0 = (uint32_t)(((lane + NW - 1) % NW) * 4);
+        d.o1 = (uint32_t)(lane * 4);
+        d.o2 = d.o3 = 0;
+        d.sh16 = 0;
+        d.offp = 20;
     } else {
         const int base = ((8 * lane + 1) * BITS - 16 + NB) % NB;   // first window's start bit
         const int a = base >> 5, off = base & 31;
-        const int sh16 = off < 16 ? 16 : 0;                        // realign so the first window sits at 16..31
-        const int offp = off + sh16;
-        const uint32_t wm1 = w[(a + NW - 1) % NW], wa = w[a], wb = w[(a + 1) % NW];
-        const uint32_t h = __funnelshift_r(wa, wm1, sh16);         // stream bits [32a - sh16, +32)
-        const uint32_t m = __funnelshift_r(wb, wa, sh16);          // the next 32
+        d.sh16 = off < 16 ? 16u : 0u;
+        d.offp = off + (int)d.sh16;
+        d.o0 = (uint32_t)(((a + NW - 1) % NW) * 4);
+        d.o1 = (uint32_t)(a * 4);
+        d.o2 = (uint32_t)(((a + 1) % NW) * 4);
+        d.o3 = (uint32_t)(((a + 2) % NW) * 4);
+    }
+    return d;
+}
+
+template <int BITS, int CB>
+__device__ __forceinline__ void decode_tile(const uint8_t* __restrict__ tile, const LaneDec<BITS>& d, uint32_t b[4]) {
+    uint32_t st[8];
+    if constexpr (BITS == 4) {
+        // window of position 8L+j at offset 20 + 4j of (word L-1 : word L)
+        const uint32_t hi = *reinterpret_cast<const uint32_t*>(tile + d.o0);
+        const uint32_t lo = *reinterpret_cast<const uint32_t*>(tile + d.o1);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) st[j] = __funnelshift_r(lo, hi, 28 - 4 * j) & 0xFFFFu;
+    } else {
+        const uint32_t wm1 = *reinterpret_cast<const uint32_t*>(tile + d.o0);
+        const uint32_t wa = *reinterpret_cast<const uint32_t*>(tile + d.o1);
+        const uint32_t wb = *reinterpret_cast<const uint32_t*>(tile + d.o2);
+        const uint32_t h = __funnelshift_r(wa, wm1, d.sh16);         // stream bits [32a - sh16, +32)
+        const uint32_t m = __funnelshift_r(wb, wa, d.sh16);          // the next 32
         if constexpr (BITS <= 4) {
 #pragma unroll
-            for (int j = 0; j < 8; ++j) st[j] = __funnelshift_rc(m, h, 48 - offp - j * BITS) & 0xFFFFu;
+            for (int j = 0; j < 8; ++j) st[j] = __funnelshift_rc(m, h, 48 - d.offp - j * BITS) & 0xFFFFu;
         } else {
-            const uint32_t wc = w[(a + 2) % NW];
-            const uint32_t l = __funnelshift_r(wc, wb, sh16);
+            const uint32_t wc = *reinterpret_cast<const uint32_t*>(tile + d.o3);
+            const uint32_t l = __funnelshift_r(wc, wb, d.sh16);
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
-                const int q = offp + j * BITS;
+                const int q = d.offp + j * BITS;
                 const uint32_t v0 = __funnelshift_rc(m, h, 48 - q);
                 const uint32_t v1 = __funnelshift_rc(l, m, 80 - q);
                 st[j] = (q <= 48 ? v0 : v1) & 0xFFFFu;
@@ -110,6 +141,13 @@ __device__ __forceinline__ void decode_lane(const uint32_t* __restrict__ w, int 
     b[1] = cb_pair<CB>(st[2], st[3]);
     b[2] = cb_pair<CB>(st[4], st[5]);
     b[3] = cb_pair<CB>(st[6], st[7]);
+}
+
+// One lane's eight positions of the tile at `w` (the per-lane setup done in place).
+template <int BITS, int CB>
+__device__ __forceinline__ void decode_lane(const uint32_t* __restrict__ w, int lane, uint32_t b[4]) {
+    const LaneDec<BITS> d = lane_dec<BITS>(lane);
+    decode_tile<BITS, CB>(reinterpret_cast<const uint8_t*>(w), d, b);
 }
 
 // ------------------------------------------------------------------------------------------ 128-point rotation
@@ -153,16 +191,27 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 // Bounded wait for the phase of `parity`; false (and the error word set) when it never completed.
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+// Bounded wait for the phase of `parity`: the thread is suspended by the hardware between tries (it takes no issue
+// slots while it waits), and gives up after kWaitLimitNs with the error word set.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int32_t* err) {
     const uint32_t a = smem_u32(bar);
-    for (int i = 0; i < kWaitLimit; ++i) {
+    uint64_t t0 = 0;
+    for (;;) {
         uint32_t done;
         asm volatile(
-            "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+            "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
             : "=r"(done)
-            : "r"(a), "r"(parity)
+            : "r"(a), "r"(parity), "r"(kSuspendNs)
             : "memory");
         if (done) return true;
+        const uint64_t now = globaltimer_ns();
+        if (!t0) t0 = now;
+        else if (now - t0 > kWaitLimitNs) break;
     }
     if (err) atomicOr(err, 1);
     return false;

@@ -58,46 +58,50 @@ __global__ void k_decode_what(const uint32_t* __restrict__ record, int64_t rows,
 }
 
 // ------------------------------------------------------------------------------------------ prep
-// One warp a (sorted row, 128-block of the class's input width). gate_up (moe_exl3_prep_gu, and the tensor-core
+// One warp a sorted row, every 128-block of the class's input width. gate_up (moe_exl3_prep_gu, and the tensor-core
 // path's xr): the token row a[sorted_tok / top_k] rotated with suh into [0, C) and with suh.1 into [C, 2C) of row i;
 // rows outside the runs are not written; a row whose sorted_tok is negative is zero across 2C
 // (docs/OPS-exl3.md:128-142). down (h_rot 0 on the tensor-core path): row i of h rotated with suh into [0, C).
 __global__ void k_prep(const Exl3bOp op, uint16_t* __restrict__ dst_base, int64_t dst_pitch) {
     const int lane = threadIdx.x & 31;
     const bool gu = op.op != EXL3B_OP_DOWN;
-    const int64_t nblk = op.x_cols / 128;
-    const int64_t task = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
-    const int64_t i = task / nblk, blk = task % nblk;
+    const int64_t i = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;   // one warp a sorted row
     if (i >= op.T) return;
     const int64_t lo = op.expert_offset[0], hi = op.expert_offset[op.n_expert];
     if (i < lo || i >= hi) return;
-    // the owner: largest e with off[e] <= i
+    // the owner, once a row: largest e with off[e] <= i
     int64_t a = 0, b = op.n_expert;
     while (b - a > 1) {
         const int64_t mid = (a + b) / 2;
         if (op.expert_offset[mid] <= i) a = mid; else b = mid;
     }
     const ExpertView ev = expert_view(op, a);
-    if (blk * 128 >= ev.C) return;
     uint16_t* y = dst_base + i * dst_pitch;
     const int32_t tok = op.sorted_tok[i];
-    for (int half = 0; half < (gu ? 2 : 1); ++half) {
-        uint16_t* dst = y + half * ev.C + blk * 128 + 4 * lane;
-        if (tok < 0) {
+    const int nhalf = gu ? 2 : 1;
+    if (tok < 0) {
+        for (int64_t c = 4 * lane; c < nhalf * ev.C; c += 128) {
 #pragma unroll
-            for (int q = 0; q < 4; ++q) dst[q] = 0;
-            continue;
+            for (int q = 0; q < 4; ++q) y[c + q] = 0;
         }
-        const int64_t src_row = gu ? (int64_t)(tok / op.top_k) : i;
-        const uint16_t* src = static_cast<const uint16_t*>(op.x) + src_row * op.x_pitch + blk * 128;
-        float v[4];
-        const bool bf = gu && op.x_bf16;
+        return;
+    }
+    const int64_t src_row = gu ? (int64_t)(tok / op.top_k) : i;
+    const uint16_t* src = static_cast<const uint16_t*>(op.x) + src_row * op.x_pitch;
+    const bool bf = gu && op.x_bf16;
+    const uint16_t* s0 = static_cast<const uint16_t*>(tab_entry(op.cls[ev.c].suh, ev.j));
+    const uint16_t* s1 = gu ? static_cast<const uint16_t*>(tab_entry(op.cls[ev.c].suh1, ev.j)) : s0;
+    for (int64_t blk = 0; blk * 128 < ev.C; ++blk) {
+        float x[4];
 #pragma unroll
-        for (int q = 0; q < 4; ++q) v[q] = bf ? bf2f(src[4 * lane + q]) : h2f(src[4 * lane + q]);
-        const Exl3bTab& st = half ? op.cls[ev.c].suh1 : op.cls[ev.c].suh;
-        prologue_warp(v, static_cast<const uint16_t*>(tab_entry(st, ev.j)) + blk * 128, lane);
+        for (int q = 0; q < 4; ++q) x[q] = bf ? bf2f(src[blk * 128 + 4 * lane + q]) : h2f(src[blk * 128 + 4 * lane + q]);
+        for (int half = 0; half < nhalf; ++half) {
+            float v[4] = { x[0], x[1], x[2], x[3] };
+            prologue_warp(v, (half ? s1 : s0) + blk * 128, lane);
+            uint16_t* dst = y + half * ev.C + blk * 128 + 4 * lane;
 #pragma unroll
-        for (int q = 0; q < 4; ++q) dst[q] = f2h(v[q]);
+            for (int q = 0; q < 4; ++q) dst[q] = f2h(v[q]);
+        }
     }
 }
 
@@ -526,7 +530,7 @@ int exl3b_cuda_decode_what(const void* record, int64_t rows, int64_t cols, int b
 // The rotation pass into `dst` (row pitch `dst_pitch` elements): prep_gu's xr (gate_up ops) or down's rotated h.
 int exl3b_cuda_prep(const Exl3bOp* op, void* dst, int64_t dst_pitch, void* stream) {
     if (op->T <= 0) return 0;
-    const int64_t tasks = op->T * (op->x_cols / 128);
+    const int64_t tasks = op->T;
     const int wpb = 8;
     k_prep<<<(unsigned)((tasks + wpb - 1) / wpb), wpb * 32, 0, as_stream(stream)>>>(*op, static_cast<uint16_t*>(dst),
                                                                                      dst_pitch);

@@ -4,13 +4,13 @@
 // One persistent CTA an SM walks the unit list -- unit = (expert, up to 64 of its sorted rows, two 128-row output
 // blocks: gate block b with up block b for gate_up, blocks 2q and 2q+1 for down) -- with warp-specialised roles:
 //
-//   warps 0..3   epilogue: tcgen05.ld of a finished unit's accumulators (lane quadrant = warp), the rotation over n
-//                (transposed through shared memory), svh, SiLU(gate)*up and h_rot / bf16, stores
-//   warp 4       producer: cp.async.bulk (TMA) of the unit's record rows, and cp.async.bulk.tensor of the input rows
+//   warps 0..7   epilogue: tcgen05.ld of a finished unit's accumulators (lane quadrant = warp % 4, block = warp / 4),
+//                the rotation over n (transposed through shared memory), svh, SiLU(gate)*up and h_rot / bf16, stores
+//   warp 8       producer: cp.async.bulk (TMA) of the unit's record rows, and cp.async.bulk.tensor of the input rows
 //                (xr / h, sorted order) through a 128-byte-swizzled tensor map
-//   warp 5       TMEM allocator and MMA issuer: tcgen05.mma.cta_group::1.kind::f16, M=128 (weight rows), N=64
+//   warp 9       TMEM allocator and MMA issuer: tcgen05.mma.cta_group::1.kind::f16, M=128 (weight rows), N=64
 //                (sorted rows), K=16, A and B from shared memory, D in TMEM; tcgen05.commit frees stages
-//   warps 6..21  decoders: each lane decodes 8 trellis positions of a tile (the same bit-exact decode as the
+//   warps 10..25 decoders: each lane decodes 8 trellis positions of a tile (the same bit-exact decode as the
 //                decode-band kernel) and stores them into the A tile in the canonical K-major SWIZZLE_128B layout
 //
 // Accumulators are double-buffered (two units x 2 blocks x 64 columns = 256 TMEM columns), so the epilogue of one
@@ -27,16 +27,16 @@
 
 namespace {
 
-constexpr int kEpiWarps = 4;
-constexpr int kProdWarp = 4;
-constexpr int kMmaWarp = 5;
-constexpr int kDecWarp0 = 6;
+constexpr int kEpiWarps = 8;                         // two a TMEM lane quadrant (warp % 4)
+constexpr int kProdWarp = 8;
+constexpr int kMmaWarp = 9;
+constexpr int kDecWarp0 = 10;
 constexpr int kDecWarps = 16;
-constexpr int kTcWarps = kDecWarp0 + kDecWarps;      // 22
-constexpr int kTcThreads = kTcWarps * 32;           // 704
+constexpr int kTcWarps = kDecWarp0 + kDecWarps;      // 26
+constexpr int kTcThreads = kTcWarps * 32;           // 832
 constexpr int kNT = 64;                              // sorted rows a unit (the MMA's N)
 constexpr int kKC = 64;                              // k a pipeline chunk (one SWIZZLE_128B atom wide)
-constexpr int kStA = 3, kStB = 3, kStR = 3;          // stages of the A, B and record rings
+constexpr int kStA = 3, kStB = 3;                    // stages of the A and B rings
 constexpr int kATile = 128 * kKC * 2;                // one block's A chunk: 16 KB
 constexpr int kBTile = kNT * kKC * 2;                // one half's B chunk: 8 KB
 constexpr int kEpiCols = 128 + 4;                    // staging row (f32), padded
@@ -47,6 +47,8 @@ struct TcCfg {
     static constexpr int TILE_BYTES = 32 * BITS;                 // one 16x16 tile of the record
     static constexpr int REC_ROW = 8 * TILE_BYTES;               // one block's 8 tiles of one k row
     static constexpr int REC_STAGE = 4 * 2 * REC_ROW;            // [tk 4][blk 2][8 tiles]
+    // the record ring runs deep (the rows are small, latency-bound reads): 3..8 stages within 48 KB
+    static constexpr int ST_R = (48 * 1024 / REC_STAGE) < 3 ? 3 : (48 * 1024 / REC_STAGE) > 8 ? 8 : (48 * 1024 / REC_STAGE);
 };
 
 // ------------------------------------------------------------------------------------------ smem descriptors
@@ -133,16 +135,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* a_ring = smem;                                        // [kStA][2][16 KB]
     uint8_t* b_ring = a_ring + kStA * 2 * kATile;                  // [kStB][2][8 KB]
-    uint8_t* r_ring = b_ring + kStB * 2 * kBTile;                  // [kStR][REC_STAGE]
-    float* epi = reinterpret_cast<float*>(r_ring + kStR * Cfg::REC_STAGE);   // [2][16][kEpiCols]
+    uint8_t* r_ring = b_ring + kStB * 2 * kBTile;                  // [ST_R][REC_STAGE]
+    float* epi = reinterpret_cast<float*>(r_ring + Cfg::ST_R * Cfg::REC_STAGE);   // [2][16][kEpiCols]
     uint64_t* bars = reinterpret_cast<uint64_t*>(epi + 2 * 16 * kEpiCols);
     uint64_t* a_full = bars;                 // decoders -> MMA (count kDecWarps)
     uint64_t* a_empty = a_full + kStA;       // MMA commit -> decoders
     uint64_t* b_full = a_empty + kStA;       // producer tx -> MMA
     uint64_t* b_empty = b_full + kStB;       // MMA commit -> producer
     uint64_t* r_full = b_empty + kStB;       // producer tx -> decoders
-    uint64_t* r_empty = r_full + kStR;       // decoders -> producer (count kDecWarps)
-    uint64_t* acc_full = r_empty + kStR;     // MMA commit -> epilogue [2]
+    uint64_t* r_empty = r_full + Cfg::ST_R;  // decoders -> producer (count kDecWarps)
+    uint64_t* acc_full = r_empty + Cfg::ST_R;  // MMA commit -> epilogue [2]
     uint64_t* acc_empty = acc_full + 2;      // epilogue -> MMA [2] (count kEpiWarps)
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
     uint32_t* prefix = tmem_slot + 4;        // [n_expert + 1]
@@ -153,7 +155,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     if (tid == 0) {
         for (int s = 0; s < kStA; ++s) { mbar_init(&a_full[s], kDecWarps); mbar_init(&a_empty[s], 1); }
         for (int s = 0; s < kStB; ++s) { mbar_init(&b_full[s], 1); mbar_init(&b_empty[s], 1); }
-        for (int s = 0; s < kStR; ++s) { mbar_init(&r_full[s], 1); mbar_init(&r_empty[s], kDecWarps); }
+        for (int s = 0; s < Cfg::ST_R; ++s) { mbar_init(&r_full[s], 1); mbar_init(&r_empty[s], kDecWarps); }
         for (int s = 0; s < 2; ++s) { mbar_init(&acc_full[s], 1); mbar_init(&acc_empty[s], kEpiWarps); }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -200,7 +202,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
     // rows no unit writes are zeroed (outside the runs, dropped slots), by every CTA over a slice of the rows
     if (warp < kEpiWarps || warp >= kDecWarp0) {
-        const int64_t lt = warp < kEpiWarps ? tid : tid - (kDecWarp0 - kEpiWarps) * 32;
+        const int64_t lt = warp < kEpiWarps ? tid : tid - (kDecWarp0 - kEpiWarps) * 32;   // 0 .. nthr-1
         const int64_t nthr = (kEpiWarps + kDecWarps) * 32;
         for (int64_t i = blockIdx.x; i < op.T; i += gridDim.x) {
             const bool live = i >= op.expert_offset[0] && i < op.expert_offset[n_exp] && op.sorted_tok[i] >= 0;
@@ -212,7 +214,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
     if (warp == kProdWarp) {
         // ---------------------------------------------------------------- producer
-        if (lane == 0) {
+        // lane 0 streams the record rows, lane 1 the input-row tiles: two independent rings, so neither waits on
+        // the other's consumer
+        if (lane < 2) {
             uint32_t ri = 0, bi = 0;
             for (int64_t unit = blockIdx.x; unit < n_units; unit += gridDim.x) {
                 const TcUnit u = tc_unit(op, prefix, unit, n_pairs);
@@ -220,13 +224,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 const Exl3bClass& cl = op.cls[ev.c];
                 const int64_t wrows = GU ? ev.R / 2 : ev.R;          // rows of one record
                 if ((int64_t)u.pair * 256 >= (GU ? 2 * wrows : wrows)) continue;   // a narrower class
-                const uint16_t* rec = static_cast<const uint16_t*>(tab_entry(cl.codes, ev.j));
-                const int64_t mat_elems = (ev.C / 16) * (wrows / 16) * 16 * BITS;
                 const int nck = (int)(ev.C / kKC);
-                for (int ck = 0; ck < nck; ++ck) {
-                    // record rows of this chunk
-                    {
-                        const uint32_t s = ri % kStR, ph = (ri / kStR) & 1;
+                if (lane == 0) {
+                    const uint16_t* rec = static_cast<const uint16_t*>(tab_entry(cl.codes, ev.j));
+                    const int64_t mat_elems = (ev.C / 16) * (wrows / 16) * 16 * BITS;
+                    for (int ck = 0; ck < nck; ++ck, ++ri) {
+                        const uint32_t s = ri % Cfg::ST_R, ph = (ri / Cfg::ST_R) & 1;
                         mbar_wait(&r_empty[s], ph ^ 1, op.err);
                         mbar_expect_tx(&r_full[s], (uint32_t)Cfg::REC_STAGE);
                         for (int q = 0; q < 4; ++q) {
@@ -242,17 +245,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                                 tma_bulk_g2s(dst, src, 2 * Cfg::REC_ROW, &r_full[s]);
                             }
                         }
-                        ++ri;
                     }
-                    // input rows of this chunk (sorted rows r0 .. r0+63; zero fill past T)
-                    {
+                } else {
+                    // input rows of each chunk (sorted rows r0 .. r0+63; zero fill past T)
+                    for (int ck = 0; ck < nck; ++ck, ++bi) {
                         const uint32_t s = bi % kStB, ph = (bi / kStB) & 1;
                         mbar_wait(&b_empty[s], ph ^ 1, op.err);
                         mbar_expect_tx(&b_full[s], (uint32_t)((GU ? 2 : 1) * kBTile));
                         for (int m = 0; m < (GU ? 2 : 1); ++m)
                             tma_tile_g2s(b_ring + (s * 2 + m) * kBTile, &tmap, (int)(m * ev.C + ck * kKC), (int)u.r0,
                                          &b_full[s]);
-                        ++bi;
                     }
                 }
             }
@@ -261,6 +263,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     } else if (warp == kMmaWarp) {
         // ---------------------------------------------------------------- MMA issuer
         if (lane == 0) {
+            // the ring bases' descriptors; a stage, block and k step only add to the start-address field (the
+            // shared-memory window is below 256 KB, so the 14-bit field never carries)
+            const uint64_t a_desc0 = sw128_desc(smem_u32(a_ring)), b_desc0 = sw128_desc(smem_u32(b_ring));
             uint32_t ai = 0, bi = 0, ui = 0;
             for (int64_t unit = blockIdx.x; unit < n_units; unit += gridDim.x) {
                 const TcUnit u = tc_unit(op, prefix, unit, n_pairs);
@@ -277,14 +282,15 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     mbar_wait(&a_full[sa], pa, op.err);
                     mbar_wait(&b_full[sb], pb, op.err);
                     tc_fence_after();
-                    for (int blk = 0; blk < 2; ++blk) {
-                        const uint32_t a0 = smem_u32(a_ring + (sa * 2 + blk) * kATile);
-                        const uint32_t b0 = smem_u32(b_ring + (sb * 2 + (GU ? blk : 0)) * kBTile);
-                        const uint32_t d = tmem + buf * (2 * kNT) + blk * kNT;
+                    const uint64_t da = a_desc0 + (uint64_t)((sa * 2 * kATile) >> 4);
+                    const uint64_t db = b_desc0 + (uint64_t)((sb * 2 * kBTile) >> 4);
+                    const uint32_t d = tmem + buf * (2 * kNT);
+#pragma unroll
+                    for (int blk = 0; blk < 2; ++blk)
 #pragma unroll
                         for (int ks = 0; ks < kKC / 16; ++ks)
-                            umma_f16(d, sw128_desc(a0 + ks * 32), sw128_desc(b0 + ks * 32), (ck | ks) ? 1u : 0u);
-                    }
+                            umma_f16(d + blk * kNT, da + (uint64_t)((blk * kATile + ks * 32) >> 4),
+                                     db + (uint64_t)(((GU ? blk : 0) * kBTile + ks * 32) >> 4), (ck | ks) ? 1u : 0u);
                     umma_commit(&a_empty[sa]);
                     umma_commit(&b_empty[sb]);
                     ++ai;
@@ -300,6 +306,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const int dw = warp - kDecWarp0;           // 0..15: block dw / 8, tile column dw % 8
         const int blk = dw >> 3, tn = dw & 7;
         const int g = lane >> 2, t = lane & 3;
+        const LaneDec<BITS> ld = lane_dec<BITS>(lane);
+        // this lane's places in the SW128 K-major A tile: row n = 16 tn + g (+8) at (n/8)*1024 + (n%8)*128, the
+        // 16-byte chunk c = k/8 at (c ^ (n%8)) * 16, k = 16 q + 2t (+8)
+        const uint32_t row_lo = (uint32_t)((2 * tn) * 1024 + g * 128 + 4 * t);
+        const uint32_t xg = (uint32_t)g << 4;
+        const uint32_t tile_off = (uint32_t)(blk * Cfg::REC_ROW + tn * Cfg::TILE_BYTES);
         uint32_t ai = 0, ri = 0;
         for (int64_t unit = blockIdx.x; unit < n_units; unit += gridDim.x) {
             const TcUnit u = tc_unit(op, prefix, unit, n_pairs);
@@ -308,27 +320,21 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             if ((int64_t)u.pair * 256 >= (GU ? 2 * wrows : wrows)) continue;
             const int nck = (int)(ev.C / kKC);
             for (int ck = 0; ck < nck; ++ck) {
-                const uint32_t sr = ri % kStR, pr = (ri / kStR) & 1;
+                const uint32_t sr = ri % Cfg::ST_R, pr = (ri / Cfg::ST_R) & 1;
                 const uint32_t sa = ai % kStA, pa = (ai / kStA) & 1;
                 mbar_wait(&r_full[sr], pr, op.err);
                 mbar_wait(&a_empty[sa], pa ^ 1, op.err);
-                uint8_t* atile = a_ring + (sa * 2 + blk) * kATile;
-                const uint8_t* rst = r_ring + sr * Cfg::REC_STAGE;
+                uint8_t* arow = a_ring + (sa * 2 + blk) * kATile + row_lo;
+                const uint8_t* rst = r_ring + sr * Cfg::REC_STAGE + tile_off;
 #pragma unroll
                 for (int q = 0; q < 4; ++q) {
-                    const uint32_t* words =
-                        reinterpret_cast<const uint32_t*>(rst + (q * 2 + blk) * Cfg::REC_ROW + tn * Cfg::TILE_BYTES);
                     uint32_t b[4];
-                    decode_lane<BITS, CB>(words, lane, b);
-                    // (n = 16 tn + g (+8), k = 16 q + 2t (+8)) into the SW128 K-major tile: row n at (n/8)*1024 +
-                    // (n%8)*128, 16-byte chunk c = k/8 at (c ^ (n%8)) * 16
-                    const int c0 = 2 * q, c1 = 2 * q + 1;
-                    uint8_t* r_lo = atile + (2 * tn) * 1024 + g * 128;
-                    uint8_t* r_hi = atile + (2 * tn + 1) * 1024 + g * 128;
-                    *reinterpret_cast<uint32_t*>(r_lo + ((c0 ^ g) << 4) + 4 * t) = b[0];
-                    *reinterpret_cast<uint32_t*>(r_lo + ((c1 ^ g) << 4) + 4 * t) = b[1];
-                    *reinterpret_cast<uint32_t*>(r_hi + ((c0 ^ g) << 4) + 4 * t) = b[2];
-                    *reinterpret_cast<uint32_t*>(r_hi + ((c1 ^ g) << 4) + 4 * t) = b[3];
+                    decode_tile<BITS, CB>(rst + q * 2 * Cfg::REC_ROW, ld, b);
+                    const uint32_t c0 = ((uint32_t)(2 * q) << 4) ^ xg, c1 = ((uint32_t)(2 * q + 1) << 4) ^ xg;
+                    *reinterpret_cast<uint32_t*>(arow + c0) = b[0];
+                    *reinterpret_cast<uint32_t*>(arow + c1) = b[1];
+                    *reinterpret_cast<uint32_t*>(arow + 1024 + c0) = b[2];
+                    *reinterpret_cast<uint32_t*>(arow + 1024 + c1) = b[3];
                 }
                 fence_async_smem();
                 __syncwarp();
@@ -341,8 +347,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             }
         }
     } else {
-        // ---------------------------------------------------------------- epilogue (warps 0..3 = lane quadrants)
-        const int q = warp;                          // TMEM lanes 32q .. 32q+31 = weight rows of a block
+        // ---------------------------------------------------------------- epilogue (warps 0..7)
+        const int q = warp & 3;                      // TMEM lanes 32q .. 32q+31 = weight rows of a block
+        const int eb = warp >> 2;                    // the block this warp moves out of TMEM
         uint32_t ui = 0;
         for (int64_t unit = blockIdx.x; unit < n_units; unit += gridDim.x) {
             const TcUnit u = tc_unit(op, prefix, unit, n_pairs);
@@ -360,62 +367,76 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 }
                 continue;
             }
+            // the unit's output scales, held for all its rows: lane l owns columns 4l .. 4l+3 of each block
+            const uint16_t* svh = static_cast<const uint16_t*>(tab_entry(cl.svh, ev.j));
+            float s0[4], s1[4], sd[4];
+            const int64_t n0 = (int64_t)u.pair * (GU ? 128 : 256) + 4 * lane;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                s0[e] = h2f(svh[n0 + e]);
+                s1[e] = GU ? h2f(svh[ev.R / 2 + n0 + e]) : h2f(svh[n0 + 128 + e]);
+                sd[e] = 0.f;
+            }
+            const uint16_t* dn = GU && op.h_rot ? static_cast<const uint16_t*>(tab_entry(cl.dn_suh, ev.j)) : nullptr;
+            uint16_t dsuh[4] = { 0, 0, 0, 0 };
+            if (dn) {
+#pragma unroll
+                for (int e = 0; e < 4; ++e) dsuh[e] = dn[(int64_t)u.pair * 128 + 4 * lane + e];
+            }
+            (void)sd;
             const uint32_t buf = ui & 1, uph = (ui >> 1) & 1;
             mbar_wait(&acc_full[buf], uph, op.err);
             tc_fence_after();
-            const uint16_t* svh = static_cast<const uint16_t*>(tab_entry(cl.svh, ev.j));
-            const uint16_t* dn = GU && op.h_rot ? static_cast<const uint16_t*>(tab_entry(cl.dn_suh, ev.j)) : nullptr;
             for (int sl = 0; sl < kNT / 16; ++sl) {
                 if (sl * 16 >= u.nr) break;
-                // TMEM -> staging [blk][16 rows][n], this warp's 32 weight rows
-                for (int blk = 0; blk < 2; ++blk) {
+                // TMEM -> staging [blk][16 rows][n]: this warp's block, its 32 weight rows
+                {
                     float v[16];
-                    tmem_ld16(tmem + ((uint32_t)(32 * q) << 16) + buf * (2 * kNT) + blk * kNT + sl * 16, v);
+                    tmem_ld16(tmem + ((uint32_t)(32 * q) << 16) + buf * (2 * kNT) + eb * kNT + sl * 16, v);
 #pragma unroll
-                    for (int j = 0; j < 16; ++j) epi[(blk * 16 + j) * kEpiCols + 32 * q + lane] = v[j];
+                    for (int j = 0; j < 16; ++j) epi[(eb * 16 + j) * kEpiCols + 32 * q + lane] = v[j];
                 }
                 asm volatile("bar.sync 2, %0;" ::"n"(kEpiWarps * 32) : "memory");
-                // rows: warp q takes rows q, q+4, q+8, q+12 of the slice
-                for (int j = q; j < 16; j += kEpiWarps) {
+                // rows: warp w takes rows w and w + 8 of the slice
+                for (int j = warp; j < 16; j += kEpiWarps) {
                     const int m = sl * 16 + j;
                     if (m >= u.nr) continue;
                     const int64_t i = u.r0 + m;
                     if (op.sorted_tok[i] < 0) continue;
-                    float a[4], b[4];
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        a[e] = epi[(0 * 16 + j) * kEpiCols + 4 * lane + e];
-                        b[e] = epi[(1 * 16 + j) * kEpiCols + 4 * lane + e];
-                    }
+                    const float4 av = *reinterpret_cast<const float4*>(&epi[(0 * 16 + j) * kEpiCols + 4 * lane]);
+                    const float4 bv = *reinterpret_cast<const float4*>(&epi[(1 * 16 + j) * kEpiCols + 4 * lane]);
+                    float a[4] = { av.x, av.y, av.z, av.w }, b[4] = { bv.x, bv.y, bv.z, bv.w };
                     had128_warp(a, lane);
                     had128_warp(b, lane);
+                    uint16_t* y = static_cast<uint16_t*>(op.y) + i * op.y_pitch + n0;
                     if (GU) {
-                        const int64_t W = ev.R / 2;
-                        const int64_t n0 = (int64_t)u.pair * 128 + 4 * lane;
                         float h[4];
 #pragma unroll
                         for (int e = 0; e < 4; ++e) {
-                            const float gte = __fmul_rn(a[e], h2f(svh[n0 + e]));
-                            const float up = __fmul_rn(b[e], h2f(svh[W + n0 + e]));
+                            const float gte = __fmul_rn(a[e], s0[e]);
+                            const float up = __fmul_rn(b[e], s1[e]);
                             const float sg = __fmul_rn(gte, __frcp_rn(__fadd_rn(1.0f, expf(-gte))));
                             h[e] = __fmul_rn(sg, up);
                         }
                         if (dn) {
 #pragma unroll
-                            for (int e = 0; e < 4; ++e) h[e] = h2f(f2h(h[e]));
-                            prologue_warp(h, dn + (int64_t)u.pair * 128, lane);
+                            for (int e = 0; e < 4; ++e) h[e] = h2f(f2h(__fmul_rn(h2f(f2h(h[e])), h2f(dsuh[e]))));
+                            had128_warp(h, lane);
                         }
-                        uint16_t* y = static_cast<uint16_t*>(op.y) + i * op.y_pitch + n0;
+                        uint2 pk;
+                        pk.x = (uint32_t)f2h(h[0]) | ((uint32_t)f2h(h[1]) << 16);
+                        pk.y = (uint32_t)f2h(h[2]) | ((uint32_t)f2h(h[3]) << 16);
+                        if ((reinterpret_cast<uintptr_t>(y) & 7) == 0) {
+                            *reinterpret_cast<uint2*>(y) = pk;
+                        } else {
 #pragma unroll
-                        for (int e = 0; e < 4; ++e) y[e] = f2h(h[e]);
+                            for (int e = 0; e < 4; ++e) y[e] = f2h(h[e]);
+                        }
                     } else {
 #pragma unroll
-                        for (int hb = 0; hb < 2; ++hb) {
-                            const float* v = hb ? b : a;
-                            const int64_t n0 = (int64_t)u.pair * 256 + hb * 128 + 4 * lane;
-                            uint16_t* y = static_cast<uint16_t*>(op.y) + i * op.y_pitch + n0;
-#pragma unroll
-                            for (int e = 0; e < 4; ++e) y[e] = f2bf(__fmul_rn(v[e], h2f(svh[n0 + e])));
+                        for (int e = 0; e < 4; ++e) {
+                            y[e] = f2bf(__fmul_rn(a[e], s0[e]));
+                            y[128 + e] = f2bf(__fmul_rn(b[e], s1[e]));
                         }
                     }
                 }
@@ -489,7 +510,9 @@ static EncodeTiledFn encode_fn() {
 
 int64_t exl3b_tc_smem_bytes(int bits) {
     const int64_t rec_stage = 4 * 2 * 8 * 32 * bits;
-    const int64_t b = (int64_t)kStA * 2 * kATile + (int64_t)kStB * 2 * kBTile + kStR * rec_stage +
+    int64_t st_r = 48 * 1024 / rec_stage;
+    st_r = st_r < 3 ? 3 : st_r > 8 ? 8 : st_r;
+    const int64_t b = (int64_t)kStA * 2 * kATile + (int64_t)kStB * 2 * kBTile + st_r * rec_stage +
                       2 * 16 * kEpiCols * 4 + 256;
     return 1024 + b;   // the alignment slack; the unit prefix follows (added by the caller)
 }

@@ -170,10 +170,21 @@ class MoeLayer:
         if events:
             events[2].record()
 
+    def band_name(self, op, T):
+        """Which kernels serve one op at T tokens: the library's band rule (live experts averaging >= 16 rows take
+        the tensor-core band; gate_up's input rotation then runs once a row in k_prep)."""
+        rows = T * self.k
+        live = min(self.n_local, rows)
+        tc = live > 0 and rows // live >= 16
+        if op == "gate_up":
+            return "moe_exl3_gate_up row: k_prep + k_gemm_tc" if tc else "moe_exl3_gate_up row: k_gemm_skinny"
+        return "moe_exl3_down row: k_gemm_tc" if tc else "moe_exl3_down row: k_gemm_skinny"
+
     def launches_per_step(self, T):
         """Kernels of this library one forward launches: router, scatter (1 small / 3 large), gate_up, down,
         the gather's inverse map and the gather."""
-        return 1 + (1 if T * self.k <= 8192 else 3) + 2 + 2
+        tc = T * self.k // max(1, min(self.n_local, T * self.k)) >= 16
+        return 1 + (1 if T * self.k <= 8192 else 3) + 2 + 2 + (1 if tc else 0)
 
     def forward(self, T, stream, events=None):
         """The whole layer over the first T tokens of self.x / self.logits into self.out (f32 [T, H])."""
