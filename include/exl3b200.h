@@ -92,6 +92,23 @@ int     exl3b200_moe_gather_noalloc(const uint16_t* rows, int64_t row_pitch, con
                                     int64_t n_rows, const float* w, int64_t n_tok, int64_t top_k, int64_t width,
                                     float* y, void* stream);
 
+/* Expert parallelism (one process a GPU; expert e held by rank e / n_local; no counterpart in the reference,
+ * which runs on one device -- the engine's EP plumbing would call these around its all-to-alls):
+ *   ep_pack:      after moe_scatter over ALL n_local * world experts (sorted_pairs, expert_offset), for sorted
+ *                 row j with pair p = sorted_pairs[j] >= 0: send_x[j] = x row p / top_k (hidden f16, row pitch
+ *                 x_pitch elements), send_e[j] = ids[p] % n_local; send_counts[r] = the pairs bound for rank r
+ *                 (expert_offset[(r+1)*n_local] - expert_offset[r*n_local]). hidden and x_pitch multiples of 8,
+ *                 x and send_x 16-byte aligned.
+ *   rows_scatter: dst row idx[j] = src row j for j < n_rows (rows of row_bytes, pitches in bytes, all multiples
+ *                 of 16); idx outside [0, n_dst) skipped. Puts the down rows of the received pairs back into
+ *                 arrival order before the all-to-all that returns them. */
+int     exl3b200_ep_pack(const uint16_t* x, int64_t x_pitch, const int32_t* ids, int64_t top_k,
+                         const int32_t* sorted_pairs, int64_t n_pairs, const int32_t* expert_offset, int64_t n_local,
+                         int64_t world, int64_t hidden, uint16_t* send_x, int32_t* send_e, int32_t* send_counts,
+                         void* stream);
+int     exl3b200_rows_scatter(const void* src, int64_t src_pitch, const int32_t* idx, int64_t n_rows,
+                              int64_t row_bytes, void* dst, int64_t dst_pitch, int64_t n_dst, void* stream);
+
 /* The device error word of the current device: nonzero once a bounded wait inside a kernel gave up (the
  * launch then finished without a valid result). Reading it synchronises the device; `clear` resets it. Not
  * for a launch path. */

@@ -216,6 +216,13 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int32_
     if (err) atomicOr(err, 1);
     return false;
 }
+// mbar_wait by a whole warp, reconverged after it: every lane has seen the phase before the warp goes on to a
+// .sync.aligned or elected instruction.
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, int32_t* err) {
+    const bool ok = mbar_wait(bar, parity, err);
+    __syncwarp();
+    return ok;
+}
 // One bulk (non-tensor) TMA copy global -> this CTA's shared memory, completing on `bar`. 16-byte aligned
 // addresses and a size that is a multiple of 16 (the host refuses weights that are not).
 __device__ __forceinline__ void tma_bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
@@ -223,6 +230,20 @@ __device__ __forceinline__ void tma_bulk_g2s(void* dst, const void* src, uint32_
         "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(dst)),
         "l"(src), "r"(bytes), "r"(smem_u32(bar))
         : "memory");
+}
+// Elected-lane forms: the whole warp executes the statement, so its operands stay warp-uniform, and the one lane
+// elect.sync picks issues it. (A single-lane branch around these asynchronous-unit instructions runs them several
+// times slower than their issue rate.)
+__device__ __forceinline__ void mbar_expect_tx_el(uint64_t* bar, uint32_t bytes) {
+    asm volatile("{\n .reg .pred e;\n elect.sync _|e, 0xffffffff;\n"
+                 " @e mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n}\n" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void tma_bulk_g2s_el(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile("{\n .reg .pred e;\n elect.sync _|e, 0xffffffff;\n"
+                 " @e cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n}\n" ::
+                     "r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar))
+                 : "memory");
 }
 
 __device__ __forceinline__ void cluster_sync_all() {

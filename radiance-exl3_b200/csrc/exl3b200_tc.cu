@@ -6,16 +6,21 @@
 //
 //   warps 0..7   epilogue: tcgen05.ld of a finished unit's accumulators (lane quadrant = warp % 4, block = warp / 4),
 //                the rotation over n (transposed through shared memory), svh, SiLU(gate)*up and h_rot / bf16, stores
-//   warp 8       producer: cp.async.bulk (TMA) of the unit's record rows, and cp.async.bulk.tensor of the input rows
-//                (xr / h, sorted order) through a 128-byte-swizzled tensor map
-//   warp 9       TMEM allocator and MMA issuer: tcgen05.mma.cta_group::1.kind::f16, M=128 (weight rows), N=64
-//                (sorted rows), K=16, A and B from shared memory, D in TMEM; tcgen05.commit frees stages
-//   warps 10..25 decoders: each lane decodes 8 trellis positions of a tile (the same bit-exact decode as the
-//                decode-band kernel) and stores them into the A tile in the canonical K-major SWIZZLE_128B layout
+//   warp 8       record producer: cp.async.bulk (TMA) of the unit's record rows into a deep ring
+//   warp 9       input producer: cp.async.bulk.tensor of the input rows (xr / h, sorted order) through a
+//                128-byte-swizzled tensor map
+//   warp 10      TMEM allocator and MMA issuer: tcgen05.mma.cta_group::1.kind::f16, M=128 (weight rows), N=64
+//                (sorted rows), K=16; A (the decoded weights) from TENSOR memory, B from shared memory, D in tensor
+//                memory; tcgen05.commit frees stages
+//   warps 11..26 decoders: each lane decodes 8 trellis positions of a tile (the same bit-exact decode as the
+//                decode-band kernel) -- exactly the 16x128b.x2 tcgen05.st fragment of a 16-row x 16-k A tile
+//                (lane g: rows g, g+8; 32-bit columns t, t+4 = k pairs 2t, 2t+8) -- and stores it into tensor
+//                memory; a decoder warp writes only its own TMEM lane quadrant (warp % 4)
 //
-// Accumulators are double-buffered (two units x 2 blocks x 64 columns = 256 TMEM columns), so the epilogue of one
-// unit runs while the next is decoded. Every wait is bounded (then the error word is set); TMEM is freed by the
-// allocating warp before the CTA exits on every path.
+// Tensor memory (512 columns): two accumulator buffers (2 units x 2 blocks x 64 columns, so the epilogue of one
+// unit runs while the next is computed) and kStA A stages of 2 blocks x 32 columns (128 lanes x 64 k of f16).
+// Shared memory holds only the input-row ring, the record ring and the epilogue's staging. Every wait is bounded
+// (then the error word is set); TMEM is freed by the allocating warp before the CTA exits on every path.
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <cuda_fp16.h>
@@ -28,27 +33,32 @@
 namespace {
 
 constexpr int kEpiWarps = 8;                         // two a TMEM lane quadrant (warp % 4)
-constexpr int kProdWarp = 8;
-constexpr int kMmaWarp = 9;
-constexpr int kDecWarp0 = 10;
-constexpr int kDecWarps = 16;
-constexpr int kTcWarps = kDecWarp0 + kDecWarps;      // 26
-constexpr int kTcThreads = kTcWarps * 32;           // 832
+constexpr int kRecWarp = 8;
+constexpr int kBWarp = 9;
+constexpr int kMmaWarp = 10;
+constexpr int kDecWarp0 = 11;
+constexpr int kDecWarps = 16;                        // four a lane quadrant
+constexpr int kTcWarps = kDecWarp0 + kDecWarps;      // 27
+constexpr int kTcThreads = kTcWarps * 32;           // 864
 constexpr int kNT = 64;                              // sorted rows a unit (the MMA's N)
 constexpr int kKC = 64;                              // k a pipeline chunk (one SWIZZLE_128B atom wide)
-constexpr int kStA = 3, kStB = 3;                    // stages of the A and B rings
-constexpr int kATile = 128 * kKC * 2;                // one block's A chunk: 16 KB
+constexpr int kStA = 4;                              // A stages (tensor memory)
+constexpr int kStB = 6;                              // input-row stages (shared memory)
 constexpr int kBTile = kNT * kKC * 2;                // one half's B chunk: 8 KB
 constexpr int kEpiCols = 128 + 4;                    // staging row (f32), padded
-constexpr int kTmemCols = 256;
+constexpr int kAccCols = 2 * 2 * kNT;                // 256: two units x two blocks
+constexpr int kAStageCols = 2 * kKC / 2;             // 64: two blocks x 64 k of f16 (two a 32-bit column)
+constexpr int kTmemCols = 512;
+constexpr int kUnitTab = 160;                        // a CTA's units held in a shared table (more: looked up)
+static_assert(kAccCols + kStA * kAStageCols <= kTmemCols, "tensor memory");
 
 template <int BITS>
 struct TcCfg {
     static constexpr int TILE_BYTES = 32 * BITS;                 // one 16x16 tile of the record
     static constexpr int REC_ROW = 8 * TILE_BYTES;               // one block's 8 tiles of one k row
     static constexpr int REC_STAGE = 4 * 2 * REC_ROW;            // [tk 4][blk 2][8 tiles]
-    // the record ring runs deep (the rows are small, latency-bound reads): 3..8 stages within 48 KB
-    static constexpr int ST_R = (48 * 1024 / REC_STAGE) < 3 ? 3 : (48 * 1024 / REC_STAGE) > 8 ? 8 : (48 * 1024 / REC_STAGE);
+    // the record ring runs deep (the rows are small, latency-bound reads): 4..12 stages within 64 KB
+    static constexpr int ST_R = (64 * 1024 / REC_STAGE) < 4 ? 4 : (64 * 1024 / REC_STAGE) > 12 ? 12 : (64 * 1024 / REC_STAGE);
 };
 
 // ------------------------------------------------------------------------------------------ smem descriptors
@@ -66,14 +76,27 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t smem_addr) {
 // kind::f16, A = B = f16, D = f32, both K-major, M = 128, N = kNT.
 constexpr uint32_t kIdesc = (1u << 4) | ((uint32_t)(kNT >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
 
-__device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
+// D[tmem_d] (+)= A[tmem_a] * B[bdesc]: A 128 lanes x 16 k of f16 in 8 columns (k pair 2c, 2c+1 in column c).
+// Executed by the whole MMA warp, issued by the elected lane (a warp-uniform issue runs at the tensor cores' rate).
+__device__ __forceinline__ void umma_f16_ts_el(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t accumulate) {
     asm volatile(
-        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-        " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n}\n" ::"r"(tmem_d),
-        "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u));
+        "{\n .reg .pred p, e;\n setp.ne.b32 p, %3, 0;\n elect.sync _|e, 0xffffffff;\n"
+        " @e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %4, p;\n}\n" ::"r"(tmem_d),
+        "r"(tmem_a), "l"(bdesc), "r"(accumulate), "r"(kIdesc));
 }
-__device__ __forceinline__ void umma_commit(uint64_t* bar) {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+// 16 TMEM lanes x 8 columns from a warp: r0 (lane g, column t), r1 (g + 8, t), r2 (g, t + 4), r3 (g + 8, t + 4),
+// g = lane / 4, t = lane % 4.
+__device__ __forceinline__ void tmem_st_16x128b_x2(uint32_t taddr, uint32_t r0, uint32_t r1, uint32_t r2,
+                                                   uint32_t r3) {
+    asm volatile("tcgen05.st.sync.aligned.16x128b.x2.b32 [%0], {%1, %2, %3, %4};" ::"r"(taddr), "r"(r0), "r"(r1),
+                 "r"(r2), "r"(r3)
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void umma_commit_el(uint64_t* bar) {
+    asm volatile("{\n .reg .pred e;\n elect.sync _|e, 0xffffffff;\n"
+                 " @e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n}\n" ::
+                     "r"(smem_u32(bar))
                  : "memory");
 }
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float v[16]) {
@@ -90,12 +113,12 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float v[16]) {
 }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
-// 2-D tensor copy global -> shared (no multicast), completing on `bar`.
-__device__ __forceinline__ void tma_tile_g2s(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+// 2-D tensor copy global -> this CTA's shared memory, completing on `bar`; whole warp, elected lane issues.
+__device__ __forceinline__ void tma_tile_g2s_el(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
     asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
+        "{\n .reg .pred e;\n elect.sync _|e, 0xffffffff;\n"
+        " @e cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];\n}\n" ::
             "r"(smem_u32(dst)),
         "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
         : "memory");
@@ -133,12 +156,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     // 1024-byte alignment of every swizzled tile
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t* a_ring = smem;                                        // [kStA][2][16 KB]
-    uint8_t* b_ring = a_ring + kStA * 2 * kATile;                  // [kStB][2][8 KB]
+    uint8_t* b_ring = smem;                                        // [kStB][2][8 KB]
     uint8_t* r_ring = b_ring + kStB * 2 * kBTile;                  // [ST_R][REC_STAGE]
     float* epi = reinterpret_cast<float*>(r_ring + Cfg::ST_R * Cfg::REC_STAGE);   // [2][16][kEpiCols]
     uint64_t* bars = reinterpret_cast<uint64_t*>(epi + 2 * 16 * kEpiCols);
-    uint64_t* a_full = bars;                 // decoders -> MMA (count kDecWarps)
+    uint64_t* a_full = bars;                 // decoders -> MMA (count kDecWarps): an A stage is in tensor memory
     uint64_t* a_empty = a_full + kStA;       // MMA commit -> decoders
     uint64_t* b_full = a_empty + kStA;       // producer tx -> MMA
     uint64_t* b_empty = b_full + kStB;       // MMA commit -> producer
@@ -148,8 +170,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     uint64_t* acc_empty = acc_full + 2;      // epilogue -> MMA [2] (count kEpiWarps)
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
     uint32_t* prefix = tmem_slot + 4;        // [n_expert + 1]
+    __shared__ TcUnit utab[kUnitTab];
 
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    // the warp index through a shuffle: the compiler then knows it is warp-uniform, and so is everything a role
+    // derives from it
+    const int tid = threadIdx.x, warp = __shfl_sync(0xFFFFFFFFu, tid >> 5, 0), lane = tid & 31;
     const int64_t n_exp = op.n_expert;
 
     if (tid == 0) {
@@ -165,9 +190,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
-    // the unit list: ceil(rows_e / 64) * n_pairs units an expert, expert-major
+    // the unit list: ceil(rows_e / 64) * n_pairs units an expert, expert-major. prefix[e] = the first unit of
+    // expert e (a block-wide exclusive scan of the per-expert counts, each thread a run of experts)
     {
-        __shared__ uint32_t part[kTcThreads];
+        __shared__ uint32_t wsum[kTcWarps];
         const int64_t per = (n_exp + kTcThreads - 1) / kTcThreads;
         const int64_t e0 = tid * per, e1 = e0 + per < n_exp ? e0 + per : n_exp;
         uint32_t sum = 0;
@@ -175,146 +201,149 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             const int64_t r = op.expert_offset[e + 1] - op.expert_offset[e];
             sum += r > 0 ? (uint32_t)(((r + kNT - 1) / kNT) * n_pairs) : 0u;
         }
-        part[tid] = sum;
-        __syncthreads();
-        if (tid == 0) {
-            uint32_t acc = 0;
-            for (int t = 0; t < kTcThreads; ++t) {
-                const uint32_t v = part[t];
-                part[t] = acc;
-                acc += v;
-            }
-            prefix[n_exp] = acc;
+        uint32_t incl = sum;                                   // inclusive scan within the warp
+#pragma unroll
+        for (int d = 1; d < 32; d <<= 1) {
+            const uint32_t v = __shfl_up_sync(0xFFFFFFFFu, incl, d);
+            if (lane >= d) incl += v;
         }
+        if (lane == 31) wsum[warp] = incl;
         __syncthreads();
-        uint32_t acc = part[tid];
+        uint32_t base = 0;
+        for (int w = 0; w < warp; ++w) base += wsum[w];
+        uint32_t acc = base + incl - sum;
         for (int64_t e = e0; e < e1; ++e) {
             prefix[e] = acc;
             const int64_t r = op.expert_offset[e + 1] - op.expert_offset[e];
             acc += r > 0 ? (uint32_t)(((r + kNT - 1) / kNT) * n_pairs) : 0u;
         }
+        if (tid == kTcThreads - 1) prefix[n_exp] = acc;
     }
+    __syncthreads();
+    // this CTA's units (blockIdx.x + i * gridDim.x), looked up once into a shared table
+    const int64_t n_units = prefix[n_exp];
+    const int64_t n_mine = n_units > blockIdx.x ? (n_units - blockIdx.x + gridDim.x - 1) / gridDim.x : 0;
+    for (int64_t i = tid; i < n_mine && i < kUnitTab; i += kTcThreads)
+        utab[i] = tc_unit(op, prefix, blockIdx.x + i * gridDim.x, n_pairs);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    const int64_t n_units = prefix[n_exp];
+    auto unit_at = [&](int64_t i) -> TcUnit {
+        return i < kUnitTab ? utab[i] : tc_unit(op, prefix, blockIdx.x + i * gridDim.x, n_pairs);
+    };
 
-    // rows no unit writes are zeroed (outside the runs, dropped slots), by every CTA over a slice of the rows
+    // rows no unit writes are zeroed (outside the runs, dropped slots): the grid's threads test the rows in
+    // parallel; a thread clears the (rare) dead row it finds
     if (warp < kEpiWarps || warp >= kDecWarp0) {
         const int64_t lt = warp < kEpiWarps ? tid : tid - (kDecWarp0 - kEpiWarps) * 32;   // 0 .. nthr-1
         const int64_t nthr = (kEpiWarps + kDecWarps) * 32;
-        for (int64_t i = blockIdx.x; i < op.T; i += gridDim.x) {
-            const bool live = i >= op.expert_offset[0] && i < op.expert_offset[n_exp] && op.sorted_tok[i] >= 0;
-            if (live) continue;
+        const int64_t lo = op.expert_offset[0], hi = op.expert_offset[n_exp];
+        for (int64_t i = (int64_t)blockIdx.x * nthr + lt; i < op.T; i += (int64_t)gridDim.x * nthr) {
+            if (i >= lo && i < hi && op.sorted_tok[i] >= 0) continue;
             uint16_t* y = static_cast<uint16_t*>(op.y) + i * op.y_pitch;
-            for (int64_t c = lt; c < op.y_cols; c += nthr) y[c] = 0;
+            for (int64_t c = 0; c < op.y_cols; ++c) y[c] = 0;
         }
     }
 
-    if (warp == kProdWarp) {
-        // ---------------------------------------------------------------- producer
-        // lane 0 streams the record rows, lane 1 the input-row tiles: two independent rings, so neither waits on
-        // the other's consumer
-        if (lane < 2) {
-            uint32_t ri = 0, bi = 0;
-            for (int64_t unit = blockIdx.x; unit < n_units; unit += gridDim.x) {
-                const TcUnit u = tc_unit(op, prefix, unit, n_pairs);
-                const ExpertView ev = expert_view(op, u.e);
-                const Exl3bClass& cl = op.cls[ev.c];
-                const int64_t wrows = GU ? ev.R / 2 : ev.R;          // rows of one record
-                if ((int64_t)u.pair * 256 >= (GU ? 2 * wrows : wrows)) continue;   // a narrower class
-                const int nck = (int)(ev.C / kKC);
-                if (lane == 0) {
-                    const uint16_t* rec = static_cast<const uint16_t*>(tab_entry(cl.codes, ev.j));
-                    const int64_t mat_elems = (ev.C / 16) * (wrows / 16) * 16 * BITS;
-                    for (int ck = 0; ck < nck; ++ck, ++ri) {
-                        const uint32_t s = ri % Cfg::ST_R, ph = (ri / Cfg::ST_R) & 1;
-                        mbar_wait(&r_empty[s], ph ^ 1, op.err);
-                        mbar_expect_tx(&r_full[s], (uint32_t)Cfg::REC_STAGE);
-                        for (int q = 0; q < 4; ++q) {
-                            const int64_t tk = (int64_t)ck * 4 + q;
-                            uint8_t* dst = r_ring + s * Cfg::REC_STAGE + q * 2 * Cfg::REC_ROW;
-                            if (GU) {
-                                for (int m = 0; m < 2; ++m) {
-                                    const uint16_t* src = rec + m * mat_elems + (tk * (wrows / 16) + u.pair * 8) * 16 * BITS;
-                                    tma_bulk_g2s(dst + m * Cfg::REC_ROW, src, Cfg::REC_ROW, &r_full[s]);
-                                }
-                            } else {
-                                const uint16_t* src = rec + (tk * (wrows / 16) + u.pair * 16) * 16 * BITS;
-                                tma_bulk_g2s(dst, src, 2 * Cfg::REC_ROW, &r_full[s]);
+    if (warp == kRecWarp || warp == kBWarp) {
+        // ---------------------------------------------------------------- producers
+        // warp 8 streams the record rows, warp 9 the input-row tiles: two rings, two warps, so neither producer's
+        // wait holds up the other. Each warp runs its loop whole; one elected lane issues the copies.
+        uint32_t ri = 0, bi = 0;
+        for (int64_t ui_ = 0; ui_ < n_mine; ++ui_) {
+            const TcUnit u = unit_at(ui_);
+            const ExpertView ev = expert_view(op, u.e);
+            const Exl3bClass& cl = op.cls[ev.c];
+            const int64_t wrows = GU ? ev.R / 2 : ev.R;          // rows of one record
+            if ((int64_t)u.pair * 256 >= (GU ? 2 * wrows : wrows)) continue;   // a narrower class
+            const int nck = (int)(ev.C / kKC);
+            if (warp == kRecWarp) {
+                const uint16_t* rec = static_cast<const uint16_t*>(tab_entry(cl.codes, ev.j));
+                const int64_t mat_elems = (ev.C / 16) * (wrows / 16) * 16 * BITS;
+                for (int ck = 0; ck < nck; ++ck, ++ri) {
+                    const uint32_t s = ri % Cfg::ST_R, ph = (ri / Cfg::ST_R) & 1;
+                    mbar_wait_warp(&r_empty[s], ph ^ 1, op.err);
+                    mbar_expect_tx_el(&r_full[s], (uint32_t)Cfg::REC_STAGE);
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        const int64_t tk = (int64_t)ck * 4 + q;
+                        uint8_t* dst = r_ring + s * Cfg::REC_STAGE + q * 2 * Cfg::REC_ROW;
+                        if (GU) {
+#pragma unroll
+                            for (int m = 0; m < 2; ++m) {
+                                const uint16_t* src = rec + m * mat_elems + (tk * (wrows / 16) + u.pair * 8) * 16 * BITS;
+                                tma_bulk_g2s_el(dst + m * Cfg::REC_ROW, src, Cfg::REC_ROW, &r_full[s]);
                             }
+                        } else {
+                            const uint16_t* src = rec + (tk * (wrows / 16) + u.pair * 16) * 16 * BITS;
+                            tma_bulk_g2s_el(dst, src, 2 * Cfg::REC_ROW, &r_full[s]);
                         }
                     }
-                } else {
-                    // input rows of each chunk (sorted rows r0 .. r0+63; zero fill past T)
-                    for (int ck = 0; ck < nck; ++ck, ++bi) {
-                        const uint32_t s = bi % kStB, ph = (bi / kStB) & 1;
-                        mbar_wait(&b_empty[s], ph ^ 1, op.err);
-                        mbar_expect_tx(&b_full[s], (uint32_t)((GU ? 2 : 1) * kBTile));
-                        for (int m = 0; m < (GU ? 2 : 1); ++m)
-                            tma_tile_g2s(b_ring + (s * 2 + m) * kBTile, &tmap, (int)(m * ev.C + ck * kKC), (int)u.r0,
-                                         &b_full[s]);
-                    }
+                }
+            } else {
+                // input rows of each chunk (sorted rows r0 .. r0+63; zero fill past T)
+                for (int ck = 0; ck < nck; ++ck, ++bi) {
+                    const uint32_t s = bi % kStB, ph = (bi / kStB) & 1;
+                    mbar_wait_warp(&b_empty[s], ph ^ 1, op.err);
+                    mbar_expect_tx_el(&b_full[s], (uint32_t)((GU ? 2 : 1) * kBTile));
+#pragma unroll
+                    for (int m = 0; m < (GU ? 2 : 1); ++m)
+                        tma_tile_g2s_el(b_ring + (s * 2 + m) * kBTile, &tmap, (int)(m * ev.C + ck * kKC), (int)u.r0,
+                                        &b_full[s]);
                 }
             }
         }
-        __syncwarp();
     } else if (warp == kMmaWarp) {
-        // ---------------------------------------------------------------- MMA issuer
-        if (lane == 0) {
-            // the ring bases' descriptors; a stage, block and k step only add to the start-address field (the
-            // shared-memory window is below 256 KB, so the 14-bit field never carries)
-            const uint64_t a_desc0 = sw128_desc(smem_u32(a_ring)), b_desc0 = sw128_desc(smem_u32(b_ring));
-            uint32_t ai = 0, bi = 0, ui = 0;
-            for (int64_t unit = blockIdx.x; unit < n_units; unit += gridDim.x) {
-                const TcUnit u = tc_unit(op, prefix, unit, n_pairs);
-                const ExpertView ev = expert_view(op, u.e);
-                const int64_t wrows = GU ? ev.R / 2 : ev.R;
-                if ((int64_t)u.pair * 256 >= (GU ? 2 * wrows : wrows)) continue;
-                const uint32_t buf = ui & 1, uph = (ui >> 1) & 1;
-                mbar_wait(&acc_empty[buf], uph ^ 1, op.err);
+        // ---------------------------------------------------------------- MMA issuer (whole warp, elected lane)
+        // the input ring's base descriptor; a stage, half and k step only add to the start-address field (the
+        // shared-memory window is below 256 KB, so the 14-bit field never carries)
+        const uint64_t b_desc0 = sw128_desc(smem_u32(b_ring));
+        uint32_t ai = 0, bi = 0, ui = 0;
+        for (int64_t ui_ = 0; ui_ < n_mine; ++ui_) {
+            const TcUnit u = unit_at(ui_);
+            const ExpertView ev = expert_view(op, u.e);
+            const int64_t wrows = GU ? ev.R / 2 : ev.R;
+            if ((int64_t)u.pair * 256 >= (GU ? 2 * wrows : wrows)) continue;
+            const uint32_t buf = ui & 1, uph = (ui >> 1) & 1;
+            mbar_wait_warp(&acc_empty[buf], uph ^ 1, op.err);
+            tc_fence_after();
+            const int nck = (int)(ev.C / kKC);
+            const uint32_t d = tmem + buf * (2 * kNT);
+            for (int ck = 0; ck < nck; ++ck) {
+                const uint32_t sa = ai % kStA, pa = (ai / kStA) & 1;
+                const uint32_t sb = bi % kStB, pb = (bi / kStB) & 1;
+                mbar_wait_warp(&a_full[sa], pa, op.err);
+                mbar_wait_warp(&b_full[sb], pb, op.err);
                 tc_fence_after();
-                const int nck = (int)(ev.C / kKC);
-                for (int ck = 0; ck < nck; ++ck) {
-                    const uint32_t sa = ai % kStA, pa = (ai / kStA) & 1;
-                    const uint32_t sb = bi % kStB, pb = (bi / kStB) & 1;
-                    mbar_wait(&a_full[sa], pa, op.err);
-                    mbar_wait(&b_full[sb], pb, op.err);
-                    tc_fence_after();
-                    const uint64_t da = a_desc0 + (uint64_t)((sa * 2 * kATile) >> 4);
-                    const uint64_t db = b_desc0 + (uint64_t)((sb * 2 * kBTile) >> 4);
-                    const uint32_t d = tmem + buf * (2 * kNT);
+                const uint32_t ta = tmem + kAccCols + sa * kAStageCols;
+                const uint64_t db = b_desc0 + (uint64_t)((sb * 2 * kBTile) >> 4);
 #pragma unroll
-                    for (int blk = 0; blk < 2; ++blk)
+                for (int blk = 0; blk < 2; ++blk)
 #pragma unroll
-                        for (int ks = 0; ks < kKC / 16; ++ks)
-                            umma_f16(d + blk * kNT, da + (uint64_t)((blk * kATile + ks * 32) >> 4),
-                                     db + (uint64_t)(((GU ? blk : 0) * kBTile + ks * 32) >> 4), (ck | ks) ? 1u : 0u);
-                    umma_commit(&a_empty[sa]);
-                    umma_commit(&b_empty[sb]);
-                    ++ai;
-                    ++bi;
-                }
-                umma_commit(&acc_full[buf]);
-                ++ui;
+                    for (int ks = 0; ks < kKC / 16; ++ks)
+                        umma_f16_ts_el(d + blk * kNT, ta + blk * (kKC / 2) + ks * 8,
+                                       db + (uint64_t)(((GU ? blk : 0) * kBTile + ks * 32) >> 4), (ck | ks) ? 1u : 0u);
+                umma_commit_el(&a_empty[sa]);
+                umma_commit_el(&b_empty[sb]);
+                ++ai;
+                ++bi;
             }
+            umma_commit_el(&acc_full[buf]);
+            ++ui;
         }
-        __syncwarp();
     } else if (warp >= kDecWarp0) {
         // ---------------------------------------------------------------- decoders
-        const int dw = warp - kDecWarp0;           // 0..15: block dw / 8, tile column dw % 8
-        const int blk = dw >> 3, tn = dw & 7;
-        const int g = lane >> 2, t = lane & 3;
+        // warp -> (lane quadrant q = warp % 4, j): block j / 2, tile row tn = 2q + j % 2 -- weight rows 16 tn ..
+        // 16 tn + 15 of the block, TMEM lanes of quadrant q only; every k tile of the chunk
+        const int q = warp & 3, j = (warp - kDecWarp0) >> 2;
+        const int blk = j >> 1, tn = 2 * q + (j & 1);
         const LaneDec<BITS> ld = lane_dec<BITS>(lane);
-        // this lane's places in the SW128 K-major A tile: row n = 16 tn + g (+8) at (n/8)*1024 + (n%8)*128, the
-        // 16-byte chunk c = k/8 at (c ^ (n%8)) * 16, k = 16 q + 2t (+8)
-        const uint32_t row_lo = (uint32_t)((2 * tn) * 1024 + g * 128 + 4 * t);
-        const uint32_t xg = (uint32_t)g << 4;
         const uint32_t tile_off = (uint32_t)(blk * Cfg::REC_ROW + tn * Cfg::TILE_BYTES);
+        const uint32_t a_t0 = tmem + ((uint32_t)(16 * tn) << 16) + kAccCols + blk * (kKC / 2);
         uint32_t ai = 0, ri = 0;
-        for (int64_t unit = blockIdx.x; unit < n_units; unit += gridDim.x) {
-            const TcUnit u = tc_unit(op, prefix, unit, n_pairs);
+        for (int64_t ui_ = 0; ui_ < n_mine; ++ui_) {
+            const TcUnit u = unit_at(ui_);
             const ExpertView ev = expert_view(op, u.e);
             const int64_t wrows = GU ? ev.R / 2 : ev.R;
             if ((int64_t)u.pair * 256 >= (GU ? 2 * wrows : wrows)) continue;
@@ -322,21 +351,19 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             for (int ck = 0; ck < nck; ++ck) {
                 const uint32_t sr = ri % Cfg::ST_R, pr = (ri / Cfg::ST_R) & 1;
                 const uint32_t sa = ai % kStA, pa = (ai / kStA) & 1;
-                mbar_wait(&r_full[sr], pr, op.err);
-                mbar_wait(&a_empty[sa], pa ^ 1, op.err);
-                uint8_t* arow = a_ring + (sa * 2 + blk) * kATile + row_lo;
+                mbar_wait_warp(&r_full[sr], pr, op.err);
+                mbar_wait_warp(&a_empty[sa], pa ^ 1, op.err);
+                tc_fence_after();
                 const uint8_t* rst = r_ring + sr * Cfg::REC_STAGE + tile_off;
+                const uint32_t ta = a_t0 + sa * kAStageCols;
 #pragma unroll
-                for (int q = 0; q < 4; ++q) {
+                for (int tk = 0; tk < 4; ++tk) {
                     uint32_t b[4];
-                    decode_tile<BITS, CB>(rst + q * 2 * Cfg::REC_ROW, ld, b);
-                    const uint32_t c0 = ((uint32_t)(2 * q) << 4) ^ xg, c1 = ((uint32_t)(2 * q + 1) << 4) ^ xg;
-                    *reinterpret_cast<uint32_t*>(arow + c0) = b[0];
-                    *reinterpret_cast<uint32_t*>(arow + c1) = b[1];
-                    *reinterpret_cast<uint32_t*>(arow + 1024 + c0) = b[2];
-                    *reinterpret_cast<uint32_t*>(arow + 1024 + c1) = b[3];
+                    decode_tile<BITS, CB>(rst + tk * 2 * Cfg::REC_ROW, ld, b);
+                    tmem_st_16x128b_x2(ta + tk * 8, b[0], b[2], b[1], b[3]);
                 }
-                fence_async_smem();
+                tmem_wait_st();
+                tc_fence_before();
                 __syncwarp();
                 if (lane == 0) {
                     mbar_arrive(&a_full[sa]);
@@ -351,8 +378,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const int q = warp & 3;                      // TMEM lanes 32q .. 32q+31 = weight rows of a block
         const int eb = warp >> 2;                    // the block this warp moves out of TMEM
         uint32_t ui = 0;
-        for (int64_t unit = blockIdx.x; unit < n_units; unit += gridDim.x) {
-            const TcUnit u = tc_unit(op, prefix, unit, n_pairs);
+        for (int64_t ui_ = 0; ui_ < n_mine; ++ui_) {
+            const TcUnit u = unit_at(ui_);
             const ExpertView ev = expert_view(op, u.e);
             const Exl3bClass& cl = op.cls[ev.c];
             const int64_t wrows = GU ? ev.R / 2 : ev.R;
@@ -385,7 +412,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             }
             (void)sd;
             const uint32_t buf = ui & 1, uph = (ui >> 1) & 1;
-            mbar_wait(&acc_full[buf], uph, op.err);
+            mbar_wait_warp(&acc_full[buf], uph, op.err);
             tc_fence_after();
             for (int sl = 0; sl < kNT / 16; ++sl) {
                 if (sl * 16 >= u.nr) break;
@@ -510,10 +537,9 @@ static EncodeTiledFn encode_fn() {
 
 int64_t exl3b_tc_smem_bytes(int bits) {
     const int64_t rec_stage = 4 * 2 * 8 * 32 * bits;
-    int64_t st_r = 48 * 1024 / rec_stage;
-    st_r = st_r < 3 ? 3 : st_r > 8 ? 8 : st_r;
-    const int64_t b = (int64_t)kStA * 2 * kATile + (int64_t)kStB * 2 * kBTile + st_r * rec_stage +
-                      2 * 16 * kEpiCols * 4 + 256;
+    int64_t st_r = 64 * 1024 / rec_stage;
+    st_r = st_r < 4 ? 4 : st_r > 12 ? 12 : st_r;
+    const int64_t b = (int64_t)kStB * 2 * kBTile + st_r * rec_stage + 2 * 16 * kEpiCols * 4 + 512;
     return 1024 + b;   // the alignment slack; the unit prefix follows (added by the caller)
 }
 

@@ -73,6 +73,13 @@ class MoeLayer:
         self.rec_dtype = self._stored_dtype()
         self._args = {}
 
+    def load_experts(self, src, base):
+        """Copy experts [base, base + n_local) of `src` (a layer of the same shapes holding more experts) into this
+        layer's resident weights: the records, suh, suh.1, svh and the down scales."""
+        sl = slice(base, base + self.n_local)
+        for name in ("gu_rec", "dn_rec", "suh", "suh1", "svh_gu", "dn_suh", "svh_dn"):
+            getattr(self, name).copy_(getattr(src, name)[sl])
+
     # ------------------------------------------------------------------ the stored codes dtype
     def _stored_dtype(self):
         """Ask the gate_up row's layout hook what it stores a codes plane as (its RadLayout dtype)."""
@@ -102,6 +109,8 @@ class MoeLayer:
         key = (T, rows, x_ptr, top_k, M)
         if key in self._args:
             return self._args[key]
+        if len(self._args) >= 32:     # pass sizes that vary step to step (expert parallelism): keep the cache bounded
+            self._args.clear()
         k = top_k or self.k
         E, H, W = self.n_local, self.H, self.W
         keep = []
@@ -156,6 +165,10 @@ class MoeLayer:
     def experts(self, T, rows, stream, x_ptr=None, top_k=None, M=None, events=None):
         """gate_up then down over the sorted rows already in sorted_tok / offset. `events`: three
         torch.cuda.Event recorded before gate_up, between the two and after down (on the current stream)."""
+        if rows == 0:                 # nothing routed here: no launch, the events still mark the (empty) ops
+            for e in events or ():
+                e.record()
+            return
         a_gu, a_dn, _ = self._build(T, rows, x_ptr, top_k, M)
         if events:
             events[0].record()

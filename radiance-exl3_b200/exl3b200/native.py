@@ -23,6 +23,8 @@ class Native:
         L.exl3b200_moe_gather_work_bytes.argtypes = [_I64, _I64]
         L.exl3b200_moe_gather.argtypes = [_VP, _I64, _VP, _I64, _VP, _I64, _I64, _I64, _VP, _VP, _VP]
         L.exl3b200_read_error.argtypes = [_I, C.POINTER(C.c_int32)]
+        L.exl3b200_ep_pack.argtypes = [_VP, _I64, _VP, _I64, _VP, _I64, _VP, _I64, _I64, _I64, _VP, _VP, _VP, _VP]
+        L.exl3b200_rows_scatter.argtypes = [_VP, _I64, _VP, _I64, _I64, _VP, _I64, _I64, _VP]
 
     @staticmethod
     def _check(rc, what):
@@ -63,3 +65,13 @@ class Native:
         v = C.c_int32(0)
         self._check(self.lib.exl3b200_read_error(1 if clear else 0, C.byref(v)), "exl3b200_read_error")
         return v.value
+
+    # ------------------------------------------------------------------ expert parallelism
+    def ep_pack(self, x, x_pitch, ids, top_k, sorted_pairs, n_pairs, expert_offset, n_local, world, hidden, send_x,
+                send_e, send_counts, stream=0):
+        self._check(self.lib.exl3b200_ep_pack(x, x_pitch, ids, top_k, sorted_pairs, n_pairs, expert_offset, n_local,
+                                              world, hidden, send_x, send_e, send_counts, stream), "exl3b200_ep_pack")
+
+    def rows_scatter(self, src, src_pitch, idx, n_rows, row_bytes, dst, dst_pitch, n_dst, stream=0):
+        self._check(self.lib.exl3b200_rows_scatter(src, src_pitch, idx, n_rows, row_bytes, dst, dst_pitch, n_dst,
+                                                   stream), "exl3b200_rows_scatter")

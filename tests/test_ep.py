@@ -1,0 +1,305 @@
+"""Expert parallelism: the exchange of exl3b200/ep.py on CPU ranks over gloo (world sizes 2 and 4), and on the GPU
+the two EP kernels (ep_pack, rows_scatter) against their numpy statements and, with two GPUs, the whole EP layer
+over NCCL against the one-GPU layer.
+
+On CPU the device steps are host stand-ins with the same contracts: the oracle's stable scatter and gather, numpy
+for the pack and the row scatter, and a synthetic expert (row * a_e + b_e, rounded to bf16) that makes every row's
+result depend on the GLOBAL expert id -- so a row sent to the wrong rank, expert or position changes the output.
+The EP output must equal, bit for bit, the single-process layer computed with the same stand-ins."""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+
+from oracle_bind import Oracle
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _bf16_bits(a32):
+    return torch.from_numpy(np.ascontiguousarray(a32, np.float32)).to(torch.bfloat16).view(torch.int16).numpy() \
+        .view(np.uint16)
+
+
+def _f16_to_f32(bits):
+    return np.asarray(bits, np.uint16).view(np.float16).astype(np.float32)
+
+
+def expert_fn(x_bits, e, n_expert):
+    """The synthetic expert: bf16(x * a_e + b_e) with a_e, b_e distinct per global expert."""
+    a = 1.0 + (e + 1) / (4.0 * n_expert)
+    b = (e - n_expert / 2) / 64.0
+    return _bf16_bits(_f16_to_f32(x_bits) * np.float32(a) + np.float32(b))
+
+
+def router_np(logits, k):
+    """softmax then the k largest, ties to the lower id (the router kernel's contract)."""
+    mx = logits.max(axis=1, keepdims=True)
+    p = np.exp(logits - mx)
+    p = p / p.sum(axis=1, keepdims=True)
+    order = np.argsort(-logits, axis=1, kind="stable")[:, :k]
+    return order.astype(np.int32), np.take_along_axis(p, order, axis=1).astype(np.float32)
+
+
+class CpuOps:
+    """Host stand-ins of DeviceOps on CPU tensors (same method contracts)."""
+
+    def __init__(self, orc, rank, n_local, n_expert, hidden, max_rows):
+        self.orc, self.rank, self.nl, self.E, self.H = orc, rank, n_local, n_expert, hidden
+        self._loc = (torch.zeros(max_rows, dtype=torch.int32), torch.zeros(n_local + 1, dtype=torch.int32),
+                     torch.zeros((max_rows, hidden), dtype=torch.bfloat16))
+
+    def local_buffers(self):
+        return self._loc
+
+    def router(self, logits, T, E, k, ids, w):
+        i, ww = router_np(logits[:T].numpy(), k)
+        ids[:T * k] = torch.from_numpy(i.reshape(-1))
+        w[:T * k] = torch.from_numpy(ww.reshape(-1))
+
+    def scatter(self, ids, n_pairs, n_expert, sorted_tok, offset):
+        st, off = self.orc.scatter(ids[:n_pairs].numpy(), n_expert)
+        sorted_tok[:n_pairs] = torch.from_numpy(st)
+        offset[:] = torch.from_numpy(off)
+
+    def pack(self, x, ids, k, sorted_pairs, n_pairs, offset, n_local, world, send_x, send_e, counts):
+        off = offset.numpy()
+        for r in range(world):
+            counts[r] = int(off[(r + 1) * n_local] - off[r * n_local])
+        xs = x.view(torch.int16).numpy()
+        sx = send_x.view(torch.int16).numpy()
+        for j in range(n_pairs):
+            p = int(sorted_pairs[j])
+            if p < 0:
+                continue
+            sx[j] = xs[p // k]
+            send_e[j] = int(ids[p]) % n_local
+
+    def experts(self, recv_x, R, events=None):
+        st, off, y = self._loc
+        xs = recv_x.view(torch.int16).numpy().view(np.uint16)
+        ys = y.view(torch.int16).numpy()
+        o = off.numpy()
+        for e in range(self.nl):
+            for j in range(o[e], o[e + 1]):
+                ys[j] = expert_fn(xs[int(st[j])], self.rank * self.nl + e, self.E).view(np.int16)
+
+    def rows_scatter(self, src, idx, n_rows, dst, n_dst):
+        for j in range(n_rows):
+            d = int(idx[j])
+            if 0 <= d < n_dst:
+                dst[d] = src[j]
+
+    def gather(self, rows, sorted_pairs, n_rows, w, T, k, out):
+        y = self.orc.gather(rows[:n_rows].view(torch.int16).numpy().view(np.uint16), sorted_pairs[:n_rows].numpy(),
+                            w[:T * k].numpy(), T, k, rows.shape[1])
+        out[:T] = torch.from_numpy(y)
+
+
+def single_layer(orc, x_bits, logits, k, n_expert):
+    """The one-process layer with the same stand-ins: every pair's row, then the gather over pairs in order."""
+    T = x_bits.shape[0]
+    ids, w = router_np(logits, k)
+    rows = np.stack([expert_fn(x_bits[p // k], int(ids.reshape(-1)[p]), n_expert) for p in range(T * k)])
+    return orc.gather(rows, np.arange(T * k, dtype=np.int32), w.reshape(-1), T, k, x_bits.shape[1])
+
+
+def _inputs(rank, T, E, H, skew):
+    rng = np.random.default_rng(100 + rank)
+    x = rng.standard_normal((T, H)).astype(np.float16).view(np.uint16)
+    logits = rng.standard_normal((T, E)).astype(np.float32)
+    if skew:   # every token routes to the first rank's experts: the other ranks receive nothing
+        logits[:, : E // 4] += 50.0
+    return x, logits
+
+
+def _ep_rank(rank, world, port, T, E, H, k, skew, q):
+    import torch.distributed as dist
+    from exl3b200.ep import EpLayer
+    os.environ["MASTER_ADDR"], os.environ["MASTER_PORT"] = "127.0.0.1", str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        orc = Oracle()
+        nl = E // world
+        ops = CpuOps(orc, rank, nl, E, H, world * T * k)
+        layer = EpLayer(rank=rank, world=world, n_expert=E, hidden=H, width=128, top_k=k, max_tokens=T,
+                        device="cpu", ops=ops)
+        x, logits = _inputs(rank, T, E, H, skew)
+        layer.x[:T] = torch.from_numpy(x.view(np.int16)).view(torch.float16)
+        layer.logits[:T] = torch.from_numpy(logits)
+        for _ in range(2):   # twice: the second step reuses every buffer
+            layer.forward(T)
+        got = layer.out[:T].numpy().copy()
+        want = single_layer(orc, x, logits, k, E)
+        q.put((rank, bool(np.array_equal(got.view(np.uint32), want.view(np.uint32))), layer.last["R"],
+               layer.last["send_counts"], layer.last["recv_counts"]))
+    except Exception as exc:  # reported to the parent, which fails the test
+        q.put((rank, repr(exc), -1, None, None))
+    finally:
+        dist.destroy_process_group()
+
+
+def _run_world(world, T, E, H, k, skew=False):
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_ep_rank, args=(r, world, port, T, E, H, k, skew, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=300) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+    return sorted(res, key=lambda r: r[0])
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_ep_exchange_equals_one_process(world):
+    res = _run_world(world, T=7, E=16, H=64, k=3)
+    for rank, ok, R, send_c, recv_c in res:
+        assert ok is True, f"rank {rank}: {ok}"
+    # every row sent is received once: the count matrices transpose into each other
+    send = np.array([r[3] for r in res])
+    recv = np.array([r[4] for r in res])
+    assert np.array_equal(send.T, recv)
+    assert send.sum() == world * 7 * 3
+
+
+def test_ep_exchange_with_ranks_that_receive_nothing():
+    res = _run_world(4, T=5, E=16, H=64, k=2, skew=True)
+    for rank, ok, R, _, _ in res:
+        assert ok is True, f"rank {rank}: {ok}"
+    assert res[0][2] == 4 * 5 * 2 and all(r[2] == 0 for r in res[1:])
+
+
+def test_ep_refuses_an_expert_count_the_world_does_not_divide():
+    from exl3b200.ep import EpLayer
+    with pytest.raises(ValueError):
+        EpLayer(rank=0, world=3, n_expert=16, hidden=64, width=128, top_k=2, max_tokens=4, device="cpu",
+                ops=object())
+
+
+# ------------------------------------------------------------------------------------------ on the GPU
+def _lib():
+    from exl3b200 import load_plugin
+    from exl3b200.native import Native
+    return Native(load_plugin().path)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("T,k,world,n_local,H", [(1, 1, 2, 4, 64), (37, 4, 2, 8, 256), (600, 10, 8, 64, 2048),
+                                                 (1000, 10, 4, 16, 128)])
+def test_ep_pack_kernel(T, k, world, n_local, H):
+    nat, dev = _lib(), torch.device("cuda")
+    E, P = n_local * world, T * k
+    g = torch.Generator().manual_seed(T + H)
+    x = torch.randn((T, H), generator=g).to(torch.float16)
+    ids = torch.stack([torch.randperm(E, generator=g)[:k] for _ in range(T)]).to(torch.int32).reshape(-1)
+    orc = Oracle()
+    st, off = orc.scatter(ids.numpy(), E)
+    xd, idd = x.to(dev), ids.to(dev)
+    std, offd = torch.from_numpy(st).to(dev), torch.from_numpy(off).to(dev)
+    sx = torch.full((P, H), 7, dtype=torch.int16, device=dev)
+    se = torch.full((P,), -5, dtype=torch.int32, device=dev)
+    cnt = torch.zeros(world, dtype=torch.int32, device=dev)
+    nat.ep_pack(xd.data_ptr(), H, idd.data_ptr(), k, std.data_ptr(), P, offd.data_ptr(), n_local, world, H,
+                sx.data_ptr(), se.data_ptr(), cnt.data_ptr(), 0)
+    torch.cuda.synchronize()
+    want_x = x.view(torch.int16).numpy()[st // k]
+    assert np.array_equal(sx.cpu().numpy(), want_x)
+    assert np.array_equal(se.cpu().numpy(), ids.numpy()[st] % n_local)
+    assert cnt.cpu().tolist() == [int(off[(r + 1) * n_local] - off[r * n_local]) for r in range(world)]
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("n,row_bytes,n_dst", [(1, 16, 1), (333, 4096, 333), (2048, 1024, 3000)])
+def test_rows_scatter_kernel(n, row_bytes, n_dst):
+    nat, dev = _lib(), torch.device("cuda")
+    g = torch.Generator().manual_seed(n)
+    src = torch.randint(-30000, 30000, (n, row_bytes // 2), generator=g, dtype=torch.int16)
+    idx = torch.randperm(n_dst, generator=g)[:n].to(torch.int32)
+    idx[::7] = -1                  # skipped
+    dst = torch.full((n_dst, row_bytes // 2), 3, dtype=torch.int16)
+    want = dst.clone()
+    for j in range(n):
+        if idx[j] >= 0:
+            want[idx[j]] = src[j]
+    s, i, d = src.to(dev), idx.to(dev), dst.to(dev)
+    nat.rows_scatter(s.data_ptr(), row_bytes, i.data_ptr(), n, row_bytes, d.data_ptr(), row_bytes, n_dst, 0)
+    torch.cuda.synchronize()
+    assert torch.equal(d.cpu(), want)
+
+
+def _ep_gpu_rank(rank, world, port, q):
+    import datetime
+
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"], os.environ["MASTER_PORT"] = "127.0.0.1", str(port)
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=dev)
+    try:
+        from exl3b200 import load_plugin
+        from exl3b200.ep import EpLayer
+        from exl3b200.layer import MoeLayer
+        plugin = load_plugin()
+        E, H, W, k = 64, 2048, 512, 8
+        res = []
+        for T in (3, 256):
+            full = MoeLayer(plugin, n_expert=E, hidden=H, width=W, top_k=k, bits_gu=3, bits_dn=4, max_tokens=T,
+                            seed=7, device=dev)
+            ep = EpLayer(plugin, rank=rank, world=world, n_expert=E, hidden=H, width=W, top_k=k, bits_gu=3,
+                         bits_dn=4, max_tokens=T, seed=7, device=dev, full=full)
+            g = torch.Generator(device=dev)
+            g.manual_seed(50 + rank + T)
+            x = torch.randn((T, H), generator=g, device=dev).to(torch.float16)
+            lg = torch.randn((T, E), generator=g, device=dev)
+            full.x[:T], full.logits[:T], ep.x[:T], ep.logits[:T] = x, lg, x, lg
+            s = torch.cuda.current_stream().cuda_stream
+            full.forward(T, s)
+            ep.forward(T, s)
+            ep.forward(T, s)
+            torch.cuda.synchronize()
+            a, b = full.out[:T].float(), ep.out[:T].float()
+            err = float((a - b).abs().max())
+            scale = float(a.abs().max())
+            cos = float(torch.nn.functional.cosine_similarity(a.reshape(1, -1), b.reshape(1, -1)))
+            res.append((T, bool(torch.equal(a, b)), err, scale, cos, full.band_name("down", T), ep.band_name("down", T)))
+        q.put((rank, res))
+    except Exception as exc:
+        q.put((rank, repr(exc)))
+    finally:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+@pytest.mark.gpu
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_ep_layer_over_nccl_equals_one_gpu():
+    """Two ranks, 32 experts each: the EP output equals the one-GPU layer's on the same tokens -- bit for bit where
+    both passes take the same band, within the ops' tolerance where the row counts put them in different bands."""
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_ep_gpu_rank, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=600) for _ in range(2)]
+    for p in procs:
+        p.join(timeout=120)
+    for rank, r in res:
+        assert isinstance(r, list), f"rank {rank}: {r}"
+        for T, same, err, scale, cos, band1, band2 in r:
+            if band1.split(":")[1].strip() == band2.split(":")[1].split("(")[0].strip():
+                assert same, f"rank {rank} T {T}: same band {band1}, max err {err}"
+            else:
+                assert err <= 1e-2 * scale and cos >= 0.9999, (rank, T, err, scale, cos, band1, band2)
