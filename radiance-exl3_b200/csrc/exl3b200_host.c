@@ -152,20 +152,29 @@ static int build_op(const RadArgs* a, int op, Exl3bGeom* g, Exl3bOp* k) {
 
 /* The band choice. The tensor-core path decodes each expert's weights once for up to 64 of its rows and pays its
  * input-rotation pass (the prep kernel into scratch) once per row; the decode-band path re-rotates per output block
- * and holds at most 64 rows in registers. The tensor-core path is taken when the live experts average at least
- * EXL3B_TC_MIN_ROWS rows, every class's output is a whole number of 256-row unit pairs, and its input rows can be
- * read by a 16-byte-aligned tensor map (else the decode-band path serves the launch, with the same result). */
+ * and holds at most 64 rows in registers, but splits K over clusters so that a few live experts still spread over
+ * the GPU. The tensor-core path is taken when the live experts average at least EXL3B_TC_MIN_ROWS rows, or when
+ * they make at least EXL3B_TC_MIN_UNITS of its units (live experts x 256-row output pairs), provided every class's
+ * output is a whole number of 256-row unit pairs and its input rows can be read by a 16-byte-aligned tensor map;
+ * otherwise the decode-band path serves the launch (the two agree within the ops' tolerance, not bit for bit:
+ * their f32 accumulations run in different orders). */
 #ifndef EXL3B_TC_MIN_ROWS
 #define EXL3B_TC_MIN_ROWS 16
+#endif
+#ifndef EXL3B_TC_MIN_UNITS
+#define EXL3B_TC_MIN_UNITS 64
 #endif
 static int tc_band(const Exl3bOp* k) {
     if (k->op == EXL3B_OP_PREP_GU || k->T <= 0) return 0;
     const int64_t live = k->n_expert < k->T ? k->n_expert : k->T;
-    if (live <= 0 || k->T / live < EXL3B_TC_MIN_ROWS) return 0;
+    if (live <= 0) return 0;
+    int64_t pairs = 0;
     for (int c = 0; c < k->n_class; ++c) {
         if (k->cls[c].cols % 64) return 0;
         if (k->op == EXL3B_OP_DOWN && k->cls[c].rows % 256) return 0;
+        if (k->cls[c].rows / 256 > pairs) pairs = k->cls[c].rows / 256;
     }
+    if (k->T / live < EXL3B_TC_MIN_ROWS && live * pairs < EXL3B_TC_MIN_UNITS) return 0;
     if ((k->n_expert + 1) * 4 > 16384) return 0;
     return 1;
 }

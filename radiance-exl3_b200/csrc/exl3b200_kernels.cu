@@ -58,49 +58,133 @@ __global__ void k_decode_what(const uint32_t* __restrict__ record, int64_t rows,
 }
 
 // ------------------------------------------------------------------------------------------ prep
-// One warp a sorted row, every 128-block of the class's input width. gate_up (moe_exl3_prep_gu, and the tensor-core
-// path's xr): the token row a[sorted_tok / top_k] rotated with suh into [0, C) and with suh.1 into [C, 2C) of row i;
-// rows outside the runs are not written; a row whose sorted_tok is negative is zero across 2C
-// (docs/OPS-exl3.md:128-142). down (h_rot 0 on the tensor-core path): row i of h rotated with suh into [0, C).
-__global__ void k_prep(const Exl3bOp op, uint16_t* __restrict__ dst_base, int64_t dst_pitch) {
-    const int lane = threadIdx.x & 31;
-    const bool gu = op.op != EXL3B_OP_DOWN;
-    const int64_t i = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;   // one warp a sorted row
-    if (i >= op.T) return;
-    const int64_t lo = op.expert_offset[0], hi = op.expert_offset[op.n_expert];
-    if (i < lo || i >= hi) return;
-    // the owner, once a row: largest e with off[e] <= i
-    int64_t a = 0, b = op.n_expert;
-    while (b - a > 1) {
-        const int64_t mid = (a + b) / 2;
-        if (op.expert_offset[mid] <= i) a = mid; else b = mid;
-    }
-    const ExpertView ev = expert_view(op, a);
-    uint16_t* y = dst_base + i * dst_pitch;
-    const int32_t tok = op.sorted_tok[i];
-    const int nhalf = gu ? 2 : 1;
-    if (tok < 0) {
-        for (int64_t c = 4 * lane; c < nhalf * ev.C; c += 128) {
+// A grid-stride pass over (sorted row, group of four 128-blocks) tasks, one warp a task and eight lanes a block, the
+// expert offsets staged once a CTA in shared memory (the owner of a row is a binary search there). gate_up
+// (moe_exl3_prep_gu, and the tensor-core path's xr): the token row a[sorted_tok / top_k] rotated with suh into
+// [0, C) and with suh.1 into [C, 2C) of row i; rows outside the runs are not written; a row whose sorted_tok is
+// negative is zero across 2C (docs/OPS-exl3.md:128-142). down (h_rot 0 on the tensor-core path): row i of h rotated
+// with suh into [0, C).
+//
+// A lane holds 16 consecutive values of its block (two 16-byte loads), so the butterfly stages h = 1, 2, 4, 8 run
+// in its registers and only h = 16, 32, 64 cross lanes (a shuffle within the block's 8 lanes). Every stage pairs
+// the same elements with the same f32 operations as the reference's loop (common/exl3_decode.c:172-189), so xr is
+// bit for bit the reference's.
+constexpr int kPrepWarps = 8;
+
+__device__ __forceinline__ void had128_x16(float v[16], int l8) {
 #pragma unroll
-            for (int q = 0; q < 4; ++q) y[c + q] = 0;
+    for (int h = 1; h < 16; h <<= 1)
+#pragma unroll
+        for (int i = 0; i < 16; ++i)
+            if (!(i & h)) {
+                const float a = v[i], b = v[i + h];
+                v[i] = __fadd_rn(a, b);
+                v[i + h] = __fsub_rn(a, b);
+            }
+#pragma unroll
+    for (int m = 1; m < 8; m <<= 1) {
+        const bool high = (l8 & m) != 0;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+            const float p = __shfl_xor_sync(0xFFFFFFFFu, v[i], m);
+            v[i] = high ? __fsub_rn(p, v[i]) : __fadd_rn(v[i], p);
         }
-        return;
     }
-    const int64_t src_row = gu ? (int64_t)(tok / op.top_k) : i;
-    const uint16_t* src = static_cast<const uint16_t*>(op.x) + src_row * op.x_pitch;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = __fmul_rn(v[i], kRs);
+}
+
+__device__ __forceinline__ void ld16(const uint16_t* p, bool vec, uint16_t h[16]) {
+    if (vec) {
+        const uint4 a = *reinterpret_cast<const uint4*>(p), b = *reinterpret_cast<const uint4*>(p + 8);
+        const uint32_t u[8] = { a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w };
+#pragma unroll
+        for (int q = 0; q < 8; ++q) { h[2 * q] = (uint16_t)u[q]; h[2 * q + 1] = (uint16_t)(u[q] >> 16); }
+    } else {
+#pragma unroll
+        for (int q = 0; q < 16; ++q) h[q] = p[q];
+    }
+}
+__device__ __forceinline__ void st16(uint16_t* p, bool vec, const uint16_t h[16]) {
+    if (vec) {
+        uint32_t u[8];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) u[q] = (uint32_t)h[2 * q] | ((uint32_t)h[2 * q + 1] << 16);
+        *reinterpret_cast<uint4*>(p) = make_uint4(u[0], u[1], u[2], u[3]);
+        *reinterpret_cast<uint4*>(p + 8) = make_uint4(u[4], u[5], u[6], u[7]);
+    } else {
+#pragma unroll
+        for (int q = 0; q < 16; ++q) p[q] = h[q];
+    }
+}
+__device__ __forceinline__ bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+__global__ void __launch_bounds__(kPrepWarps * 32) k_prep(const Exl3bOp op, uint16_t* __restrict__ dst_base,
+                                                           int64_t dst_pitch, int ngrp) {
+    extern __shared__ int32_t s_off[];                 // expert_offset [n_expert + 1]
+    for (int64_t e = threadIdx.x; e <= op.n_expert; e += blockDim.x) s_off[e] = op.expert_offset[e];
+    __syncthreads();
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    const int l8 = lane & 7, bq = lane >> 3;           // the lane's 16 values: block 4g + bq, elements 16 l8 ..
+    const bool gu = op.op != EXL3B_OP_DOWN;
+    const int64_t lo = s_off[0], hi = s_off[op.n_expert] < op.T ? s_off[op.n_expert] : op.T;
     const bool bf = gu && op.x_bf16;
-    const uint16_t* s0 = static_cast<const uint16_t*>(tab_entry(op.cls[ev.c].suh, ev.j));
-    const uint16_t* s1 = gu ? static_cast<const uint16_t*>(tab_entry(op.cls[ev.c].suh1, ev.j)) : s0;
-    for (int64_t blk = 0; blk * 128 < ev.C; ++blk) {
-        float x[4];
+    const bool xvec = al16(op.x) && (op.x_pitch % 8) == 0;
+    const bool yvec = al16(dst_base) && (dst_pitch % 8) == 0;
+    const int64_t n_task = (hi - lo) * ngrp;
+    for (int64_t task = (int64_t)blockIdx.x * kPrepWarps + w; task < n_task; task += (int64_t)gridDim.x * kPrepWarps) {
+        const int64_t i = lo + task / ngrp;
+        int64_t a = 0, b = op.n_expert;                // the owner: largest e with off[e] <= i
+        while (b - a > 1) {
+            const int64_t mid = (a + b) / 2;
+            if (s_off[mid] <= i) a = mid; else b = mid;
+        }
+        const ExpertView ev = expert_view(op, a);
+        const int64_t blk = (task % ngrp) * 4 + bq;
+        const bool mine = blk * 128 < ev.C;            // lanes past the class's width idle (shuffles stay whole)
+        const int64_t c = (mine ? blk : 0) * 128 + 16 * l8;
+        uint16_t* y = dst_base + i * dst_pitch;
+        const int32_t tok = op.sorted_tok[i];
+        if (tok < 0) {
+            uint16_t z[16];
 #pragma unroll
-        for (int q = 0; q < 4; ++q) x[q] = bf ? bf2f(src[blk * 128 + 4 * lane + q]) : h2f(src[blk * 128 + 4 * lane + q]);
-        for (int half = 0; half < nhalf; ++half) {
-            float v[4] = { x[0], x[1], x[2], x[3] };
-            prologue_warp(v, (half ? s1 : s0) + blk * 128, lane);
-            uint16_t* dst = y + half * ev.C + blk * 128 + 4 * lane;
+            for (int q = 0; q < 16; ++q) z[q] = 0;
+            if (mine) {
+                st16(y + c, yvec, z);
+                if (gu) st16(y + ev.C + c, yvec, z);
+            }
+            continue;
+        }
+        const int64_t src_row = gu ? (int64_t)(tok / op.top_k) : i;
+        const uint16_t* src = static_cast<const uint16_t*>(op.x) + src_row * op.x_pitch;
+        const uint16_t* s0 = static_cast<const uint16_t*>(tab_entry(op.cls[ev.c].suh, ev.j));
+        const uint16_t* s1 = gu ? static_cast<const uint16_t*>(tab_entry(op.cls[ev.c].suh1, ev.j)) : s0;
+        const bool svec = al16(s0) && al16(s1);
+        uint16_t hx[16], hs[16];
+        ld16(src + c, xvec, hx);
+        float xf[16], va[16], vb[16];
 #pragma unroll
-            for (int q = 0; q < 4; ++q) dst[q] = f2h(v[q]);
+        for (int q = 0; q < 16; ++q) xf[q] = bf ? bf2f(hx[q]) : h2f(hx[q]);
+        ld16(s0 + c, svec, hs);
+#pragma unroll
+        for (int q = 0; q < 16; ++q) va[q] = h2f(f2h(__fmul_rn(xf[q], h2f(hs[q]))));
+        if (gu) {
+            ld16(s1 + c, svec, hs);
+#pragma unroll
+            for (int q = 0; q < 16; ++q) vb[q] = h2f(f2h(__fmul_rn(xf[q], h2f(hs[q]))));
+        }
+        had128_x16(va, l8);
+        if (gu) had128_x16(vb, l8);
+        if (mine) {
+            uint16_t o[16];
+#pragma unroll
+            for (int q = 0; q < 16; ++q) o[q] = f2h(va[q]);
+            st16(y + c, yvec, o);
+            if (gu) {
+#pragma unroll
+                for (int q = 0; q < 16; ++q) o[q] = f2h(vb[q]);
+                st16(y + ev.C + c, yvec, o);
+            }
         }
     }
 }
@@ -528,12 +612,23 @@ int exl3b_cuda_decode_what(const void* record, int64_t rows, int64_t cols, int b
 }
 
 // The rotation pass into `dst` (row pitch `dst_pitch` elements): prep_gu's xr (gate_up ops) or down's rotated h.
+int exl3b_cuda_device_info(int* sm_count, int32_t** err_word);   // exl3b200_moe.cu
+
 int exl3b_cuda_prep(const Exl3bOp* op, void* dst, int64_t dst_pitch, void* stream) {
     if (op->T <= 0) return 0;
-    const int64_t tasks = op->T;
-    const int wpb = 8;
-    k_prep<<<(unsigned)((tasks + wpb - 1) / wpb), wpb * 32, 0, as_stream(stream)>>>(*op, static_cast<uint16_t*>(dst),
-                                                                                     dst_pitch);
+    int sm = 0;
+    int32_t* err = nullptr;
+    if (exl3b_cuda_device_info(&sm, &err) != 0) return -6;
+    int64_t cmax = 0;
+    for (int c = 0; c < op->n_class; ++c)
+        if (op->cls[c].cols > cmax) cmax = op->cls[c].cols;
+    const int ngrp = (int)((cmax / 128 + 3) / 4);     // tasks a row: groups of four 128-blocks
+    // enough warps to keep every SM's memory pipeline full (8 CTAs of 8 warps an SM), no more than the tasks
+    const int64_t want = (op->T * ngrp + kPrepWarps - 1) / kPrepWarps;
+    const int64_t cap = (int64_t)sm * 8;
+    const unsigned grid = (unsigned)(want < cap ? (want > 0 ? want : 1) : cap);
+    const size_t smem = (size_t)(op->n_expert + 1) * 4;
+    k_prep<<<grid, kPrepWarps * 32, smem, as_stream(stream)>>>(*op, static_cast<uint16_t*>(dst), dst_pitch, ngrp);
     return cudaGetLastError() == cudaSuccess ? 0 : -6;
 }
 

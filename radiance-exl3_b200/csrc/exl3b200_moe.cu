@@ -58,6 +58,85 @@ __global__ void k_router_topk(const float* __restrict__ logits, int64_t n_tok, i
     }
 }
 
+// The same router with the token's logits held in registers (RPL a lane, n_expert <= 32 * RPL): one read of the
+// row, then softmax and the top_k rounds on registers. Same reductions in the same order as k_router_topk.
+template <int RPL>
+__global__ void k_router_topk_reg(const float* __restrict__ logits, int64_t n_tok, int n_expert, int top_k,
+                                  int32_t* __restrict__ ids, float* __restrict__ w) {
+    const int lane = threadIdx.x & 31;
+    const int64_t t = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+    if (t >= n_tok) return;
+    const float* l = logits + t * n_expert;
+    float v[RPL];
+#pragma unroll
+    for (int q = 0; q < RPL; ++q) {
+        const int e = lane + 32 * q;
+        v[q] = e < n_expert ? l[e] : 0.f;
+    }
+    float mx = -INFINITY;
+#pragma unroll
+    for (int q = 0; q < RPL; ++q)
+        if (lane + 32 * q < n_expert) mx = fmaxf(mx, v[q]);
+    for (int m = 16; m; m >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, m));
+    float s = 0.f;
+#pragma unroll
+    for (int q = 0; q < RPL; ++q)
+        if (lane + 32 * q < n_expert) s += expf(v[q] - mx);
+    for (int m = 16; m; m >>= 1) s += __shfl_xor_sync(0xFFFFFFFFu, s, m);
+    uint32_t taken = 0;                     // bit q: expert lane + 32 q already chosen
+    for (int r = 0; r < top_k; ++r) {
+        float best = -INFINITY;
+        int bid = 0x7FFFFFFF;
+#pragma unroll
+        for (int q = 0; q < RPL; ++q) {
+            const int e = lane + 32 * q;
+            if (e >= n_expert || ((taken >> q) & 1u)) continue;
+            if (v[q] > best || (v[q] == best && e < bid)) { best = v[q]; bid = e; }
+        }
+        for (int m = 16; m; m >>= 1) {
+            const float ov = __shfl_xor_sync(0xFFFFFFFFu, best, m);
+            const int oid = __shfl_xor_sync(0xFFFFFFFFu, bid, m);
+            if (ov > best || (ov == best && oid < bid)) { best = ov; bid = oid; }
+        }
+        if (bid != 0x7FFFFFFF && (bid & 31) == lane) taken |= 1u << (bid >> 5);
+        if (lane == 0) {
+            ids[t * top_k + r] = bid == 0x7FFFFFFF ? -1 : bid;
+            w[t * top_k + r] = bid == 0x7FFFFFFF ? 0.f : expf(best - mx) / s;
+        }
+    }
+}
+
+// Exclusive scan of cnt[0 .. n) in place (block-wide: each thread a run, warp shuffles, warp totals); returns the
+// total to every thread. `wtot` holds blockDim.x / 32 ints.
+__device__ int block_scan_excl(int* cnt, int n, int* wtot) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
+    const int per = (n + blockDim.x - 1) / blockDim.x;
+    const int e0 = tid * per, e1 = e0 + per < n ? e0 + per : n;
+    int sum = 0;
+    for (int e = e0; e < e1; ++e) sum += cnt[e];
+    int incl = sum;
+    for (int d = 1; d < 32; d <<= 1) {
+        const int v = __shfl_up_sync(0xFFFFFFFFu, incl, d);
+        if (lane >= d) incl += v;
+    }
+    if (lane == 31) wtot[warp] = incl;
+    __syncthreads();
+    int base = 0, total = 0;
+    for (int w = 0; w < nw; ++w) {
+        const int v = wtot[w];
+        if (w < warp) base += v;
+        total += v;
+    }
+    int acc = base + incl - sum;
+    for (int e = e0; e < e1; ++e) {
+        const int v = cnt[e];
+        cnt[e] = acc;
+        acc += v;
+    }
+    __syncthreads();
+    return total;
+}
+
 // ------------------------------------------------------------------------------------------ scatter
 __device__ __forceinline__ int local_expert(int32_t id, int64_t base, int n_expert) {
     const int64_t e = (int64_t)id - base;
@@ -97,19 +176,10 @@ __global__ void k_scatter_small(const int32_t* __restrict__ ids, int64_t n_pairs
         if (e >= 0) atomicAdd(&cnt[e], 1);
     }
     __syncthreads();
-    if (tid == 0) {
-        int acc = 0;
-        for (int e = 0; e < n_expert; ++e) {
-            const int v = cnt[e];
-            cnt[e] = acc;
-            off[e] = acc;
-            acc += v;
-        }
-        off[n_expert] = acc;
-        cnt[n_expert] = acc;
-    }
-    __syncthreads();
-    const int live = cnt[n_expert];
+    __shared__ int wtot[32];
+    const int live = block_scan_excl(cnt, n_expert, wtot);
+    for (int e = tid; e < n_expert; e += blockDim.x) off[e] = cnt[e];
+    if (tid == 0) off[n_expert] = live;
     for (int64_t f = live + tid; f < n_pairs; f += blockDim.x) sorted_tok[f] = -1;
     for (int64_t c0 = 0; c0 < n_pairs; c0 += blockDim.x) place_chunk(ids, c0, n_pairs, base, n_expert, cnt, sorted_tok);
 }
@@ -144,17 +214,10 @@ __global__ void k_scatter_scan(int32_t* __restrict__ hist, int nb, int n_expert,
         sm[e] = acc;
     }
     __syncthreads();
-    if (tid == 0) {
-        int acc = 0;
-        for (int e = 0; e < n_expert; ++e) {
-            const int v = sm[e];
-            sm[e] = acc;
-            off[e] = acc;
-            acc += v;
-        }
-        off[n_expert] = acc;
-    }
-    __syncthreads();
+    __shared__ int wtot[32];
+    const int live = block_scan_excl(sm, n_expert, wtot);
+    for (int e = tid; e < n_expert; e += blockDim.x) off[e] = sm[e];
+    if (tid == 0) off[n_expert] = live;
     for (int e = tid; e < n_expert; e += blockDim.x)
         for (int b = 0; b < nb; ++b) hist[(int64_t)b * n_expert + e] += sm[e];
 }
@@ -203,6 +266,48 @@ __global__ void k_gather(const uint16_t* __restrict__ rows, int64_t pitch, const
     }
 }
 
+// One block a token, a thread 8 columns (16-byte loads of bf16 rows); each slot's row is loaded before any is
+// summed, then the slots are summed in ascending order exactly as k_gather does. rows 16-byte aligned with a pitch
+// of a multiple of 8 elements, width a multiple of 8, y 16-byte aligned (the host checks).
+constexpr int kGatherSlots = 16;
+__global__ void k_gather_v8(const uint16_t* __restrict__ rows, int64_t pitch, const int32_t* __restrict__ pos,
+                            const float* __restrict__ w, int top_k, int64_t width, float* __restrict__ y) {
+    const int64_t t = blockIdx.x;
+    for (int64_t n = 8 * (int64_t)threadIdx.x; n < width; n += 8 * (int64_t)blockDim.x) {
+        float acc[8] = { 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f };
+        for (int s0 = 0; s0 < top_k; s0 += kGatherSlots) {
+            uint4 r[kGatherSlots];
+            float ws[kGatherSlots];
+            bool live[kGatherSlots];
+#pragma unroll
+            for (int q = 0; q < kGatherSlots; ++q) {
+                live[q] = false;
+                if (s0 + q >= top_k) continue;
+                const int32_t i = pos[t * top_k + s0 + q];
+                if (i < 0) continue;
+                live[q] = true;
+                ws[q] = w[t * top_k + s0 + q];
+                r[q] = *reinterpret_cast<const uint4*>(rows + (int64_t)i * pitch + n);
+            }
+#pragma unroll
+            for (int q = 0; q < kGatherSlots; ++q) {
+                if (!live[q]) continue;
+                const uint32_t u[4] = { r[q].x, r[q].y, r[q].z, r[q].w };
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    const uint16_t b = (uint16_t)(u[j >> 1] >> (16 * (j & 1)));
+                    acc[j] = __fadd_rn(acc[j], __fmul_rn(ws[q], __bfloat162float(__ushort_as_bfloat16(b))));
+                }
+            }
+        }
+        float4* o = reinterpret_cast<float4*>(y + t * width + n);
+        o[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+        o[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+    }
+}
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
 }  // namespace
 
 extern "C" {
@@ -246,8 +351,16 @@ int exl3b200_router_topk(const float* logits, int64_t n_tok, int64_t n_expert, i
         return -12;
     if (n_tok == 0) return 0;
     const int wpb = 8;
-    k_router_topk<<<(unsigned)((n_tok + wpb - 1) / wpb), wpb * 32, 0, as_stream(stream)>>>(
-        logits, n_tok, (int)n_expert, (int)top_k, ids, w);
+    const unsigned grid = (unsigned)((n_tok + wpb - 1) / wpb);
+    cudaStream_t st = as_stream(stream);
+    if (n_expert <= 256)
+        k_router_topk_reg<8><<<grid, wpb * 32, 0, st>>>(logits, n_tok, (int)n_expert, (int)top_k, ids, w);
+    else if (n_expert <= 512)
+        k_router_topk_reg<16><<<grid, wpb * 32, 0, st>>>(logits, n_tok, (int)n_expert, (int)top_k, ids, w);
+    else if (n_expert <= 1024)
+        k_router_topk_reg<32><<<grid, wpb * 32, 0, st>>>(logits, n_tok, (int)n_expert, (int)top_k, ids, w);
+    else
+        k_router_topk<<<grid, wpb * 32, 0, st>>>(logits, n_tok, (int)n_expert, (int)top_k, ids, w);
     return cudaGetLastError() == cudaSuccess ? 0 : -6;
 }
 
@@ -287,7 +400,10 @@ int exl3b200_moe_gather(const uint16_t* rows, int64_t row_pitch, const int32_t* 
     if (cudaMemsetAsync(pos, 0xFF, (size_t)(n_tok * top_k) * 4, st) != cudaSuccess) return -6;
     if (n_rows > 0)
         k_invert<<<(unsigned)((n_rows + 255) / 256), 256, 0, st>>>(sorted_tok, n_rows, n_tok * top_k, pos);
-    k_gather<<<(unsigned)n_tok, 256, 0, st>>>(rows, row_pitch, pos, w, (int)top_k, width, y);
+    if (aligned16(rows) && row_pitch % 8 == 0 && width % 8 == 0 && aligned16(y))
+        k_gather_v8<<<(unsigned)n_tok, 256, 0, st>>>(rows, row_pitch, pos, w, (int)top_k, width, y);
+    else
+        k_gather<<<(unsigned)n_tok, 256, 0, st>>>(rows, row_pitch, pos, w, (int)top_k, width, y);
     return cudaGetLastError() == cudaSuccess ? 0 : -6;
 }
 
@@ -320,7 +436,10 @@ int exl3b200_moe_gather_noalloc(const uint16_t* rows, int64_t row_pitch, const i
     if (cudaMemsetAsync(pos, 0xFF, (size_t)(n_tok * top_k) * 4, st) != cudaSuccess) return -6;
     if (n_rows > 0)
         k_invert<<<(unsigned)((n_rows + 255) / 256), 256, 0, st>>>(sorted_tok, n_rows, n_tok * top_k, pos);
-    k_gather<<<(unsigned)n_tok, 256, 0, st>>>(rows, row_pitch, pos, w, (int)top_k, width, y);
+    if (aligned16(rows) && row_pitch % 8 == 0 && width % 8 == 0 && aligned16(y))
+        k_gather_v8<<<(unsigned)n_tok, 256, 0, st>>>(rows, row_pitch, pos, w, (int)top_k, width, y);
+    else
+        k_gather<<<(unsigned)n_tok, 256, 0, st>>>(rows, row_pitch, pos, w, (int)top_k, width, y);
     return cudaGetLastError() == cudaSuccess ? 0 : -6;
 }
 

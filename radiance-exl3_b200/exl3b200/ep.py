@@ -82,8 +82,7 @@ class DeviceOps:
     def kernels(self, T, k, E, R):
         """How many of the library's kernels one step launches (ep_pack and rows_scatter counted)."""
         P = T * k
-        live = max(1, min(self.local.n_local, R))
-        tc = R > 0 and R // live >= 16
+        tc = R > 0 and self.local._tc("gate_up", R)
         n = 1 + (1 if P <= 8192 else 3) + 1 + (1 if R <= 8192 else 3)
         n += (2 + (1 if tc else 0)) if R > 0 else 0
         n += 1 if R > 0 else 0
@@ -166,6 +165,11 @@ class EpLayer:
 
     def expert_bytes(self):
         return self.ops.local.expert_bytes()
+
+    def time_prep_step(self, T, n=5):
+        """The local pass's gate_up input rotation alone (ms), over the rows the last step received."""
+        R = self.last["R"]
+        return self.ops.local.time_prep(R, R, x_ptr=self.recv_x.data_ptr(), top_k=1, n=n)
 
     def expert_flops(self, rows):
         return self.ops.local.expert_flops(rows)

@@ -183,21 +183,65 @@ class MoeLayer:
         if events:
             events[2].record()
 
-    def band_name(self, op, T):
-        """Which kernels serve one op at T tokens: the library's band rule (live experts averaging >= 16 rows take
-        the tensor-core band; gate_up's input rotation then runs once a row in k_prep)."""
-        rows = T * self.k
+    def time_prep(self, T, rows, x_ptr=None, top_k=None, n=5):
+        """Mean device time (ms, CUDA events on the current stream) of the gate_up input rotation alone: the
+        moe_exl3_prep_gu row over the same sorted rows, i.e. the k_prep launch the tensor-core gate_up runs first.
+        The bench subtracts it from the gate_up op to time k_gemm_tc by itself."""
+        torch = self.torch
+        if rows == 0:
+            return 0.0
+        k = top_k or self.k
+        if getattr(self, "_xr", None) is None or self._xr.shape[0] < rows:
+            self._xr = torch.empty((rows, 2 * self.H), dtype=torch.float16, device=self.dev)
+        absent = rad.RadTensor()
+        E, H = self.n_local, self.H
+        P, nP, kp = rad.make_params({"M": T, "K": H, "n_expert": E, "top_k": k, "dtype": f"exl3k{self.bits_gu}"})
+        ts = [rad.tensor(x_ptr or self.x.data_ptr(), rad.DT["f16"], [T, H]),
+              rad.tensor(self.suh.data_ptr(), rad.DT["f16"], [E, 1, H]),
+              rad.tensor(self.suh1.data_ptr(), rad.DT["f16"], [E, 1, H]),
+              rad.tensor(self.sorted_tok.data_ptr(), rad.DT["i32"], [rows]),
+              rad.tensor(self.offset.data_ptr(), rad.DT["i32"], [E + 1]),
+              absent, absent,
+              rad.tensor(self._xr.data_ptr(), rad.DT["f16"], [rows, 2 * H])]
+        arr = (rad.RadTensor * len(ts))(*ts)
+        a = rad.RadArgs()
+        a.t, a.n_t, a.p, a.n_p, a.world_size = arr, len(ts), P, nP, 1
+        row = self.plugin.row("moe_exl3_prep_gu")
+        stream = torch.cuda.current_stream().cuda_stream
+        for _ in range(2):
+            if row.launch(C.byref(a), stream) != 0:
+                raise RuntimeError("moe_exl3_prep_gu launch failed")
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(n):
+            row.launch(C.byref(a), stream)
+        e1.record()
+        torch.cuda.synchronize()
+        del kp
+        return e0.elapsed_time(e1) / n
+
+    def _tc(self, op, rows):
+        """The library's band rule (exl3b200_host.c tc_band): the tensor-core band once the live experts average 16
+        rows or make 64 units (live experts x 256-row output pairs)."""
         live = min(self.n_local, rows)
-        tc = live > 0 and rows // live >= 16
+        if live <= 0:
+            return False
+        pairs = (2 * self.W if op == "gate_up" else self.H) // 256
+        return rows // live >= 16 or live * pairs >= 64
+
+    def band_name(self, op, T):
+        """Which kernels serve one op at T tokens (gate_up's input rotation runs once a row in k_prep on the
+        tensor-core band)."""
+        tc = self._tc(op, T * self.k)
         if op == "gate_up":
             return "moe_exl3_gate_up row: k_prep + k_gemm_tc" if tc else "moe_exl3_gate_up row: k_gemm_skinny"
         return "moe_exl3_down row: k_gemm_tc" if tc else "moe_exl3_down row: k_gemm_skinny"
 
     def launches_per_step(self, T):
-        """Kernels of this library one forward launches: router, scatter (1 small / 3 large), gate_up, down,
-        the gather's inverse map and the gather."""
-        tc = T * self.k // max(1, min(self.n_local, T * self.k)) >= 16
-        return 1 + (1 if T * self.k <= 8192 else 3) + 2 + 2 + (1 if tc else 0)
+        """Kernels of this library one forward launches: router, scatter (1 small / 3 large), gate_up (+ prep on the
+        tensor-core band), down, the gather's inverse map and the gather."""
+        rows = T * self.k
+        return 1 + (1 if rows <= 8192 else 3) + 2 + 2 + (1 if self._tc("gate_up", rows) else 0)
 
     def forward(self, T, stream, events=None):
         """The whole layer over the first T tokens of self.x / self.logits into self.out (f32 [T, H])."""
@@ -210,6 +254,9 @@ class MoeLayer:
                        self.H, self.out.data_ptr(), self.gather_work.data_ptr(), stream)
 
     # ------------------------------------------------------------------ accounting
+    def time_prep_step(self, T, n=5):
+        return self.time_prep(T, T * self.k, n=n)
+
     def expert_bytes(self):
         """Algorithmic bytes of one expert: both records plus every scale vector the pass reads."""
         H, W = self.H, self.W

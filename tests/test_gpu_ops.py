@@ -102,11 +102,14 @@ OPS = [
          bits=6, codebook="mul1"),
     dict(op="moe_exl3_gate_up_mod4", M=4, top_k=2, n_expert=6,
          geom=[(256, 128), (512, 128), (256, 256), (256, 128)], bits=7, codebook="mcg", h_rot=1),
+    dict(op="moe_exl3_down", M=2, top_k=2, n_expert=3, geom=[(256, 128)], bits=8, codebook="3inst"),
+    # the decode band at the config's shapes (fewer than 64 units: live experts x 256-row output pairs)
+    dict(op="moe_exl3_gate_up", M=1, top_k=10, n_expert=64, geom=[(1024, 2048)], bits=3, codebook="mul1"),
+    dict(op="moe_exl3_down", M=1, top_k=4, n_expert=64, geom=[(2048, 512)], bits=4, codebook="mul1", h_rot=1),
+    # the tensor-core band (live experts averaging >= 16 rows, or at least 64 units)
     dict(op="moe_exl3_down", M=8, top_k=10, n_expert=64, geom=[(2048, 512)], bits=4, codebook="mul1",
          table_form="stacked"),
     dict(op="moe_exl3_gate_up", M=8, top_k=10, n_expert=64, geom=[(1024, 2048)], bits=3, codebook="mul1"),
-    dict(op="moe_exl3_down", M=2, top_k=2, n_expert=3, geom=[(256, 128)], bits=8, codebook="3inst"),
-    # the tensor-core band (live experts averaging >= 16 rows)
     dict(op="moe_exl3_down", M=100, top_k=2, n_expert=4, geom=[(512, 256)], bits=4, codebook="mul1", h_rot=1),
     dict(op="moe_exl3_gate_up", M=64, top_k=2, n_expert=4, geom=[(512, 256), (256, 128)], bits=2, codebook="3inst",
          drop=0.1),
