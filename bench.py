@@ -221,11 +221,16 @@ def bench_ours(args, rank, world, local_rank):
     torch.cuda.synchronize()
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
     kev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    pev = ([[torch.cuda.Event(enable_timing=True) for _ in range(len(layer.PHASES) + 1)] for _ in range(args.steps)]
+           if world > 1 else None)
     barrier()
     wall0 = time.perf_counter()
     ev[0].record(stream)
     for s in range(args.steps):
-        layer.forward(T, sh, events=kev[s])
+        if world > 1:
+            layer.forward(T, sh, events=kev[s], phases=pev[s])
+        else:
+            layer.forward(T, sh, events=kev[s])
     ev[1].record(stream)
     barrier()
     wall = time.perf_counter() - wall0
@@ -233,10 +238,16 @@ def bench_ours(args, rank, world, local_rank):
     ms = ev[0].elapsed_time(ev[1]) / args.steps
     gu_ms = float(np.mean([k[0].elapsed_time(k[1]) for k in kev]))
     dn_ms = float(np.mean([k[1].elapsed_time(k[2]) for k in kev]))
+    ep_phases = None
     if world > 1:
         t = torch.tensor([ms, gu_ms, dn_ms], device=dev)
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
         ms, gu_ms, dn_ms = (float(v) for v in t.cpu())
+        ph = torch.tensor([float(np.mean([p[i].elapsed_time(p[i + 1]) for p in pev]))
+                           for i in range(len(layer.PHASES))], device=dev)
+        torch.distributed.all_reduce(ph, op=torch.distributed.ReduceOp.MAX)
+        ep_phases = {n: round(float(v), 4) for n, v in zip(layer.PHASES, ph.cpu())}
+        ep_phases["exchange_bytes_rank0"] = layer.exchange_bytes()
     live = layer.live_experts()
     gu_b, dn_b = layer.expert_bytes()
     tokens_total = T * world
@@ -372,6 +383,7 @@ def bench_ours(args, rank, world, local_rank):
                                "down_op_ms": round(dn_ms, 4)}},
         "clocks": clk, "gpu_launches": int(launches_per_step * args.steps),
         "e2e": e2e, "cpu_baseline": cpu, "sweep": sweep, "wall_s": round(wall, 3),
+        "ep_phases_ms": ep_phases,
     }
     return line
 

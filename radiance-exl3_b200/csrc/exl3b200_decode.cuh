@@ -159,13 +159,15 @@ __device__ __forceinline__ void had128_warp(float v[4], int lane) {
     a = v[2]; b = v[3]; v[2] = __fadd_rn(a, b); v[3] = __fsub_rn(a, b);
     a = v[0]; b = v[2]; v[0] = __fadd_rn(a, b); v[2] = __fsub_rn(a, b);
     a = v[1]; b = v[3]; v[1] = __fadd_rn(a, b); v[3] = __fsub_rn(a, b);
+    // across lanes: the low lane of a pair keeps a + b, the high lane a - b, written as one FMA p + (+-1) v (the
+    // product by +-1 is exact, so the FMA rounds exactly as the add or the subtract would)
 #pragma unroll
     for (int m = 1; m < 32; m <<= 1) {
-        const bool high = (lane & m) != 0;
+        const float sg = (lane & m) ? -1.0f : 1.0f;
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
             const float p = __shfl_xor_sync(0xFFFFFFFFu, v[i], m);
-            v[i] = high ? __fsub_rn(p, v[i]) : __fadd_rn(v[i], p);
+            v[i] = __fmaf_rn(sg, v[i], p);
         }
     }
 #pragma unroll

@@ -83,38 +83,57 @@ __device__ __forceinline__ void had128_x16(float v[16], int l8) {
             }
 #pragma unroll
     for (int m = 1; m < 8; m <<= 1) {
-        const bool high = (l8 & m) != 0;
+        const float sg = (l8 & m) ? -1.0f : 1.0f;       // p + (+-1) v: exact product, one rounding
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
             const float p = __shfl_xor_sync(0xFFFFFFFFu, v[i], m);
-            v[i] = high ? __fsub_rn(p, v[i]) : __fadd_rn(v[i], p);
+            v[i] = __fmaf_rn(sg, v[i], p);
         }
     }
 #pragma unroll
     for (int i = 0; i < 16; ++i) v[i] = __fmul_rn(v[i], kRs);
 }
 
-__device__ __forceinline__ void ld16(const uint16_t* p, bool vec, uint16_t h[16]) {
+// 16 consecutive 16-bit values as 8 packed pairs (low half = the lower index)
+__device__ __forceinline__ void ld16(const uint16_t* p, bool vec, uint32_t u[8]) {
     if (vec) {
         const uint4 a = *reinterpret_cast<const uint4*>(p), b = *reinterpret_cast<const uint4*>(p + 8);
-        const uint32_t u[8] = { a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w };
-#pragma unroll
-        for (int q = 0; q < 8; ++q) { h[2 * q] = (uint16_t)u[q]; h[2 * q + 1] = (uint16_t)(u[q] >> 16); }
+        u[0] = a.x; u[1] = a.y; u[2] = a.z; u[3] = a.w; u[4] = b.x; u[5] = b.y; u[6] = b.z; u[7] = b.w;
     } else {
 #pragma unroll
-        for (int q = 0; q < 16; ++q) h[q] = p[q];
+        for (int q = 0; q < 8; ++q) u[q] = (uint32_t)p[2 * q] | ((uint32_t)p[2 * q + 1] << 16);
     }
 }
-__device__ __forceinline__ void st16(uint16_t* p, bool vec, const uint16_t h[16]) {
-    if (vec) {
-        uint32_t u[8];
+// v = f32(f16(x * s)) for 16 values: the product rounded once to f16, as the reference's f16(f32 x * f32 s) (the
+// product of two f16 values is exact in f32). f16 x: one HMUL2 a pair; bf16 x: in f32, then rounded.
+__device__ __forceinline__ void scale16(const uint32_t x[8], const uint32_t s[8], bool bf, float v[16]) {
 #pragma unroll
-        for (int q = 0; q < 8; ++q) u[q] = (uint32_t)h[2 * q] | ((uint32_t)h[2 * q + 1] << 16);
+    for (int q = 0; q < 8; ++q) {
+        if (!bf) {
+            const __half2 r = __hmul2(*reinterpret_cast<const __half2*>(&x[q]), *reinterpret_cast<const __half2*>(&s[q]));
+            const float2 f = __half22float2(r);
+            v[2 * q] = f.x;
+            v[2 * q + 1] = f.y;
+        } else {
+            v[2 * q] = h2f(f2h(__fmul_rn(bf2f((uint16_t)x[q]), h2f((uint16_t)s[q]))));
+            v[2 * q + 1] = h2f(f2h(__fmul_rn(bf2f((uint16_t)(x[q] >> 16)), h2f((uint16_t)(s[q] >> 16)))));
+        }
+    }
+}
+// 16 f32 values rounded to f16 and stored (8 packed pairs)
+__device__ __forceinline__ void st16f(uint16_t* p, bool vec, const float v[16]) {
+    uint32_t u[8];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+        const __half2 h = __floats2half2_rn(v[2 * q], v[2 * q + 1]);
+        u[q] = *reinterpret_cast<const uint32_t*>(&h);
+    }
+    if (vec) {
         *reinterpret_cast<uint4*>(p) = make_uint4(u[0], u[1], u[2], u[3]);
         *reinterpret_cast<uint4*>(p + 8) = make_uint4(u[4], u[5], u[6], u[7]);
     } else {
 #pragma unroll
-        for (int q = 0; q < 16; ++q) p[q] = h[q];
+        for (int q = 0; q < 8; ++q) { p[2 * q] = (uint16_t)u[q]; p[2 * q + 1] = (uint16_t)(u[q] >> 16); }
     }
 }
 __device__ __forceinline__ bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
@@ -131,27 +150,28 @@ __global__ void __launch_bounds__(kPrepWarps * 32) k_prep(const Exl3bOp op, uint
     const bool bf = gu && op.x_bf16;
     const bool xvec = al16(op.x) && (op.x_pitch % 8) == 0;
     const bool yvec = al16(dst_base) && (dst_pitch % 8) == 0;
-    const int64_t n_task = (hi - lo) * ngrp;
-    for (int64_t task = (int64_t)blockIdx.x * kPrepWarps + w; task < n_task; task += (int64_t)gridDim.x * kPrepWarps) {
-        const int64_t i = lo + task / ngrp;
-        int64_t a = 0, b = op.n_expert;                // the owner: largest e with off[e] <= i
+    const uint32_t n_task = (uint32_t)((hi - lo) * ngrp);      // < 2^31 (the host checks)
+    for (uint32_t task = blockIdx.x * kPrepWarps + w; task < n_task; task += gridDim.x * kPrepWarps) {
+        const uint32_t rr = task / (uint32_t)ngrp;
+        const int64_t i = lo + rr;
+        int a = 0, b = (int)op.n_expert;               // the owner: largest e with off[e] <= i
         while (b - a > 1) {
-            const int64_t mid = (a + b) / 2;
+            const int mid = (a + b) >> 1;
             if (s_off[mid] <= i) a = mid; else b = mid;
         }
         const ExpertView ev = expert_view(op, a);
-        const int64_t blk = (task % ngrp) * 4 + bq;
+        const int64_t blk = (int64_t)(task - rr * (uint32_t)ngrp) * 4 + bq;
         const bool mine = blk * 128 < ev.C;            // lanes past the class's width idle (shuffles stay whole)
         const int64_t c = (mine ? blk : 0) * 128 + 16 * l8;
         uint16_t* y = dst_base + i * dst_pitch;
         const int32_t tok = op.sorted_tok[i];
         if (tok < 0) {
-            uint16_t z[16];
+            float z[16];
 #pragma unroll
-            for (int q = 0; q < 16; ++q) z[q] = 0;
+            for (int q = 0; q < 16; ++q) z[q] = 0.f;
             if (mine) {
-                st16(y + c, yvec, z);
-                if (gu) st16(y + ev.C + c, yvec, z);
+                st16f(y + c, yvec, z);
+                if (gu) st16f(y + ev.C + c, yvec, z);
             }
             continue;
         }
@@ -160,31 +180,20 @@ __global__ void __launch_bounds__(kPrepWarps * 32) k_prep(const Exl3bOp op, uint
         const uint16_t* s0 = static_cast<const uint16_t*>(tab_entry(op.cls[ev.c].suh, ev.j));
         const uint16_t* s1 = gu ? static_cast<const uint16_t*>(tab_entry(op.cls[ev.c].suh1, ev.j)) : s0;
         const bool svec = al16(s0) && al16(s1);
-        uint16_t hx[16], hs[16];
+        uint32_t hx[8], hs[8];
+        float va[16], vb[16];
         ld16(src + c, xvec, hx);
-        float xf[16], va[16], vb[16];
-#pragma unroll
-        for (int q = 0; q < 16; ++q) xf[q] = bf ? bf2f(hx[q]) : h2f(hx[q]);
         ld16(s0 + c, svec, hs);
-#pragma unroll
-        for (int q = 0; q < 16; ++q) va[q] = h2f(f2h(__fmul_rn(xf[q], h2f(hs[q]))));
+        scale16(hx, hs, bf, va);
         if (gu) {
             ld16(s1 + c, svec, hs);
-#pragma unroll
-            for (int q = 0; q < 16; ++q) vb[q] = h2f(f2h(__fmul_rn(xf[q], h2f(hs[q]))));
+            scale16(hx, hs, bf, vb);
         }
         had128_x16(va, l8);
         if (gu) had128_x16(vb, l8);
         if (mine) {
-            uint16_t o[16];
-#pragma unroll
-            for (int q = 0; q < 16; ++q) o[q] = f2h(va[q]);
-            st16(y + c, yvec, o);
-            if (gu) {
-#pragma unroll
-                for (int q = 0; q < 16; ++q) o[q] = f2h(vb[q]);
-                st16(y + ev.C + c, yvec, o);
-            }
+            st16f(y + c, yvec, va);
+            if (gu) st16f(y + ev.C + c, yvec, vb);
         }
     }
 }
@@ -623,6 +632,7 @@ int exl3b_cuda_prep(const Exl3bOp* op, void* dst, int64_t dst_pitch, void* strea
     for (int c = 0; c < op->n_class; ++c)
         if (op->cls[c].cols > cmax) cmax = op->cls[c].cols;
     const int ngrp = (int)((cmax / 128 + 3) / 4);     // tasks a row: groups of four 128-blocks
+    if (op->T * ngrp >= ((int64_t)1 << 31)) return -1;
     // enough warps to keep every SM's memory pipeline full (8 CTAs of 8 warps an SM), no more than the tasks
     const int64_t want = (op->T * ngrp + kPrepWarps - 1) / kPrepWarps;
     const int64_t cap = (int64_t)sm * 8;

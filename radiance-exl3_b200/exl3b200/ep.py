@@ -135,27 +135,38 @@ class EpLayer:
             out, inp = out.view(t.float16), inp.view(t.float16)
         self.dist.all_to_all_single(out, inp, out_splits, in_splits, group=self.group)
 
-    def forward(self, T, stream=None, events=None):
+    PHASES = ("route+pack", "counts+dispatch", "local sort", "experts", "combine", "gather")
+
+    def forward(self, T, stream=None, events=None, phases=None):
         """The layer over the first T tokens of self.x / self.logits into self.out[:T]. `stream` must be torch's
-        current stream (the collectives run there); `events` as MoeLayer.experts."""
+        current stream (the collectives run there); `events` as MoeLayer.experts; `phases`: len(PHASES) + 1 CUDA
+        events recorded between the steps (for a per-phase breakdown)."""
         if T > self.max_tokens:
             raise ValueError(f"T {T} > max_tokens {self.max_tokens}")
         o, G, k, P = self.ops, self.G, self.k, T * self.k
+        mark = (lambda i: phases[i].record()) if phases else (lambda i: None)
+        mark(0)
         o.router(self.logits, T, self.E, k, self.ids, self.w)
         o.scatter(self.ids, P, self.E, self.sorted_pairs[:P], self.offset)
         o.pack(self.x, self.ids, k, self.sorted_pairs, P, self.offset, self.nl, G, self.send_x, self.send_e,
                self.counts[:G])
+        mark(1)
         self.dist.all_to_all_single(self.counts[G:], self.counts[:G], group=self.group)
         c = self.counts.cpu().tolist()          # the split sizes: the one host read of a step
         send_c, recv_c = c[:G], c[G:]
         S, R = sum(send_c), sum(recv_c)
         self._a2a(self.recv_x[:R], self.send_x[:S], recv_c, send_c)
         self._a2a(self.recv_e[:R], self.send_e[:S], recv_c, send_c)
+        mark(2)
         o.scatter(self.recv_e[:R], R, self.nl, self.sorted_loc[:R], self.off_loc)
+        mark(3)
         o.experts(self.recv_x, R, events)
+        mark(4)
         o.rows_scatter(self.y_rows, self.sorted_loc, R, self.y_recv, R)
         self._a2a(self.y_back[:S], self.y_recv[:R], send_c, recv_c)
+        mark(5)
         o.gather(self.y_back, self.sorted_pairs, S, self.w, T, k, self.out)
+        mark(6)
         self.last = {"R": R, "sent": S, "send_counts": send_c, "recv_counts": recv_c}
 
     # ------------------------------------------------------------------ accounting (this rank)
