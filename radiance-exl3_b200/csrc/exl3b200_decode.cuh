@@ -218,6 +218,39 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int32_
     if (err) atomicOr(err, 1);
     return false;
 }
+// Two bounded waits at once: both try_waits are in flight together, so a chunk that needs two barriers pays one
+// barrier round trip, not two (a try_wait on a completed phase still takes a shared-memory round trip).
+__device__ __forceinline__ bool mbar_wait2(uint64_t* bar1, uint32_t par1, uint64_t* bar2, uint32_t par2,
+                                           int32_t* err) {
+    const uint32_t a1 = smem_u32(bar1), a2 = smem_u32(bar2);
+    uint64_t t0 = 0;
+    uint32_t d1 = 0, d2 = 0;
+    for (;;) {
+        uint32_t r1 = 1, r2 = 1;
+        if (!d1)
+            asm volatile("{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
+                         " selp.u32 %0, 1, 0, p;\n}\n"
+                         : "=r"(r1) : "r"(a1), "r"(par1), "r"(kSuspendNs) : "memory");
+        if (!d2)
+            asm volatile("{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
+                         " selp.u32 %0, 1, 0, p;\n}\n"
+                         : "=r"(r2) : "r"(a2), "r"(par2), "r"(kSuspendNs) : "memory");
+        d1 |= r1;
+        d2 |= r2;
+        if (d1 && d2) return true;
+        const uint64_t now = globaltimer_ns();
+        if (!t0) t0 = now;
+        else if (now - t0 > kWaitLimitNs) break;
+    }
+    if (err) atomicOr(err, 1);
+    return false;
+}
+__device__ __forceinline__ bool mbar_wait2_warp(uint64_t* bar1, uint32_t par1, uint64_t* bar2, uint32_t par2,
+                                                int32_t* err) {
+    const bool ok = mbar_wait2(bar1, par1, bar2, par2, err);
+    __syncwarp();
+    return ok;
+}
 // mbar_wait by a whole warp, reconverged after it: every lane has seen the phase before the warp goes on to a
 // .sync.aligned or elected instruction.
 __device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, int32_t* err) {

@@ -241,7 +241,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_skinny(const Exl3bOp op, i
     uint16_t* xr = reinterpret_cast<uint16_t*>(xr_raw);                   // [MATS][MMAX][xr_stride]
     float* red = reinterpret_cast<float*>(xr_raw);                        // [MMAX][RED_COLS] (aliases xr)
 
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int tid = threadIdx.x, warp = __shfl_sync(0xFFFFFFFFu, tid >> 5, 0), lane = tid & 31;
     const int S = ksplit;
     const uint32_t rank = S > 1 ? cluster_rank() : 0;
     const int64_t cluster_id = blockIdx.y, n_clusters = gridDim.y;
@@ -256,7 +256,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_skinny(const Exl3bOp op, i
     }
     // ---- the unit list: units of expert e = ceil(rows_e / MMAX) * n_blocks (block-scan of the counts)
     {
-        __shared__ uint32_t part[kThreads];
+        // a block-wide exclusive scan: each thread a run of experts, warp shuffles, then the warp totals
+        __shared__ uint32_t wsum[kThreads / 32];
         const int64_t per = (n_exp + kThreads - 1) / kThreads;
         const int64_t e0 = tid * per, e1 = e0 + per < n_exp ? e0 + per : n_exp;
         uint32_t sum = 0;
@@ -264,25 +265,26 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_skinny(const Exl3bOp op, i
             const int64_t r = op.expert_offset[e + 1] - op.expert_offset[e];
             sum += r > 0 ? (uint32_t)(((r + MMAX - 1) / MMAX) * n_blocks) : 0u;
         }
-        part[tid] = sum;
-        __syncthreads();
-        if (tid == 0) {
-            uint32_t acc = 0;
-            for (int t = 0; t < kThreads; ++t) {
-                const uint32_t v = part[t];
-                part[t] = acc;
-                acc += v;
-            }
-            s_misc[0] = (int)acc;
+        uint32_t incl = sum;
+#pragma unroll
+        for (int d = 1; d < 32; d <<= 1) {
+            const uint32_t v = __shfl_up_sync(0xFFFFFFFFu, incl, d);
+            if (lane >= d) incl += v;
         }
+        if (lane == 31) wsum[warp] = incl;
         __syncthreads();
-        uint32_t acc = part[tid];
+        uint32_t base = 0;
+        for (int w = 0; w < warp; ++w) base += wsum[w];
+        uint32_t acc = base + incl - sum;
         for (int64_t e = e0; e < e1; ++e) {
             prefix[e] = acc;
             const int64_t r = op.expert_offset[e + 1] - op.expert_offset[e];
             acc += r > 0 ? (uint32_t)(((r + MMAX - 1) / MMAX) * n_blocks) : 0u;
         }
-        if (tid == 0) prefix[n_exp] = (uint32_t)s_misc[0];
+        if (tid == kThreads - 1) {
+            prefix[n_exp] = acc;
+            s_misc[0] = (int)acc;
+        }
     }
     __syncthreads();
     if (S > 1) cluster_sync_all();
@@ -338,30 +340,27 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_skinny(const Exl3bOp op, i
         const int nstages = (ntk + kTks - 1) / kTks;
 
         if (warp == kConsumerWarps) {
-            // ------------------------------------------------ producer
-            if (lane == 0) {
-                const uint16_t* rec = static_cast<const uint16_t*>(tab_entry(cl.codes, ev.j));
-                const int64_t wrows = GU ? ev.R / 2 : ev.R;                  // rows of one record
-                const int64_t mat_elems = (ev.C / 16) * (wrows / 16) * 16 * BITS;
-                for (int sidx = 0; sidx < nstages; ++sidx, ++it) {
-                    const uint32_t s = it % kNst, ph = (it / kNst) & 1;
-                    mbar_wait(&empty[s], ph ^ 1, op.err);
-                    const int tk_first = sidx * kTks;
-                    const int n_in = ntk - tk_first < kTks ? ntk - tk_first : kTks;
-                    mbar_expect_tx(&full[s], (uint32_t)(n_in * MATS * Cfg::COPY_BYTES));
-                    for (int q = 0; q < n_in; ++q) {
-                        const int64_t tk = ch0 * 8 + tk_first + q;
-                        for (int mat = 0; mat < MATS; ++mat) {
-                            const uint16_t* src = rec + mat * mat_elems + (tk * (wrows / 16) + blk * 8) * 16 * BITS;
-                            tma_bulk_g2s(ring + s * Cfg::STAGE_BYTES + (q * MATS + mat) * Cfg::COPY_BYTES, src,
-                                         Cfg::COPY_BYTES, &full[s]);
-                        }
+            // ------------------------------------------------ producer (the whole warp runs the loop; the
+            // elected lane issues the copies)
+            const uint16_t* rec = static_cast<const uint16_t*>(tab_entry(cl.codes, ev.j));
+            const int64_t wrows = GU ? ev.R / 2 : ev.R;                  // rows of one record
+            const int64_t mat_elems = (ev.C / 16) * (wrows / 16) * 16 * BITS;
+            for (int sidx = 0; sidx < nstages; ++sidx, ++it) {
+                const uint32_t s = it % kNst, ph = (it / kNst) & 1;
+                mbar_wait_warp(&empty[s], ph ^ 1, op.err);
+                const int tk_first = sidx * kTks;
+                const int n_in = ntk - tk_first < kTks ? ntk - tk_first : kTks;
+                mbar_expect_tx_el(&full[s], (uint32_t)(n_in * MATS * Cfg::COPY_BYTES));
+                for (int q = 0; q < n_in; ++q) {
+                    const int64_t tk = ch0 * 8 + tk_first + q;
+#pragma unroll
+                    for (int mat = 0; mat < MATS; ++mat) {
+                        const uint16_t* src = rec + mat * mat_elems + (tk * (wrows / 16) + blk * 8) * 16 * BITS;
+                        tma_bulk_g2s_el(ring + s * Cfg::STAGE_BYTES + (q * MATS + mat) * Cfg::COPY_BYTES, src,
+                                        Cfg::COPY_BYTES, &full[s]);
                     }
                 }
-            } else {
-                it += nstages;
             }
-            __syncwarp();
         } else {
             // ------------------------------------------------ consumers: the rotated input rows into xr
             const int nchl = (int)(ch1 - ch0);
@@ -417,7 +416,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_skinny(const Exl3bOp op, i
             const int arow = (lane & 7) + 8 * ((lane >> 3) & 1), acol = 8 * (lane >> 4);
             for (int sidx = 0; sidx < nstages; ++sidx, ++it) {
                 const uint32_t s = it % kNst, ph = (it / kNst) & 1;
-                mbar_wait(&full[s], ph, op.err);
+                mbar_wait_warp(&full[s], ph, op.err);
                 const int tk_first = sidx * kTks;
                 const int n_in = ntk - tk_first < kTks ? ntk - tk_first : kTks;
                 for (int q = 0; q < n_in; ++q) {

@@ -37,7 +37,11 @@ constexpr int kRecWarp = 8;
 constexpr int kBWarp = 9;
 constexpr int kMmaWarp = 10;
 constexpr int kDecWarp0 = 11;
-constexpr int kDecWarps = 16;                        // four a lane quadrant
+#ifndef EXL3B_TC_DEC_TN
+#define EXL3B_TC_DEC_TN 1
+#endif
+constexpr int kDecTn = EXL3B_TC_DEC_TN;              // 16-row tile rows a decoder warp takes (1 or 2)
+constexpr int kDecWarps = 16 / kDecTn;               // 16 / kDecTn: 4 / kDecTn a lane quadrant
 constexpr int kTcWarps = kDecWarp0 + kDecWarps;      // 27
 constexpr int kTcThreads = kTcWarps * 32;           // 864
 constexpr int kNT = 64;                              // sorted rows a unit (the MMA's N)
@@ -313,8 +317,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             for (int ck = 0; ck < nck; ++ck) {
                 const uint32_t sa = ai % kStA, pa = (ai / kStA) & 1;
                 const uint32_t sb = bi % kStB, pb = (bi / kStB) & 1;
-                mbar_wait_warp(&a_full[sa], pa, op.err);
-                mbar_wait_warp(&b_full[sb], pb, op.err);
+                mbar_wait2_warp(&a_full[sa], pa, &b_full[sb], pb, op.err);
                 tc_fence_after();
                 const uint32_t ta = tmem + kAccCols + sa * kAStageCols;
                 const uint64_t db = b_desc0 + (uint64_t)((sb * 2 * kBTile) >> 4);
@@ -337,7 +340,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         // warp -> (lane quadrant q = warp % 4, j): block j / 2, tile row tn = 2q + j % 2 -- weight rows 16 tn ..
         // 16 tn + 15 of the block, TMEM lanes of quadrant q only; every k tile of the chunk
         const int q = warp & 3, j = (warp - kDecWarp0) >> 2;
-        const int blk = j >> 1, tn = 2 * q + (j & 1);
+        const int blk = kDecTn == 1 ? j >> 1 : j, tn = kDecTn == 1 ? 2 * q + (j & 1) : 2 * q;
         const LaneDec<BITS> ld = lane_dec<BITS>(lane);
         const uint32_t tile_off = (uint32_t)(blk * Cfg::REC_ROW + tn * Cfg::TILE_BYTES);
         const uint32_t a_t0 = tmem + ((uint32_t)(16 * tn) << 16) + kAccCols + blk * (kKC / 2);
@@ -351,17 +354,18 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             for (int ck = 0; ck < nck; ++ck) {
                 const uint32_t sr = ri % Cfg::ST_R, pr = (ri / Cfg::ST_R) & 1;
                 const uint32_t sa = ai % kStA, pa = (ai / kStA) & 1;
-                mbar_wait_warp(&r_full[sr], pr, op.err);
-                mbar_wait_warp(&a_empty[sa], pa ^ 1, op.err);
+                mbar_wait2_warp(&r_full[sr], pr, &a_empty[sa], pa ^ 1, op.err);
                 tc_fence_after();
                 const uint8_t* rst = r_ring + sr * Cfg::REC_STAGE + tile_off;
                 const uint32_t ta = a_t0 + sa * kAStageCols;
 #pragma unroll
-                for (int tk = 0; tk < 4; ++tk) {
-                    uint32_t b[4];
-                    decode_tile<BITS, CB>(rst + tk * 2 * Cfg::REC_ROW, ld, b);
-                    tmem_st_16x128b_x2(ta + tk * 8, b[0], b[2], b[1], b[3]);
-                }
+                for (int tt = 0; tt < kDecTn; ++tt)
+#pragma unroll
+                    for (int tk = 0; tk < 4; ++tk) {
+                        uint32_t b[4];
+                        decode_tile<BITS, CB>(rst + tk * 2 * Cfg::REC_ROW + tt * Cfg::TILE_BYTES, ld, b);
+                        tmem_st_16x128b_x2(ta + ((uint32_t)(16 * tt) << 16) + tk * 8, b[0], b[2], b[1], b[3]);
+                    }
                 tmem_wait_st();
                 tc_fence_before();
                 __syncwarp();
