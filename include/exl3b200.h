@@ -108,6 +108,27 @@ int     exl3b200_ep_pack(const uint16_t* x, int64_t x_pitch, const int32_t* ids,
                          void* stream);
 int     exl3b200_rows_scatter(const void* src, int64_t src_pitch, const int32_t* idx, int64_t n_rows,
                               int64_t row_bytes, void* dst, int64_t dst_pitch, int64_t n_dst, void* stream);
+/* The deduplicated dispatch (one row a distinct (token, rank), every pair still its own combine row):
+ *   ep_dest:       dest[p] = ids[p] / n_local, -1 for a dropped slot (sort the pairs by it with moe_scatter over
+ *                  `world` "experts": stable, so each rank's pairs come out in token order).
+ *   ep_pack_dedup: for rank d's pairs sorted_pairs[dest_off[d] .. dest_off[d+1]) (n_pairs in all): the first
+ *                  pair of each token makes row r of rank d (r = the rank's rows so far); row r's token goes to
+ *                  row_tok[dest_off[d] + r] (scratch, n_pairs ints) and its x row to send_x[(rows of ranks before
+ *                  d) + r]; pair j's meta is (r << 12) | (ids % n_local); counts[2d] = rows, counts[2d+1] = pairs.
+ *                  n_local <= 4096, fewer than 2^20 tokens.
+ *   ep_unpack:     received pairs (concatenated by source, recv_counts as counts above): pair q's local expert and
+ *                  its row among the received rows (rows before its source + its r).
+ *   ep_map:        out[i] = table[idx[i]] (-1 outside the table): the token row of each sorted pair. */
+int     exl3b200_ep_dest(const int32_t* ids, int64_t n_pairs, int64_t n_local, int64_t world, int32_t* dest,
+                         void* stream);
+int     exl3b200_ep_pack_dedup(const uint16_t* x, int64_t x_pitch, const int32_t* ids, int64_t top_k,
+                               const int32_t* sorted_pairs, const int32_t* dest_off, int64_t n_pairs, int64_t n_local,
+                               int64_t world, int64_t hidden, uint16_t* send_x, uint32_t* send_meta,
+                               int32_t* row_tok, int32_t* counts, void* stream);
+int     exl3b200_ep_unpack(const uint32_t* meta, int64_t n_pairs, const int32_t* recv_counts, int64_t world,
+                           int32_t* expert, int32_t* row, void* stream);
+int     exl3b200_ep_map(const int32_t* idx, int64_t n, const int32_t* table, int64_t n_table, int32_t* out,
+                        void* stream);
 
 /* The device error word of the current device: nonzero once a bounded wait inside a kernel gave up (the
  * launch then finished without a valid result). Reading it synchronises the device; `clear` resets it. Not

@@ -5,19 +5,21 @@ The reference runs the layer on one device; this is the multi-GPU form the path 
 contiguous blocks (expert e on rank e // n_local); every rank routes its own tokens. One step on each rank:
 
     router_topk                      ids, w                          [T, top_k]
-    moe_scatter over ALL experts     sorted_pairs, expert_offset     the pairs grouped by the rank of their expert
-    ep_pack                          send_x (token rows), send_e (local expert ids), send counts per rank
+    ep_dest + moe_scatter over ranks sorted_pairs, dest_off          pairs grouped by owning rank, token order inside
+    ep_pack_dedup                    send_x: ONE row a distinct (token, rank); a meta word a pair (row, local expert)
     all-to-all of the counts         -> the one host read of a step: the split sizes
-    all-to-all of send_x, send_e     -> recv_x, recv_e               rows in arrival order (source rank, then sorted)
-    moe_scatter over local experts   sorted_loc, off_loc             (top_k 1: a received row is its own token)
-    moe_exl3_gate_up, moe_exl3_down  y_rows (bf16, sorted order)     the plugin rows, exactly as on one GPU
-    rows_scatter                     y_recv (arrival order)
-    all-to-all back                  y_back                          in the order the pairs were sent
-    moe_gather over sorted_pairs     out f32 [T, H]                  slots summed in ascending order, as on one GPU
+    all-to-all of rows and metas     -> recv_x (rows), recv_meta (pairs), in source-rank order
+    ep_unpack, moe_scatter (local)   each received pair's local expert and row; pairs sorted by local expert
+    ep_map                           sorted pair -> its token row (the sorted_tok the ops read, top_k 1)
+    moe_exl3_gate_up, moe_exl3_down  y_rows (bf16, one a pair, sorted order), the plugin rows as on one GPU
+    rows_scatter                     y_recv (arrival order of the pairs)
+    all-to-all back                  y_back, in the order the pairs were sent
+    moe_gather over sorted_pairs     out f32 [T, H]: slots summed in ascending order, as on one GPU
 
-Each pair's down row is the one a single GPU computes (same expert, same input row), and the gather sums a
-token's slots in the same order, so the layer's output does not depend on the number of ranks. The all-to-alls
-move bf16/fp16 rows bit for bit (as float16 views: a copy, no arithmetic).
+A token row crosses to a rank once however many of its slots that rank serves (dispatch bytes: distinct
+(token, rank) pairs, not slots); every pair still returns its own down row, so each pair's down row is the one a
+single GPU computes and the gather sums a token's slots in the same order -- the layer's output does not depend on
+the number of ranks. The all-to-alls move bf16/fp16 rows bit for bit (as float16 views: a copy, no arithmetic).
 
 `ops` supplies the device steps: `DeviceOps` (the library, CUDA tensors, NCCL) or a host stand-in with the same
 methods for testing the exchange on CPU ranks over gloo."""
@@ -61,13 +63,25 @@ class DeviceOps:
         self.nat.moe_scatter(ids.data_ptr(), n_pairs, n_expert, 0, sorted_tok.data_ptr(), offset.data_ptr(),
                              work.data_ptr(), self._stream())
 
-    def pack(self, x, ids, k, sorted_pairs, n_pairs, offset, n_local, world, send_x, send_e, counts):
-        self.nat.ep_pack(x.data_ptr(), x.shape[1], ids.data_ptr(), k, sorted_pairs.data_ptr(), n_pairs,
-                         offset.data_ptr(), n_local, world, x.shape[1], send_x.data_ptr(), send_e.data_ptr(),
-                         counts.data_ptr(), self._stream())
+    def dest(self, ids, n_pairs, n_local, world, dest):
+        self.nat.ep_dest(ids.data_ptr(), n_pairs, n_local, world, dest.data_ptr(), self._stream())
 
-    def experts(self, recv_x, R, events=None):
-        self.local.experts(R, R, self._stream(), x_ptr=recv_x.data_ptr(), top_k=1, M=R, events=events)
+    def pack_dedup(self, x, ids, k, sorted_pairs, dest_off, n_pairs, n_local, world, send_x, send_meta, row_tok,
+                   counts):
+        self.nat.ep_pack_dedup(x.data_ptr(), x.shape[1], ids.data_ptr(), k, sorted_pairs.data_ptr(),
+                               dest_off.data_ptr(), n_pairs, n_local, world, x.shape[1], send_x.data_ptr(),
+                               send_meta.data_ptr(), row_tok.data_ptr(), counts.data_ptr(), self._stream())
+
+    def unpack(self, meta, n_pairs, recv_counts, world, expert, row):
+        self.nat.ep_unpack(meta.data_ptr(), n_pairs, recv_counts.data_ptr(), world, expert.data_ptr(),
+                           row.data_ptr(), self._stream())
+
+    def map(self, idx, n, table, n_table, out):
+        self.nat.ep_map(idx.data_ptr(), n, table.data_ptr(), n_table, out.data_ptr(), self._stream())
+
+    def experts(self, recv_x, n_rows, n_pairs, events=None):
+        self.local.experts(n_rows, n_pairs, self._stream(), x_ptr=recv_x.data_ptr(), top_k=1, M=n_rows,
+                           events=events)
 
     def rows_scatter(self, src, idx, n_rows, dst, n_dst):
         rb = src.shape[1] * src.element_size()
@@ -80,12 +94,13 @@ class DeviceOps:
                             out.shape[1], out.data_ptr(), work.data_ptr(), self._stream())
 
     def kernels(self, T, k, E, R):
-        """How many of the library's kernels one step launches (ep_pack and rows_scatter counted)."""
+        """How many of the library's kernels one step launches: router, ep_dest, rank scatter, the two pack
+        kernels, ep_unpack, local scatter, ep_map, gate_up (+ prep), down, rows_scatter, the gather's two."""
         P = T * k
         tc = R > 0 and self.local._tc("gate_up", R)
-        n = 1 + (1 if P <= 8192 else 3) + 1 + (1 if R <= 8192 else 3)
-        n += (2 + (1 if tc else 0)) if R > 0 else 0
-        n += 1 if R > 0 else 0
+        n = 1 + 1 + (1 if P <= 8192 else 3) + 2
+        if R > 0:
+            n += 1 + (1 if R <= 8192 else 3) + 1 + 2 + (1 if tc else 0) + 1
         return n + 2
 
 
@@ -116,14 +131,19 @@ class EpLayer:
         e = lambda *shape, dt: torch.empty(shape, dtype=dt, device=dev)  # noqa: E731
         f16, bf16, i32, f32 = torch.float16, torch.bfloat16, torch.int32, torch.float32
         self.x, self.logits = e(max_tokens, H, dt=f16), e(max_tokens, n_expert, dt=f32)
-        self.ids, self.w = e(P, dt=i32), e(P, dt=f32)
-        self.sorted_pairs, self.offset = e(P, dt=i32), e(n_expert + 1, dt=i32)
-        self.send_x, self.send_e = e(P, H, dt=f16), e(P, dt=i32)
-        self.counts = torch.zeros(2 * world, dtype=i32, device=dev)     # [send counts | receive counts]
-        self.recv_x, self.recv_e = e(self.Rcap, H, dt=f16), e(self.Rcap, dt=i32)
+        self.ids, self.w, self.dest = e(P, dt=i32), e(P, dt=f32), e(P, dt=i32)
+        self.sorted_pairs, self.row_tok = e(P, dt=i32), e(P, dt=i32)
+        # one host read a step: [send counts 2G | receive counts 2G | rank offsets of the sorted pairs G + 1]
+        self.hdr = torch.zeros(5 * world + 1, dtype=i32, device=dev)
+        self.counts_send, self.counts_recv = self.hdr[:2 * world], self.hdr[2 * world:4 * world]
+        self.dest_off = self.hdr[4 * world:]
+        self.send_x, self.send_meta = e(P, H, dt=f16), e(P, dt=i32)
+        self.recv_x = e(world * max_tokens, H, dt=f16)                # rows: at most T from each source
+        self.recv_meta, self.pair_e, self.pair_row = e(self.Rcap, dt=i32), e(self.Rcap, dt=i32), e(self.Rcap, dt=i32)
+        self.sorted_pair = e(self.Rcap, dt=i32)
         self.y_recv, self.y_back = e(self.Rcap, H, dt=bf16), e(P, H, dt=bf16)
         self.out = e(max_tokens, H, dt=f32)
-        self.sorted_loc, self.off_loc, self.y_rows = ops.local_buffers()
+        self.sorted_row, self.off_loc, self.y_rows = ops.local_buffers()
         self.last = {"R": 0, "sent": 0}
 
     # ------------------------------------------------------------------ the exchange
@@ -137,37 +157,46 @@ class EpLayer:
 
     PHASES = ("route+pack", "counts+dispatch", "local sort", "experts", "combine", "gather")
 
-    def forward(self, T, stream=None, events=None, phases=None):
-        """The layer over the first T tokens of self.x / self.logits into self.out[:T]. `stream` must be torch's
-        current stream (the collectives run there); `events` as MoeLayer.experts; `phases`: len(PHASES) + 1 CUDA
-        events recorded between the steps (for a per-phase breakdown)."""
+    def forward(self, T, stream=None, events=None, phases=None, x=None, logits=None, out=None):
+        """The layer over the first T tokens of self.x / self.logits into self.out[:T] (`x`, `logits`, `out`
+        replace them, e.g. for double-buffered inputs). `stream` must be torch's current stream (the collectives
+        run there); `events` as MoeLayer.experts; `phases`: len(PHASES) + 1 CUDA events recorded between the steps
+        (for a per-phase breakdown)."""
         if T > self.max_tokens:
             raise ValueError(f"T {T} > max_tokens {self.max_tokens}")
+        x = self.x if x is None else x
+        logits = self.logits if logits is None else logits
+        out = self.out if out is None else out
         o, G, k, P = self.ops, self.G, self.k, T * self.k
         mark = (lambda i: phases[i].record()) if phases else (lambda i: None)
         mark(0)
-        o.router(self.logits, T, self.E, k, self.ids, self.w)
-        o.scatter(self.ids, P, self.E, self.sorted_pairs[:P], self.offset)
-        o.pack(self.x, self.ids, k, self.sorted_pairs, P, self.offset, self.nl, G, self.send_x, self.send_e,
-               self.counts[:G])
+        o.router(logits, T, self.E, k, self.ids, self.w)
+        o.dest(self.ids, P, self.nl, G, self.dest)
+        o.scatter(self.dest, P, G, self.sorted_pairs[:P], self.dest_off)
+        o.pack_dedup(x, self.ids, k, self.sorted_pairs, self.dest_off, P, self.nl, G, self.send_x,
+                     self.send_meta, self.row_tok, self.counts_send)
         mark(1)
-        self.dist.all_to_all_single(self.counts[G:], self.counts[:G], group=self.group)
-        c = self.counts.cpu().tolist()          # the split sizes: the one host read of a step
-        send_c, recv_c = c[:G], c[G:]
-        S, R = sum(send_c), sum(recv_c)
-        self._a2a(self.recv_x[:R], self.send_x[:S], recv_c, send_c)
-        self._a2a(self.recv_e[:R], self.send_e[:S], recv_c, send_c)
+        self.dist.all_to_all_single(self.counts_recv, self.counts_send, group=self.group)
+        h = self.hdr.cpu().tolist()             # the split sizes: the one host read of a step
+        rows_s, pairs_s = h[0:2 * G:2], h[1:2 * G:2]
+        rows_r, pairs_r = h[2 * G:4 * G:2], h[2 * G + 1:4 * G:2]
+        S, Rr, R = sum(pairs_s), sum(rows_r), sum(pairs_r)
+        self._a2a(self.recv_x[:Rr], self.send_x[:sum(rows_s)], rows_r, rows_s)
+        self._a2a(self.recv_meta[:R], self.send_meta[:S], pairs_r, pairs_s)
         mark(2)
-        o.scatter(self.recv_e[:R], R, self.nl, self.sorted_loc[:R], self.off_loc)
+        o.unpack(self.recv_meta, R, self.counts_recv, G, self.pair_e, self.pair_row)
+        o.scatter(self.pair_e[:R], R, self.nl, self.sorted_pair[:R], self.off_loc)
+        o.map(self.sorted_pair, R, self.pair_row, R, self.sorted_row)
         mark(3)
-        o.experts(self.recv_x, R, events)
+        o.experts(self.recv_x, Rr, R, events)
         mark(4)
-        o.rows_scatter(self.y_rows, self.sorted_loc, R, self.y_recv, R)
-        self._a2a(self.y_back[:S], self.y_recv[:R], send_c, recv_c)
+        o.rows_scatter(self.y_rows, self.sorted_pair, R, self.y_recv, R)
+        self._a2a(self.y_back[:S], self.y_recv[:R], pairs_s, pairs_r)
         mark(5)
-        o.gather(self.y_back, self.sorted_pairs, S, self.w, T, k, self.out)
+        o.gather(self.y_back, self.sorted_pairs, S, self.w, T, k, out)
         mark(6)
-        self.last = {"R": R, "sent": S, "send_counts": send_c, "recv_counts": recv_c}
+        self.last = {"R": R, "rows_recv": Rr, "sent": S, "rows_sent": sum(rows_s), "send_counts": pairs_s,
+                     "recv_counts": pairs_r, "send_rows": rows_s, "recv_rows": rows_r}
 
     # ------------------------------------------------------------------ accounting (this rank)
     def live_experts(self):
@@ -179,8 +208,8 @@ class EpLayer:
 
     def time_prep_step(self, T, n=5):
         """The local pass's gate_up input rotation alone (ms), over the rows the last step received."""
-        R = self.last["R"]
-        return self.ops.local.time_prep(R, R, x_ptr=self.recv_x.data_ptr(), top_k=1, n=n)
+        R, Rr = self.last["R"], self.last.get("rows_recv", self.last["R"])
+        return self.ops.local.time_prep(Rr, R, x_ptr=self.recv_x.data_ptr(), top_k=1, n=n)
 
     def expert_flops(self, rows):
         return self.ops.local.expert_flops(rows)
@@ -192,10 +221,12 @@ class EpLayer:
         return self.ops.kernels(T, self.k, self.E, self.last["R"])
 
     def exchange_bytes(self):
-        """Bytes this rank sent to other ranks in the last step (rows out and back, ids), its own rows excluded."""
+        """Bytes this rank sent to other ranks in the last step: token rows and pair metas out, the down rows of the
+        pairs it served back; what it keeps for itself excluded."""
         if "send_counts" not in self.last:
             return 0
-        own_s, own_r = self.last["send_counts"][self.rank], self.last["recv_counts"][self.rank]
-        rows_out = self.last["sent"] - own_s
-        rows_back = self.last["R"] - own_r
-        return rows_out * (2 * self.H + 4) + rows_back * 2 * self.H
+        L, r = self.last, self.rank
+        rows_out = L["rows_sent"] - L["send_rows"][r]
+        metas_out = L["sent"] - L["send_counts"][r]
+        rows_back = L["R"] - L["recv_counts"][r]
+        return rows_out * 2 * self.H + metas_out * 4 + rows_back * 2 * self.H

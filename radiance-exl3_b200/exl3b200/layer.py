@@ -243,15 +243,19 @@ class MoeLayer:
         rows = T * self.k
         return 1 + (1 if rows <= 8192 else 3) + 2 + 2 + (1 if self._tc("gate_up", rows) else 0)
 
-    def forward(self, T, stream, events=None):
-        """The whole layer over the first T tokens of self.x / self.logits into self.out (f32 [T, H])."""
+    def forward(self, T, stream, events=None, x=None, logits=None, out=None):
+        """The whole layer over the first T tokens of self.x / self.logits into self.out (f32 [T, H]); `x`,
+        `logits`, `out` (tensors of the same shapes) replace them, e.g. for double-buffered inputs."""
         nat, rows = self.native, T * self.k
-        nat.router_topk(self.logits.data_ptr(), T, self.E, self.k, self.ids.data_ptr(), self.w.data_ptr(), stream)
+        xp = x.data_ptr() if x is not None else None
+        lp = (logits if logits is not None else self.logits).data_ptr()
+        op_ = (out if out is not None else self.out).data_ptr()
+        nat.router_topk(lp, T, self.E, self.k, self.ids.data_ptr(), self.w.data_ptr(), stream)
         nat.moe_scatter(self.ids.data_ptr(), rows, self.n_local, self.base, self.sorted_tok.data_ptr(),
                         self.offset.data_ptr(), self.scatter_work.data_ptr(), stream)
-        self.experts(T, rows, stream, events=events)
+        self.experts(T, rows, stream, x_ptr=xp, events=events)
         nat.moe_gather(self.y_rows.data_ptr(), self.H, self.sorted_tok.data_ptr(), rows, self.w.data_ptr(), T, self.k,
-                       self.H, self.out.data_ptr(), self.gather_work.data_ptr(), stream)
+                       self.H, op_, self.gather_work.data_ptr(), stream)
 
     # ------------------------------------------------------------------ accounting
     def time_prep_step(self, T, n=5):

@@ -25,6 +25,10 @@ class Native:
         L.exl3b200_read_error.argtypes = [_I, C.POINTER(C.c_int32)]
         L.exl3b200_ep_pack.argtypes = [_VP, _I64, _VP, _I64, _VP, _I64, _VP, _I64, _I64, _I64, _VP, _VP, _VP, _VP]
         L.exl3b200_rows_scatter.argtypes = [_VP, _I64, _VP, _I64, _I64, _VP, _I64, _I64, _VP]
+        L.exl3b200_ep_dest.argtypes = [_VP, _I64, _I64, _I64, _VP, _VP]
+        L.exl3b200_ep_pack_dedup.argtypes = [_VP, _I64, _VP, _I64, _VP, _VP, _I64, _I64, _I64, _I64, _VP, _VP, _VP, _VP, _VP]
+        L.exl3b200_ep_unpack.argtypes = [_VP, _I64, _VP, _I64, _VP, _VP, _VP]
+        L.exl3b200_ep_map.argtypes = [_VP, _I64, _VP, _I64, _VP, _VP]
 
     @staticmethod
     def _check(rc, what):
@@ -75,3 +79,19 @@ class Native:
     def rows_scatter(self, src, src_pitch, idx, n_rows, row_bytes, dst, dst_pitch, n_dst, stream=0):
         self._check(self.lib.exl3b200_rows_scatter(src, src_pitch, idx, n_rows, row_bytes, dst, dst_pitch, n_dst,
                                                    stream), "exl3b200_rows_scatter")
+
+    def ep_dest(self, ids, n_pairs, n_local, world, dest, stream=0):
+        self._check(self.lib.exl3b200_ep_dest(ids, n_pairs, n_local, world, dest, stream), "exl3b200_ep_dest")
+
+    def ep_pack_dedup(self, x, x_pitch, ids, top_k, sorted_pairs, dest_off, n_pairs, n_local, world, hidden,
+                      send_x, send_meta, row_tok, counts, stream=0):
+        self._check(self.lib.exl3b200_ep_pack_dedup(x, x_pitch, ids, top_k, sorted_pairs, dest_off, n_pairs, n_local,
+                                                    world, hidden, send_x, send_meta, row_tok, counts, stream),
+                    "exl3b200_ep_pack_dedup")
+
+    def ep_unpack(self, meta, n_pairs, recv_counts, world, expert, row, stream=0):
+        self._check(self.lib.exl3b200_ep_unpack(meta, n_pairs, recv_counts, world, expert, row, stream),
+                    "exl3b200_ep_unpack")
+
+    def ep_map(self, idx, n, table, n_table, out, stream=0):
+        self._check(self.lib.exl3b200_ep_map(idx, n, table, n_table, out, stream), "exl3b200_ep_map")

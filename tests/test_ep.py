@@ -1,6 +1,6 @@
 """Expert parallelism: the exchange of exl3b200/ep.py on CPU ranks over gloo (world sizes 2 and 4), and on the GPU
-the two EP kernels (ep_pack, rows_scatter) against their numpy statements and, with two GPUs, the whole EP layer
-over NCCL against the one-GPU layer.
+the EP kernels (ep_pack, rows_scatter, ep_dest, ep_pack_dedup, ep_unpack, ep_map) against their host statements
+and, with two GPUs, the whole EP layer over NCCL against the one-GPU layer.
 
 On CPU the device steps are host stand-ins with the same contracts: the oracle's stable scatter and gather, numpy
 for the pack and the row scatter, and a synthetic expert (row * a_e + b_e, rounded to bf16) that makes every row's
@@ -68,20 +68,48 @@ class CpuOps:
         sorted_tok[:n_pairs] = torch.from_numpy(st)
         offset[:] = torch.from_numpy(off)
 
-    def pack(self, x, ids, k, sorted_pairs, n_pairs, offset, n_local, world, send_x, send_e, counts):
-        off = offset.numpy()
-        for r in range(world):
-            counts[r] = int(off[(r + 1) * n_local] - off[r * n_local])
-        xs = x.view(torch.int16).numpy()
-        sx = send_x.view(torch.int16).numpy()
-        for j in range(n_pairs):
-            p = int(sorted_pairs[j])
-            if p < 0:
-                continue
-            sx[j] = xs[p // k]
-            send_e[j] = int(ids[p]) % n_local
+    def dest(self, ids, n_pairs, n_local, world, dest):
+        i = ids[:n_pairs].numpy()
+        dest[:n_pairs] = torch.from_numpy(np.where(i >= 0, i // n_local, -1).astype(np.int32))
 
-    def experts(self, recv_x, R, events=None):
+    def pack_dedup(self, x, ids, k, sorted_pairs, dest_off, n_pairs, n_local, world, send_x, send_meta, row_tok,
+                   counts):
+        """The contract of exl3b200_ep_pack_dedup, restated: per rank, one row per distinct token in pair order."""
+        off = dest_off.numpy()
+        xs, sx = x.view(torch.int16).numpy(), send_x.view(torch.int16).numpy()
+        sp, ii = sorted_pairs.numpy(), ids.numpy()
+        base = 0
+        for d in range(world):
+            r, prev = -1, None
+            for j in range(off[d], off[d + 1]):
+                p = int(sp[j])
+                t = p // k
+                if t != prev:
+                    r += 1
+                    prev = t
+                    sx[base + r] = xs[t]
+                send_meta[j] = (r << 12) | (int(ii[p]) % n_local)
+            counts[2 * d] = r + 1
+            counts[2 * d + 1] = int(off[d + 1] - off[d])
+            base += r + 1
+
+    def unpack(self, meta, n_pairs, recv_counts, world, expert, row):
+        rc = recv_counts.numpy()
+        m = meta[:n_pairs].numpy().view(np.uint32)
+        q, rb = 0, 0
+        for s in range(world):
+            for _ in range(int(rc[2 * s + 1])):
+                expert[q] = int(m[q] & 0xFFF)
+                row[q] = rb + int(m[q] >> 12)
+                q += 1
+            rb += int(rc[2 * s])
+
+    def map(self, idx, n, table, n_table, out):
+        for i in range(n):
+            j = int(idx[i])
+            out[i] = int(table[j]) if 0 <= j < n_table else -1
+
+    def experts(self, recv_x, n_rows, n_pairs, events=None):
         st, off, y = self._loc
         xs = recv_x.view(torch.int16).numpy().view(np.uint16)
         ys = y.view(torch.int16).numpy()
@@ -137,10 +165,12 @@ def _ep_rank(rank, world, port, T, E, H, k, skew, q):
             layer.forward(T)
         got = layer.out[:T].numpy().copy()
         want = single_layer(orc, x, logits, k, E)
-        q.put((rank, bool(np.array_equal(got.view(np.uint32), want.view(np.uint32))), layer.last["R"],
-               layer.last["send_counts"], layer.last["recv_counts"]))
+        L = layer.last
+        q.put((rank, bool(np.array_equal(got.view(np.uint32), want.view(np.uint32))), L["R"],
+               L["send_counts"], L["recv_counts"], L["send_rows"], L["recv_rows"]))
     except Exception as exc:  # reported to the parent, which fails the test
-        q.put((rank, repr(exc), -1, None, None))
+        import traceback
+        q.put((rank, repr(exc) + traceback.format_exc()[-800:], -1, None, None, None, None))
     finally:
         dist.destroy_process_group()
 
@@ -162,19 +192,21 @@ def _run_world(world, T, E, H, k, skew=False):
 @pytest.mark.parametrize("world", [2, 4])
 def test_ep_exchange_equals_one_process(world):
     res = _run_world(world, T=7, E=16, H=64, k=3)
-    for rank, ok, R, send_c, recv_c in res:
-        assert ok is True, f"rank {rank}: {ok}"
-    # every row sent is received once: the count matrices transpose into each other
-    send = np.array([r[3] for r in res])
-    recv = np.array([r[4] for r in res])
-    assert np.array_equal(send.T, recv)
+    for r in res:
+        assert r[1] is True, f"rank {r[0]}: {r[1]}"
+    # every pair and every row sent is received once: the count matrices transpose into each other
+    send, recv = np.array([r[3] for r in res]), np.array([r[4] for r in res])
+    srow, rrow = np.array([r[5] for r in res]), np.array([r[6] for r in res])
+    assert np.array_equal(send.T, recv) and np.array_equal(srow.T, rrow)
     assert send.sum() == world * 7 * 3
+    # a token row crosses to a rank once: rows sent = distinct (token, rank) pairs <= pairs, and fewer in all
+    assert (srow <= send).all() and srow.sum() < send.sum()
 
 
 def test_ep_exchange_with_ranks_that_receive_nothing():
     res = _run_world(4, T=5, E=16, H=64, k=2, skew=True)
-    for rank, ok, R, _, _ in res:
-        assert ok is True, f"rank {rank}: {ok}"
+    for r in res:
+        assert r[1] is True, f"rank {r[0]}: {r[1]}"
     assert res[0][2] == 4 * 5 * 2 and all(r[2] == 0 for r in res[1:])
 
 
@@ -234,6 +266,63 @@ def test_rows_scatter_kernel(n, row_bytes, n_dst):
     nat.rows_scatter(s.data_ptr(), row_bytes, i.data_ptr(), n, row_bytes, d.data_ptr(), row_bytes, n_dst, 0)
     torch.cuda.synchronize()
     assert torch.equal(d.cpu(), want)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("T,k,world,n_local,H", [(1, 1, 2, 4, 64), (37, 4, 2, 8, 256), (600, 10, 8, 64, 2048),
+                                                 (3000, 10, 4, 16, 128)])
+def test_ep_dedup_kernels(T, k, world, n_local, H):
+    """ep_dest -> moe_scatter over ranks -> ep_pack_dedup -> (as if received whole by one rank) ep_unpack -> ep_map,
+    each against CpuOps' restatement of its contract."""
+    nat, dev = _lib(), torch.device("cuda")
+    E, P = n_local * world, T * k
+    g = torch.Generator().manual_seed(T * 7 + H)
+    x = torch.randn((T, H), generator=g).to(torch.float16)
+    ids = torch.stack([torch.randperm(E, generator=g)[:k] for _ in range(T)]).to(torch.int32).reshape(-1)
+    orc = Oracle()
+    cpu = CpuOps(orc, 0, n_local, E, H, P)
+    # ep_dest
+    dest_d = torch.full((P,), -7, dtype=torch.int32, device=dev)
+    idd = ids.to(dev)
+    nat.ep_dest(idd.data_ptr(), P, n_local, world, dest_d.data_ptr(), 0)
+    want_dest = torch.zeros(P, dtype=torch.int32)
+    cpu.dest(ids, P, n_local, world, want_dest)
+    assert torch.equal(dest_d.cpu(), want_dest)
+    # the rank sort (the oracle's stable scatter), then the pack
+    sp, doff = orc.scatter(want_dest.numpy(), world)
+    spd, doffd = torch.from_numpy(sp).to(dev), torch.from_numpy(doff).to(dev)
+    sx = torch.full((P, H), 3, dtype=torch.int16, device=dev)
+    meta = torch.zeros(P, dtype=torch.int32, device=dev)
+    rtok = torch.zeros(P, dtype=torch.int32, device=dev)
+    cnt = torch.zeros(2 * world, dtype=torch.int32, device=dev)
+    xd = x.to(dev)
+    nat.ep_pack_dedup(xd.data_ptr(), H, idd.data_ptr(), k, spd.data_ptr(), doffd.data_ptr(), P, n_local, world, H,
+                      sx.data_ptr(), meta.data_ptr(), rtok.data_ptr(), cnt.data_ptr(), 0)
+    torch.cuda.synchronize()
+    w_sx = torch.full((P, H), 3, dtype=torch.int16).view(torch.float16)
+    w_meta, w_cnt = torch.zeros(P, dtype=torch.int32), torch.zeros(2 * world, dtype=torch.int32)
+    cpu.pack_dedup(x, ids, k, torch.from_numpy(sp), torch.from_numpy(doff), P, n_local, world, w_sx, w_meta, None,
+                   w_cnt)
+    assert torch.equal(cnt.cpu(), w_cnt)
+    n_rows = int(w_cnt[0::2].sum())
+    assert torch.equal(sx.cpu()[:n_rows], w_sx.view(torch.int16)[:n_rows])
+    assert torch.equal(meta.cpu(), w_meta)
+    # unpack as if one rank received every rank's pairs and rows, then map a permutation through the row table
+    ex = torch.zeros(P, dtype=torch.int32, device=dev)
+    rw = torch.zeros(P, dtype=torch.int32, device=dev)
+    nat.ep_unpack(meta.data_ptr(), P, cnt.data_ptr(), world, ex.data_ptr(), rw.data_ptr(), 0)
+    w_ex, w_rw = torch.zeros(P, dtype=torch.int32), torch.zeros(P, dtype=torch.int32)
+    cpu.unpack(w_meta, P, w_cnt, world, w_ex, w_rw)
+    torch.cuda.synchronize()
+    assert torch.equal(ex.cpu(), w_ex) and torch.equal(rw.cpu(), w_rw)
+    perm = torch.randperm(P, generator=g).to(torch.int32)
+    perm[::5] = -1
+    out = torch.zeros(P, dtype=torch.int32, device=dev)
+    nat.ep_map(perm.to(dev).data_ptr(), P, rw.data_ptr(), P, out.data_ptr(), 0)
+    w_out = torch.zeros(P, dtype=torch.int32)
+    cpu.map(perm, P, w_rw, P, w_out)
+    torch.cuda.synchronize()
+    assert torch.equal(out.cpu(), w_out)
 
 
 def _ep_gpu_rank(rank, world, port, q):
