@@ -15,11 +15,12 @@
 #include <stdlib.h>
 #include <string.h>
 
-/* The CUDA side (exl3b200_kernels.cu, exl3b200_moe.cu). */
+/* The CUDA side (exl3b200_kernels.cu, exl3b200_moe.cu, exl3b200_tc.cu). */
 int     exl3b_cuda_decode_what(const void* record, int64_t rows, int64_t cols, int bits, int codebook, void* out,
                                void* stream);
 int     exl3b_cuda_prep(const Exl3bOp* op, void* dst, int64_t dst_pitch, void* stream);
 int     exl3b_cuda_gemm_tc(const Exl3bOp* op, const void* xin, int64_t xin_pitch, int sm_count, void* stream);
+int64_t exl3b_tc_smem_bytes(int bits);
 int     exl3b_plan_skinny(const Exl3bOp* op, int sm_count, Exl3bPlan* p);
 int     exl3b_cuda_gemm_skinny(const Exl3bOp* op, const Exl3bPlan* p, void* stream);
 int     exl3b_cuda_device_info(int* sm_count, int32_t** err_word);
@@ -170,12 +171,14 @@ static int tc_band(const Exl3bOp* k) {
     if (live <= 0) return 0;
     int64_t pairs = 0;
     for (int c = 0; c < k->n_class; ++c) {
-        if (k->cls[c].cols % 64) return 0;
+        if (k->cls[c].cols % 128) return 0;
         if (k->op == EXL3B_OP_DOWN && k->cls[c].rows % 256) return 0;
         if (k->cls[c].rows / 256 > pairs) pairs = k->cls[c].rows / 256;
     }
     if (k->T / live < EXL3B_TC_MIN_ROWS && live * pairs < EXL3B_TC_MIN_UNITS) return 0;
     if ((k->n_expert + 1) * 4 > 16384) return 0;
+    /* the kernel's shared memory (rings by bitrate + the unit prefix) must fit a CTA */
+    if (exl3b_tc_smem_bytes(k->bits) + ((k->n_expert + 1) * 4 + 15) / 16 * 16 + 16 + 4096 > 227 * 1024) return 0;
     return 1;
 }
 

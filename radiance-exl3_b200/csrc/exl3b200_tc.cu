@@ -18,7 +18,7 @@
 //                memory; a decoder warp writes only its own TMEM lane quadrant (warp % 4)
 //
 // Tensor memory (512 columns): two accumulator buffers (2 units x 2 blocks x 64 columns, so the epilogue of one
-// unit runs while the next is computed) and kStA A stages of 2 blocks x 32 columns (128 lanes x 64 k of f16).
+// unit runs while the next is computed) and kStA A stages of 2 blocks x kKC / 2 columns (128 lanes x kKC k of f16).
 // Shared memory holds only the input-row ring, the record ring and the epilogue's staging. Every wait is bounded
 // (then the error word is set); TMEM is freed by the allocating warp before the CTA exits on every path.
 #include <cuda.h>
@@ -45,13 +45,19 @@ constexpr int kDecWarps = 16 / kDecTn;               // 16 / kDecTn: 4 / kDecTn 
 constexpr int kTcWarps = kDecWarp0 + kDecWarps;      // 27
 constexpr int kTcThreads = kTcWarps * 32;           // 864
 constexpr int kNT = 64;                              // sorted rows a unit (the MMA's N)
-constexpr int kKC = 64;                              // k a pipeline chunk (one SWIZZLE_128B atom wide)
-constexpr int kStA = 4;                              // A stages (tensor memory)
-constexpr int kStB = 6;                              // input-row stages (shared memory)
-constexpr int kBTile = kNT * kKC * 2;                // one half's B chunk: 8 KB
+constexpr int kBox = 64;                             // k of one TMA box = one SWIZZLE_128B atom row (128 B)
+#ifndef EXL3B_TC_KC
+#define EXL3B_TC_KC 128
+#endif
+constexpr int kKC = EXL3B_TC_KC;                     // k a pipeline chunk: one handoff between the roles
+constexpr int kKT = kKC / 16;                        // k tiles a chunk
+constexpr int kNBox = kKC / kBox;                    // boxes a half of a chunk
+constexpr int kStA = kKC == 64 ? 4 : 2;              // A stages (tensor memory)
+constexpr int kBTile = kNT * kBox * 2;               // one box of input rows: 8 KB
+constexpr int kBHalf = kNBox * kBTile;               // one half's input rows of a chunk
 constexpr int kEpiCols = 128 + 4;                    // staging row (f32), padded
 constexpr int kAccCols = 2 * 2 * kNT;                // 256: two units x two blocks
-constexpr int kAStageCols = 2 * kKC / 2;             // 64: two blocks x 64 k of f16 (two a 32-bit column)
+constexpr int kAStageCols = 2 * kKC / 2;             // two blocks x kKC k of f16 (two a 32-bit column)
 constexpr int kTmemCols = 512;
 constexpr int kUnitTab = 160;                        // a CTA's units held in a shared table (more: looked up)
 static_assert(kAccCols + kStA * kAStageCols <= kTmemCols, "tensor memory");
@@ -60,9 +66,11 @@ template <int BITS>
 struct TcCfg {
     static constexpr int TILE_BYTES = 32 * BITS;                 // one 16x16 tile of the record
     static constexpr int REC_ROW = 8 * TILE_BYTES;               // one block's 8 tiles of one k row
-    static constexpr int REC_STAGE = 4 * 2 * REC_ROW;            // [tk 4][blk 2][8 tiles]
-    // the record ring runs deep (the rows are small, latency-bound reads): 4..12 stages within 64 KB
-    static constexpr int ST_R = (64 * 1024 / REC_STAGE) < 4 ? 4 : (64 * 1024 / REC_STAGE) > 12 ? 12 : (64 * 1024 / REC_STAGE);
+    static constexpr int REC_STAGE = kKT * 2 * REC_ROW;          // [tk][blk 2][8 tiles]
+    // the record ring runs deep (the rows are small, latency-bound reads): 3..12 stages within 64 KB
+    static constexpr int ST_R = (64 * 1024 / REC_STAGE) < 3 ? 3 : (64 * 1024 / REC_STAGE) > 12 ? 12 : (64 * 1024 / REC_STAGE);
+    // input-row stages: as many as shared memory leaves beside the record ring
+    static constexpr int ST_B = kKC == 64 ? 6 : (BITS >= 6 ? 3 : 4);
 };
 
 // ------------------------------------------------------------------------------------------ smem descriptors
@@ -160,8 +168,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     // 1024-byte alignment of every swizzled tile
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t* b_ring = smem;                                        // [kStB][2][8 KB]
-    uint8_t* r_ring = b_ring + kStB * 2 * kBTile;                  // [ST_R][REC_STAGE]
+    constexpr int kStB = Cfg::ST_B;
+    uint8_t* b_ring = smem;                                        // [kStB][half 2][box kNBox][8 KB]
+    uint8_t* r_ring = b_ring + kStB * 2 * kBHalf;                  // [ST_R][REC_STAGE]
     float* epi = reinterpret_cast<float*>(r_ring + Cfg::ST_R * Cfg::REC_STAGE);   // [2][16][kEpiCols]
     uint64_t* bars = reinterpret_cast<uint64_t*>(epi + 2 * 16 * kEpiCols);
     uint64_t* a_full = bars;                 // decoders -> MMA (count kDecWarps): an A stage is in tensor memory
@@ -270,8 +279,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     mbar_wait_warp(&r_empty[s], ph ^ 1, op.err);
                     mbar_expect_tx_el(&r_full[s], (uint32_t)Cfg::REC_STAGE);
 #pragma unroll
-                    for (int q = 0; q < 4; ++q) {
-                        const int64_t tk = (int64_t)ck * 4 + q;
+                    for (int q = 0; q < kKT; ++q) {
+                        const int64_t tk = (int64_t)ck * kKT + q;
                         uint8_t* dst = r_ring + s * Cfg::REC_STAGE + q * 2 * Cfg::REC_ROW;
                         if (GU) {
 #pragma unroll
@@ -290,11 +299,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 for (int ck = 0; ck < nck; ++ck, ++bi) {
                     const uint32_t s = bi % kStB, ph = (bi / kStB) & 1;
                     mbar_wait_warp(&b_empty[s], ph ^ 1, op.err);
-                    mbar_expect_tx_el(&b_full[s], (uint32_t)((GU ? 2 : 1) * kBTile));
+                    mbar_expect_tx_el(&b_full[s], (uint32_t)((GU ? 2 : 1) * kBHalf));
 #pragma unroll
                     for (int m = 0; m < (GU ? 2 : 1); ++m)
-                        tma_tile_g2s_el(b_ring + (s * 2 + m) * kBTile, &tmap, (int)(m * ev.C + ck * kKC), (int)u.r0,
-                                        &b_full[s]);
+#pragma unroll
+                        for (int bx = 0; bx < kNBox; ++bx)
+                            tma_tile_g2s_el(b_ring + (s * 2 + m) * kBHalf + bx * kBTile, &tmap,
+                                            (int)(m * ev.C + ck * kKC + bx * kBox), (int)u.r0, &b_full[s]);
                 }
             }
         }
@@ -320,13 +331,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 mbar_wait2_warp(&a_full[sa], pa, &b_full[sb], pb, op.err);
                 tc_fence_after();
                 const uint32_t ta = tmem + kAccCols + sa * kAStageCols;
-                const uint64_t db = b_desc0 + (uint64_t)((sb * 2 * kBTile) >> 4);
+                const uint64_t db = b_desc0 + (uint64_t)((sb * 2 * kBHalf) >> 4);
 #pragma unroll
                 for (int blk = 0; blk < 2; ++blk)
 #pragma unroll
-                    for (int ks = 0; ks < kKC / 16; ++ks)
+                    for (int ks = 0; ks < kKT; ++ks)
                         umma_f16_ts_el(d + blk * kNT, ta + blk * (kKC / 2) + ks * 8,
-                                       db + (uint64_t)(((GU ? blk : 0) * kBTile + ks * 32) >> 4), (ck | ks) ? 1u : 0u);
+                                       db + (uint64_t)(((GU ? blk : 0) * kBHalf + (ks / 4) * kBTile + (ks % 4) * 32) >> 4),
+                                       (ck | ks) ? 1u : 0u);
                 umma_commit_el(&a_empty[sa]);
                 umma_commit_el(&b_empty[sb]);
                 ++ai;
@@ -361,7 +373,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 #pragma unroll
                 for (int tt = 0; tt < kDecTn; ++tt)
 #pragma unroll
-                    for (int tk = 0; tk < 4; ++tk) {
+                    for (int tk = 0; tk < kKT; ++tk) {
                         uint32_t b[4];
                         decode_tile<BITS, CB>(rst + tk * 2 * Cfg::REC_ROW + tt * Cfg::TILE_BYTES, ld, b);
                         tmem_st_16x128b_x2(ta + ((uint32_t)(16 * tt) << 16) + tk * 8, b[0], b[2], b[1], b[3]);
@@ -540,10 +552,11 @@ static EncodeTiledFn encode_fn() {
 }
 
 int64_t exl3b_tc_smem_bytes(int bits) {
-    const int64_t rec_stage = 4 * 2 * 8 * 32 * bits;
+    const int64_t rec_stage = (int64_t)kKT * 2 * 8 * 32 * bits;
     int64_t st_r = 64 * 1024 / rec_stage;
-    st_r = st_r < 4 ? 4 : st_r > 12 ? 12 : st_r;
-    const int64_t b = (int64_t)kStB * 2 * kBTile + st_r * rec_stage + 2 * 16 * kEpiCols * 4 + 512;
+    st_r = st_r < 3 ? 3 : st_r > 12 ? 12 : st_r;
+    const int64_t st_b = kKC == 64 ? 6 : (bits >= 6 ? 3 : 4);
+    const int64_t b = st_b * 2 * kBHalf + st_r * rec_stage + 2 * 16 * kEpiCols * 4 + 512;
     return 1024 + b;   // the alignment slack; the unit prefix follows (added by the caller)
 }
 
@@ -555,7 +568,7 @@ static int make_map(CUtensorMap* map, const void* base, int64_t rows, int64_t co
     if ((reinterpret_cast<uintptr_t>(base) & 15) || (pitch * 2) % 16) return -3;
     const cuuint64_t dims[2] = { (cuuint64_t)cols, (cuuint64_t)rows };
     const cuuint64_t strides[1] = { (cuuint64_t)(pitch * 2) };
-    const cuuint32_t box[2] = { (cuuint32_t)kKC, (cuuint32_t)kNT };
+    const cuuint32_t box[2] = { (cuuint32_t)kBox, (cuuint32_t)kNT };
     const cuuint32_t estr[2] = { 1, 1 };
     const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
