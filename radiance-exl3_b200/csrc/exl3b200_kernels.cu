@@ -180,20 +180,19 @@ __global__ void __launch_bounds__(kPrepWarps * 32) k_prep(const Exl3bOp op, uint
         const uint16_t* s0 = static_cast<const uint16_t*>(tab_entry(op.cls[ev.c].suh, ev.j));
         const uint16_t* s1 = gu ? static_cast<const uint16_t*>(tab_entry(op.cls[ev.c].suh1, ev.j)) : s0;
         const bool svec = al16(s0) && al16(s1);
+        // the two halves one after the other: 16 values live a lane, 4 CTAs an SM
         uint32_t hx[8], hs[8];
-        float va[16], vb[16];
+        float va[16];
         ld16(src + c, xvec, hx);
         ld16(s0 + c, svec, hs);
         scale16(hx, hs, bf, va);
+        had128_x16(va, l8);
+        if (mine) st16f(y + c, yvec, va);
         if (gu) {
             ld16(s1 + c, svec, hs);
-            scale16(hx, hs, bf, vb);
-        }
-        had128_x16(va, l8);
-        if (gu) had128_x16(vb, l8);
-        if (mine) {
-            st16f(y + c, yvec, va);
-            if (gu) st16f(y + ev.C + c, yvec, vb);
+            scale16(hx, hs, bf, va);
+            had128_x16(va, l8);
+            if (mine) st16f(y + ev.C + c, yvec, va);
         }
     }
 }
