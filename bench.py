@@ -192,7 +192,7 @@ def bench_ours(args, rank, world, local_rank):
     if world > 1:
         from exl3b200.ep import EpLayer
         layer = EpLayer(plugin, rank=rank, world=world, n_expert=E, hidden=H, width=W, top_k=TOPK, bits_gu=KGU,
-                        bits_dn=KDN, codebook=CB, max_tokens=T, seed=1 + rank)
+                        bits_dn=KDN, codebook=CB, max_tokens=T, seed=1 + rank, transport=args.transport)
     else:
         layer = MoeLayer(plugin, n_expert=E, hidden=H, width=W, top_k=TOPK, bits_gu=KGU, bits_dn=KDN, codebook=CB,
                          max_tokens=T, seed=1)
@@ -247,7 +247,6 @@ def bench_ours(args, rank, world, local_rank):
                            for i in range(len(layer.PHASES))], device=dev)
         torch.distributed.all_reduce(ph, op=torch.distributed.ReduceOp.MAX)
         ep_phases = {n: round(float(v), 4) for n, v in zip(layer.PHASES, ph.cpu())}
-        ep_phases["exchange_bytes_rank0"] = layer.exchange_bytes()
     live = layer.live_experts()
     gu_b, dn_b = layer.expert_bytes()
     tokens_total = T * world
@@ -386,6 +385,13 @@ def bench_ours(args, rank, world, local_rank):
         except Exception as exc:  # the reference library is absent on this box
             cpu = {"value": None, "unit": "tokens/s", "cores": 0, "kind": "reference", "sample": f"unavailable: {exc}"}
 
+    if world > 1:
+        layer.check()
+        exch = layer.exchange_bytes()
+        if ep_phases is not None:
+            ep_phases["exchange_bytes_rank0"] = exch
+            ep_phases["transport"] = args.transport
+        layer.close()          # collective: every rank releases its peer-memory window
     if rank != 0:
         return None
     flops = layer.expert_flops(T * TOPK) * world
@@ -395,7 +401,7 @@ def bench_ours(args, rank, world, local_rank):
         "vs_baseline": None, "dtype": "fp16 operands (decoded trellis), f32 accumulate", "data": "synthetic",
         "config": {"workload": WORKLOAD, "tokens_per_gpu": T, "n_expert": E, "hidden": H, "width": W, "top_k": TOPK,
                    "bits": {"gate_up": KGU, "down": KDN}, "codebook": CB,
-                   "parallelism": f"ep{world}" if world > 1 else "single",
+                   "parallelism": f"ep{world} ({args.transport})" if world > 1 else "single",
                    "l2": "no flush: the packed weights (679 MB) exceed the 126 MB L2 and stream every step",
                    "inputs": "codes uniform random record words, suh +-1, svh +-|N(0,1)|*0.02, x and logits N(0,1)"},
         "hbm_gbs_per_chip": round(step_bytes / (ms / 1e3) / 1e9, 1),
@@ -424,6 +430,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--tokens", type=int, default=2048)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--transport", default="p2p", choices=["p2p", "nccl"],
+                    help="N > 1: the expert-parallel exchange over peer memory (default) or NCCL all-to-alls")
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")

@@ -127,6 +127,47 @@ int     exl3b200_ep_pack_dedup(const uint16_t* x, int64_t x_pitch, const int32_t
                                int32_t* row_tok, int32_t* counts, void* stream);
 int     exl3b200_ep_unpack(const uint32_t* meta, int64_t n_pairs, const int32_t* recv_counts, int64_t world,
                            int32_t* expert, int32_t* row, void* stream);
+/* ep_pack_dedup's first step alone (send_meta, row_tok, counts; no rows copied): for the peer-memory dispatch. */
+int     exl3b200_ep_dedup_scan(const int32_t* ids, int64_t top_k, const int32_t* sorted_pairs, const int32_t* dest_off,
+                               int64_t n_pairs, int64_t n_local, int64_t world, uint32_t* send_meta, int32_t* row_tok,
+                               int32_t* counts, void* stream);
+
+/* Expert parallelism over peer memory (no collective library on the data path). Each rank owns a "window",
+ * allocated here (device memory, zeroed) and exported by a 64-byte CUDA IPC handle that every other rank maps.
+ * Every window has the same layout, byte offsets offs[5] = {rows, meta, yback, ctl, done}:
+ *   rows  [world][t_cap][hidden] f16, meta [world][p_cap] u32   what each source sent here (its own segment)
+ *   yback [p_cap][hidden] bf16                                    the down row of each pair this rank sent
+ *   ctl   [world][8] u32, done [2] u32                            epoch flags and counts; last-block counters
+ * peers[world] = every rank's window base as this rank maps it (its own for itself).
+ *   p2p_dispatch:      after ep_dedup_scan: pair metas and the deduplicated token rows straight into the owners'
+ *                      windows, then each owner's dispatch flag (epoch) with the counts.
+ *   p2p_wait_dispatch: waits (at most 5 s) for every source's flag; hdr[3s .. 3s+2] = rows, pairs, base of source
+ *                      s; hdr[3 world] = 0, or -1 if a wait gave up (the error word is set too).
+ *   p2p_unpack:        the received pairs (source-major): local expert, row in the window's rows, and where the
+ *                      pair's down row returns (source rank, position).
+ *   p2p_combine:       each sorted down row straight into its source's yback, then each source's combine flag.
+ *   p2p_wait_combine:  waits (at most 5 s) for every owner's combine flag; status[0] = 0 or -1.
+ * Ranks call the same steps with the same epoch (1, 2, ...). No counterpart in the reference (one device). */
+int     exl3b200_ep_window_alloc(int64_t bytes, void** ptr);
+int     exl3b200_ep_window_free(void* ptr);
+int     exl3b200_ep_window_handle(void* ptr, void* handle64);
+int     exl3b200_ep_window_open(const void* handle64, void** ptr);
+int     exl3b200_ep_window_close(void* ptr);
+int     exl3b200_p2p_dispatch(const uint16_t* x, int64_t x_pitch, const int32_t* row_tok, const uint32_t* meta,
+                              const int32_t* dest_off, const int32_t* counts, int64_t n_slots, const uint64_t* peers,
+                              const int64_t* offs, int64_t self, int64_t world, int64_t t_cap, int64_t p_cap,
+                              int64_t hidden, uint32_t epoch, void* stream);
+int     exl3b200_p2p_wait_dispatch(void* own, const int64_t* offs, int64_t world, uint32_t epoch, int32_t* hdr,
+                                   void* stream);
+int     exl3b200_p2p_unpack(const void* own, const int64_t* offs, const int32_t* hdr, int64_t world, int64_t t_cap,
+                            int64_t p_cap, int64_t n_pairs, int32_t* expert, int32_t* row, int32_t* dst_rank,
+                            int32_t* dst_pos, void* stream);
+int     exl3b200_p2p_combine(const uint16_t* y_rows, int64_t y_pitch, const int32_t* sorted_pair, int64_t n_rows,
+                             const int32_t* dst_rank, const int32_t* dst_pos, const uint64_t* peers,
+                             const int64_t* offs, int64_t self, int64_t world, int64_t p_cap, int64_t hidden,
+                             uint32_t epoch, void* stream);
+int     exl3b200_p2p_wait_combine(const void* own, const int64_t* offs, int64_t world, uint32_t epoch,
+                                  int32_t* status, void* stream);
 int     exl3b200_ep_map(const int32_t* idx, int64_t n, const int32_t* table, int64_t n_table, int32_t* out,
                         void* stream);
 

@@ -221,6 +221,18 @@ int exl3b200_ep_pack_dedup(const uint16_t* x, int64_t x_pitch, const int32_t* id
     return cudaGetLastError() == cudaSuccess ? 0 : -6;
 }
 
+int exl3b200_ep_dedup_scan(const int32_t* ids, int64_t top_k, const int32_t* sorted_pairs, const int32_t* dest_off,
+                           int64_t n_pairs, int64_t n_local, int64_t world, uint32_t* send_meta, int32_t* row_tok,
+                           int32_t* counts, void* stream) {
+    if (!ids || !sorted_pairs || !dest_off || !send_meta || !row_tok || !counts) return -12;
+    if (top_k < 1 || n_local < 1 || n_local > 4096 || world < 1 || world > 65535 || n_pairs < 0 ||
+        n_pairs / top_k >= ((int64_t)1 << 20))
+        return -12;
+    k_ep_dedup_scan<<<(unsigned)world, kDedupThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+        ids, (int)top_k, sorted_pairs, dest_off, (int)n_local, send_meta, row_tok, counts);
+    return cudaGetLastError() == cudaSuccess ? 0 : -6;
+}
+
 int exl3b200_ep_unpack(const uint32_t* meta, int64_t n_pairs, const int32_t* recv_counts, int64_t world,
                        int32_t* expert, int32_t* row, void* stream) {
     if (!meta || !recv_counts || !expert || !row || n_pairs < 0 || world < 1) return -12;

@@ -23,6 +23,8 @@ the number of ranks. The all-to-alls move bf16/fp16 rows bit for bit (as float16
 
 `ops` supplies the device steps: `DeviceOps` (the library, CUDA tensors, NCCL) or a host stand-in with the same
 methods for testing the exchange on CPU ranks over gloo."""
+import ctypes as C
+
 import numpy as np
 
 
@@ -79,8 +81,8 @@ class DeviceOps:
     def map(self, idx, n, table, n_table, out):
         self.nat.ep_map(idx.data_ptr(), n, table.data_ptr(), n_table, out.data_ptr(), self._stream())
 
-    def experts(self, recv_x, n_rows, n_pairs, events=None):
-        self.local.experts(n_rows, n_pairs, self._stream(), x_ptr=recv_x.data_ptr(), top_k=1, M=n_rows,
+    def experts(self, recv_x, n_rows, n_pairs, events=None, x_ptr=None):
+        self.local.experts(n_rows, n_pairs, self._stream(), x_ptr=x_ptr or recv_x.data_ptr(), top_k=1, M=n_rows,
                            events=events)
 
     def rows_scatter(self, src, idx, n_rows, dst, n_dst):
@@ -88,10 +90,10 @@ class DeviceOps:
         self.nat.rows_scatter(src.data_ptr(), rb, idx.data_ptr(), n_rows, rb, dst.data_ptr(),
                               dst.shape[1] * dst.element_size(), n_dst, self._stream())
 
-    def gather(self, rows, sorted_pairs, n_rows, w, T, k, out):
-        work = self._work(("gather", k), self.nat.gather_work_bytes(w.numel() // k, k), rows.device)
-        self.nat.moe_gather(rows.data_ptr(), rows.shape[1], sorted_pairs.data_ptr(), n_rows, w.data_ptr(), T, k,
-                            out.shape[1], out.data_ptr(), work.data_ptr(), self._stream())
+    def gather(self, rows, sorted_pairs, n_rows, w, T, k, out, rows_ptr=None):
+        work = self._work(("gather", k), self.nat.gather_work_bytes(w.numel() // k, k), out.device)
+        self.nat.moe_gather(rows_ptr or rows.data_ptr(), out.shape[1], sorted_pairs.data_ptr(), n_rows,
+                            w.data_ptr(), T, k, out.shape[1], out.data_ptr(), work.data_ptr(), self._stream())
 
     def kernels(self, T, k, E, R):
         """How many of the library's kernels one step launches: router, ep_dest, rank scatter, the two pack
@@ -104,12 +106,53 @@ class DeviceOps:
         return n + 2
 
 
+class P2pWindow:
+    """This rank's peer-memory window (exl3b200_ep_window_*: device memory exported by CUDA IPC) and every peer's,
+    mapped here. Layout (the same on every rank, byte offsets): rows [world][t_cap][H] f16 | meta [world][p_cap]
+    u32 | yback [p_cap][H] bf16 | ctl [world][8] u32 | done [2] u32."""
+
+    def __init__(self, nat, dist, group, rank, world, t_cap, p_cap, hidden, device):
+        import torch
+        al = lambda n: (n + 255) // 256 * 256  # noqa: E731
+        self.nat, self.dist, self.group, self.rank, self.world = nat, dist, group, rank, world
+        o_rows = 0
+        o_meta = al(world * t_cap * hidden * 2)
+        o_yback = o_meta + al(world * p_cap * 4)
+        o_ctl = o_yback + al(p_cap * hidden * 2)
+        o_done = o_ctl + al(world * 32)
+        self.offs = (C.c_int64 * 5)(o_rows, o_meta, o_yback, o_ctl, o_done)
+        self.base = nat.window_alloc(o_done + 256)
+        handles = [None] * world
+        dist.all_gather_object(handles, nat.window_handle(self.base), group=group)
+        self.ptrs = [self.base if r == rank else nat.window_open(handles[r]) for r in range(world)]
+        self.peers = torch.tensor(self.ptrs, dtype=torch.int64, device=device)
+        dist.barrier(group=group)
+
+    def rows_ptr(self):
+        return self.base + self.offs[0]
+
+    def yback_ptr(self):
+        return self.base + self.offs[2]
+
+    def close(self):
+        """Collective: unmap the peers' windows, then (after every rank has) free this one."""
+        if self.base is None:
+            return
+        for r, p in enumerate(self.ptrs):
+            if r != self.rank:
+                self.nat.window_close(p)
+        self.dist.barrier(group=self.group)
+        self.nat.window_free(self.base)
+        self.base = None
+
+
 class EpLayer:
     """The routed-MoE layer over `world` ranks. Buffers are sized for the largest step: this rank sends at most
     max_tokens * top_k rows and receives at most world times that (every rank routing everything here)."""
 
     def __init__(self, plugin=None, *, rank, world, n_expert, hidden, width, top_k, bits_gu=3, bits_dn=4,
-                 codebook="mul1", max_tokens=2048, seed=0, group=None, device="cuda", ops=None, full=None):
+                 codebook="mul1", max_tokens=2048, seed=0, group=None, device="cuda", ops=None, full=None,
+                 transport="nccl"):
         import torch
         import torch.distributed as dist
         if n_expert % world:
@@ -145,6 +188,18 @@ class EpLayer:
         self.out = e(max_tokens, H, dt=f32)
         self.sorted_row, self.off_loc, self.y_rows = ops.local_buffers()
         self.last = {"R": 0, "sent": 0}
+        if transport not in ("nccl", "p2p"):
+            raise ValueError(f"transport {transport!r}")
+        self.transport, self.win, self.epoch = transport, None, 0
+        if transport == "p2p":
+            # peer-memory exchange: rows and metas straight into the owners' windows, down rows straight back
+            self.nat = ops.nat
+            self.win = P2pWindow(self.nat, dist, group, rank, world, max_tokens, P, H, dev)
+            self.dest_off_p = e(world + 1, dt=i32)
+            self.counts_p = e(2 * world, dt=i32)
+            self.hdr_p = torch.zeros(3 * world + 1, dtype=i32, device=dev)
+            self.status_p = torch.zeros(1, dtype=i32, device=dev)
+            self.dst_rank, self.dst_pos = e(self.Rcap, dt=i32), e(self.Rcap, dt=i32)
 
     # ------------------------------------------------------------------ the exchange
     def _a2a(self, out, inp, out_splits, in_splits):
@@ -167,6 +222,8 @@ class EpLayer:
         x = self.x if x is None else x
         logits = self.logits if logits is None else logits
         out = self.out if out is None else out
+        if self.transport == "p2p":
+            return self._forward_p2p(T, events, phases, x, logits, out)
         o, G, k, P = self.ops, self.G, self.k, T * self.k
         mark = (lambda i: phases[i].record()) if phases else (lambda i: None)
         mark(0)
@@ -198,6 +255,58 @@ class EpLayer:
         self.last = {"R": R, "rows_recv": Rr, "sent": S, "rows_sent": sum(rows_s), "send_counts": pairs_s,
                      "recv_counts": pairs_r, "send_rows": rows_s, "recv_rows": rows_r}
 
+    def _forward_p2p(self, T, events, phases, x, logits, out):
+        """The same step with the exchange over peer memory: no collective, one host read (the received counts)."""
+        o, nat, win, G, k, P = self.ops, self.nat, self.win, self.G, self.k, T * self.k
+        st = o._stream()
+        self.epoch += 1
+        ep = self.epoch & 0xFFFFFFFF
+        mark = (lambda i: phases[i].record()) if phases else (lambda i: None)
+        mark(0)
+        o.router(logits, T, self.E, k, self.ids, self.w)
+        o.dest(self.ids, P, self.nl, G, self.dest)
+        o.scatter(self.dest, P, G, self.sorted_pairs[:P], self.dest_off_p)
+        nat.ep_dedup_scan(self.ids.data_ptr(), k, self.sorted_pairs.data_ptr(), self.dest_off_p.data_ptr(), P,
+                          self.nl, G, self.send_meta.data_ptr(), self.row_tok.data_ptr(), self.counts_p.data_ptr(), st)
+        mark(1)
+        nat.p2p_dispatch(x.data_ptr(), x.shape[1], self.row_tok.data_ptr(), self.send_meta.data_ptr(),
+                         self.dest_off_p.data_ptr(), self.counts_p.data_ptr(), P, win.peers.data_ptr(), win.offs,
+                         self.rank, G, self.max_tokens, self.max_tokens * k, self.H, ep, st)
+        nat.p2p_wait_dispatch(win.base, win.offs, G, ep, self.hdr_p.data_ptr(), st)
+        h = self.hdr_p.cpu().tolist()            # the received counts: the one host read of a step
+        if h[3 * G] != 0:
+            raise RuntimeError("expert parallelism: a peer's dispatch did not arrive within the wait limit")
+        rows_r, pairs_r = h[0:3 * G:3], h[1:3 * G:3]
+        R, Rr = sum(pairs_r), sum(rows_r)
+        mark(2)
+        nat.p2p_unpack(win.base, win.offs, self.hdr_p.data_ptr(), G, self.max_tokens, self.max_tokens * k, R,
+                       self.pair_e.data_ptr(), self.pair_row.data_ptr(), self.dst_rank.data_ptr(),
+                       self.dst_pos.data_ptr(), st)
+        o.scatter(self.pair_e[:R], R, self.nl, self.sorted_pair[:R], self.off_loc)
+        o.map(self.sorted_pair, R, self.pair_row, R, self.sorted_row)
+        mark(3)
+        o.experts(None, G * self.max_tokens, R, events, x_ptr=win.rows_ptr())
+        mark(4)
+        nat.p2p_combine(self.y_rows.data_ptr(), self.H, self.sorted_pair.data_ptr(), R, self.dst_rank.data_ptr(),
+                        self.dst_pos.data_ptr(), win.peers.data_ptr(), win.offs, self.rank, G, self.max_tokens * k,
+                        self.H, ep, st)
+        nat.p2p_wait_combine(win.base, win.offs, G, ep, self.status_p.data_ptr(), st)
+        mark(5)
+        o.gather(None, self.sorted_pairs, P, self.w, T, k, out, rows_ptr=win.yback_ptr())
+        mark(6)
+        self.last = {"R": R, "rows_recv": Rr, "sent": P, "recv_counts": pairs_r, "recv_rows": rows_r, "p2p": True}
+
+    def check(self):
+        """Raise if a peer's combine never arrived in the last step (reads the status word: synchronises)."""
+        if self.transport == "p2p" and int(self.status_p.item()) != 0:
+            raise RuntimeError("expert parallelism: a peer's combine did not arrive within the wait limit")
+
+    def close(self):
+        """Collective: release the peer-memory window (p2p transport)."""
+        if self.win is not None:
+            self.win.close()
+            self.win = None
+
     # ------------------------------------------------------------------ accounting (this rank)
     def live_experts(self):
         off = self.off_loc.cpu().numpy()
@@ -209,6 +318,8 @@ class EpLayer:
     def time_prep_step(self, T, n=5):
         """The local pass's gate_up input rotation alone (ms), over the rows the last step received."""
         R, Rr = self.last["R"], self.last.get("rows_recv", self.last["R"])
+        if self.transport == "p2p":
+            return self.ops.local.time_prep(self.G * self.max_tokens, R, x_ptr=self.win.rows_ptr(), top_k=1, n=n)
         return self.ops.local.time_prep(Rr, R, x_ptr=self.recv_x.data_ptr(), top_k=1, n=n)
 
     def expert_flops(self, rows):
@@ -223,6 +334,13 @@ class EpLayer:
     def exchange_bytes(self):
         """Bytes this rank sent to other ranks in the last step: token rows and pair metas out, the down rows of the
         pairs it served back; what it keeps for itself excluded."""
+        if self.last.get("p2p"):
+            c = self.counts_p.cpu().tolist()     # rows, pairs sent to each rank
+            r = self.rank
+            rows_out = sum(c[0::2]) - c[2 * r]
+            metas_out = sum(c[1::2]) - c[2 * r + 1]
+            rows_back = self.last["R"] - self.last["recv_counts"][r]
+            return rows_out * 2 * self.H + metas_out * 4 + rows_back * 2 * self.H
         if "send_counts" not in self.last:
             return 0
         L, r = self.last, self.rank

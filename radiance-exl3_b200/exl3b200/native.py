@@ -29,6 +29,19 @@ class Native:
         L.exl3b200_ep_pack_dedup.argtypes = [_VP, _I64, _VP, _I64, _VP, _VP, _I64, _I64, _I64, _I64, _VP, _VP, _VP, _VP, _VP]
         L.exl3b200_ep_unpack.argtypes = [_VP, _I64, _VP, _I64, _VP, _VP, _VP]
         L.exl3b200_ep_map.argtypes = [_VP, _I64, _VP, _I64, _VP, _VP]
+        L.exl3b200_ep_dedup_scan.argtypes = [_VP, _I64, _VP, _VP, _I64, _I64, _I64, _VP, _VP, _VP, _VP]
+        L.exl3b200_ep_window_alloc.argtypes = [_I64, C.POINTER(_VP)]
+        L.exl3b200_ep_window_free.argtypes = [_VP]
+        L.exl3b200_ep_window_handle.argtypes = [_VP, _VP]
+        L.exl3b200_ep_window_open.argtypes = [_VP, C.POINTER(_VP)]
+        L.exl3b200_ep_window_close.argtypes = [_VP]
+        _U32 = C.c_uint32
+        L.exl3b200_p2p_dispatch.argtypes = [_VP, _I64, _VP, _VP, _VP, _VP, _I64, _VP, _VP, _I64, _I64, _I64, _I64,
+                                            _I64, _U32, _VP]
+        L.exl3b200_p2p_wait_dispatch.argtypes = [_VP, _VP, _I64, _U32, _VP, _VP]
+        L.exl3b200_p2p_unpack.argtypes = [_VP, _VP, _VP, _I64, _I64, _I64, _I64, _VP, _VP, _VP, _VP, _VP]
+        L.exl3b200_p2p_combine.argtypes = [_VP, _I64, _VP, _I64, _VP, _VP, _VP, _VP, _I64, _I64, _I64, _I64, _U32, _VP]
+        L.exl3b200_p2p_wait_combine.argtypes = [_VP, _VP, _I64, _U32, _VP, _VP]
 
     @staticmethod
     def _check(rc, what):
@@ -95,3 +108,54 @@ class Native:
 
     def ep_map(self, idx, n, table, n_table, out, stream=0):
         self._check(self.lib.exl3b200_ep_map(idx, n, table, n_table, out, stream), "exl3b200_ep_map")
+
+    def ep_dedup_scan(self, ids, top_k, sorted_pairs, dest_off, n_pairs, n_local, world, send_meta, row_tok, counts,
+                      stream=0):
+        self._check(self.lib.exl3b200_ep_dedup_scan(ids, top_k, sorted_pairs, dest_off, n_pairs, n_local, world,
+                                                    send_meta, row_tok, counts, stream), "exl3b200_ep_dedup_scan")
+
+    # ------------------------------------------------------------------ peer-memory windows
+    def window_alloc(self, nbytes):
+        p = C.c_void_p()
+        self._check(self.lib.exl3b200_ep_window_alloc(nbytes, C.byref(p)), "exl3b200_ep_window_alloc")
+        return p.value
+
+    def window_free(self, ptr):
+        self._check(self.lib.exl3b200_ep_window_free(ptr), "exl3b200_ep_window_free")
+
+    def window_handle(self, ptr):
+        buf = C.create_string_buffer(64)
+        self._check(self.lib.exl3b200_ep_window_handle(ptr, buf), "exl3b200_ep_window_handle")
+        return bytes(buf.raw)
+
+    def window_open(self, handle):
+        p = C.c_void_p()
+        buf = C.create_string_buffer(handle, 64)
+        self._check(self.lib.exl3b200_ep_window_open(buf, C.byref(p)), "exl3b200_ep_window_open")
+        return p.value
+
+    def window_close(self, ptr):
+        self._check(self.lib.exl3b200_ep_window_close(ptr), "exl3b200_ep_window_close")
+
+    def p2p_dispatch(self, x, x_pitch, row_tok, meta, dest_off, counts, n_slots, peers, offs, rank, world, t_cap,
+                     p_cap, hidden, epoch, stream=0):
+        self._check(self.lib.exl3b200_p2p_dispatch(x, x_pitch, row_tok, meta, dest_off, counts, n_slots, peers, offs,
+                                                   rank, world, t_cap, p_cap, hidden, epoch, stream),
+                    "exl3b200_p2p_dispatch")
+
+    def p2p_wait_dispatch(self, own, offs, world, epoch, hdr, stream=0):
+        self._check(self.lib.exl3b200_p2p_wait_dispatch(own, offs, world, epoch, hdr, stream),
+                    "exl3b200_p2p_wait_dispatch")
+
+    def p2p_unpack(self, own, offs, hdr, world, t_cap, p_cap, n_pairs, expert, row, dst_rank, dst_pos, stream=0):
+        self._check(self.lib.exl3b200_p2p_unpack(own, offs, hdr, world, t_cap, p_cap, n_pairs, expert, row, dst_rank,
+                                                 dst_pos, stream), "exl3b200_p2p_unpack")
+
+    def p2p_combine(self, y_rows, y_pitch, sorted_pair, n_rows, dst_rank, dst_pos, peers, offs, rank, world, p_cap,
+                    hidden, epoch, stream=0):
+        self._check(self.lib.exl3b200_p2p_combine(y_rows, y_pitch, sorted_pair, n_rows, dst_rank, dst_pos, peers, offs,
+                                                  rank, world, p_cap, hidden, epoch, stream), "exl3b200_p2p_combine")
+
+    def p2p_wait_combine(self, own, offs, world, epoch, status, stream=0):
+        self._check(self.lib.exl3b200_p2p_wait_combine(own, offs, world, epoch, status, stream),
+                    "exl3b200_p2p_wait_combine")

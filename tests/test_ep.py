@@ -342,11 +342,11 @@ def _ep_gpu_rank(rank, world, port, q):
         plugin = load_plugin()
         E, H, W, k = 64, 2048, 512, 8
         res = []
-        for T in (3, 256):
+        for T, transport in ((3, "nccl"), (256, "nccl"), (3, "p2p"), (256, "p2p")):
             full = MoeLayer(plugin, n_expert=E, hidden=H, width=W, top_k=k, bits_gu=3, bits_dn=4, max_tokens=T,
                             seed=7, device=dev)
             ep = EpLayer(plugin, rank=rank, world=world, n_expert=E, hidden=H, width=W, top_k=k, bits_gu=3,
-                         bits_dn=4, max_tokens=T, seed=7, device=dev, full=full)
+                         bits_dn=4, max_tokens=T, seed=7, device=dev, full=full, transport=transport)
             g = torch.Generator(device=dev)
             g.manual_seed(50 + rank + T)
             x = torch.randn((T, H), generator=g, device=dev).to(torch.float16)
@@ -354,14 +354,16 @@ def _ep_gpu_rank(rank, world, port, q):
             full.x[:T], full.logits[:T], ep.x[:T], ep.logits[:T] = x, lg, x, lg
             s = torch.cuda.current_stream().cuda_stream
             full.forward(T, s)
-            ep.forward(T, s)
-            ep.forward(T, s)
+            for _ in range(3):       # the windows and flags are reused step to step
+                ep.forward(T, s)
             torch.cuda.synchronize()
+            ep.check()
             a, b = full.out[:T].float(), ep.out[:T].float()
             err = float((a - b).abs().max())
             scale = float(a.abs().max())
             cos = float(torch.nn.functional.cosine_similarity(a.reshape(1, -1), b.reshape(1, -1)))
             res.append((T, bool(torch.equal(a, b)), err, scale, cos, full.band_name("down", T), ep.band_name("down", T)))
+            ep.close()
         q.put((rank, res))
     except Exception as exc:
         q.put((rank, repr(exc)))
@@ -373,8 +375,9 @@ def _ep_gpu_rank(rank, world, port, q):
 @pytest.mark.gpu
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs two GPUs")
 def test_ep_layer_over_nccl_equals_one_gpu():
-    """Two ranks, 32 experts each: the EP output equals the one-GPU layer's on the same tokens -- bit for bit where
-    both passes take the same band, within the ops' tolerance where the row counts put them in different bands."""
+    """Two ranks, 32 experts each, over NCCL and over peer memory: the EP output equals the one-GPU layer's on the
+    same tokens -- bit for bit where both passes take the same band, within the ops' tolerance where the row counts
+    put them in different bands."""
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
