@@ -43,7 +43,7 @@ __device__ __forceinline__ uint32_t cb_pair(uint32_t s0, uint32_t s1) {
         const uint32_t x0 = s0 * 0x83DCD12Du, x1 = s1 * 0x83DCD12Du;
         const uint32_t u0 = __dp4a(x0, 0x01010101u, 0x6400u);
         const uint32_t u1 = __dp4a(x1, 0x01010101u, 0x6400u);
-        const uint32_t h = __byte_perm(u0, u1, 0x5410);
+        const uint32_t h = u1 * 65536u + u0;   // the pair packed by an IMAD (FMA pipe): u0, u1 < 2^16
         const __half2 kinv = __halves2half2(__ushort_as_half(0x1EEE), __ushort_as_half(0x1EEE));
         const __half2 kbias = __halves2half2(__ushort_as_half(0xC931), __ushort_as_half(0xC931));
         const __half2 r = __hfma2(*reinterpret_cast<const __half2*>(&h), kinv, kbias);
@@ -115,7 +115,14 @@ __device__ __forceinline__ void decode_tile(const uint8_t* __restrict__ tile, co
         const uint32_t hi = *reinterpret_cast<const uint32_t*>(tile + d.o0);
         const uint32_t lo = *reinterpret_cast<const uint32_t*>(tile + d.o1);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) st[j] = __funnelshift_r(lo, hi, 28 - 4 * j) & 0xFFFFu;
+        for (int j = 0; j < 8; ++j) {
+            // the windows that lie byte-aligned inside `lo` are one PRMT; the others a funnel shift and a mask
+            const int sh = 28 - 4 * j;
+            if (sh == 16) st[j] = __byte_perm(lo, 0u, 0x4432);
+            else if (sh == 8) st[j] = __byte_perm(lo, 0u, 0x4421);
+            else if (sh == 0) st[j] = __byte_perm(lo, 0u, 0x4410);
+            else st[j] = __funnelshift_r(lo, hi, sh) & 0xFFFFu;
+        }
     } else {
         const uint32_t wm1 = *reinterpret_cast<const uint32_t*>(tile + d.o0);
         const uint32_t wa = *reinterpret_cast<const uint32_t*>(tile + d.o1);
