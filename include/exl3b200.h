@@ -134,10 +134,11 @@ int     exl3b200_ep_dedup_scan(const int32_t* ids, int64_t top_k, const int32_t*
 
 /* Expert parallelism over peer memory (no collective library on the data path). Each rank owns a "window",
  * allocated here (device memory, zeroed) and exported by a 64-byte CUDA IPC handle that every other rank maps.
- * Every window has the same layout, byte offsets offs[5] = {rows, meta, yback, ctl, done}:
+ * Every window has the same layout, byte offsets offs[6] = {rows, meta, yback, ctl, done, sink}:
  *   rows  [world][t_cap][hidden] f16, meta [world][p_cap] u32   what each source sent here (its own segment)
  *   yback [p_cap][hidden] bf16                                    the down row of each pair this rank sent
  *   ctl   [world][8] u32, done [2] u32                            epoch flags and counts; last-block counters
+ *   sink  [H] bf16                                                where a row that would fall outside goes
  * peers[world] = every rank's window base as this rank maps it (its own for itself).
  *   p2p_dispatch:      after ep_dedup_scan: pair metas and the deduplicated token rows straight into the owners'
  *                      windows, then each owner's dispatch flag (epoch) with the counts.
@@ -147,6 +148,9 @@ int     exl3b200_ep_dedup_scan(const int32_t* ids, int64_t top_k, const int32_t*
  *                      pair's down row returns (source rank, position).
  *   p2p_combine:       each sorted down row straight into its source's yback, then each source's combine flag.
  *   p2p_wait_combine:  waits (at most 5 s) for every owner's combine flag; status[0] = 0 or -1.
+ *   The combine fused into down instead of p2p_combine: p2p_row_dst (each sorted row's destination address in
+ *   its source's window), exl3b200_moe_down_rows with that table (down's epilogue stores each row straight into
+ *   the source over NVLink, fenced at system scope), then p2p_signal_combine (the flags).
  * Ranks call the same steps with the same epoch (1, 2, ...). No counterpart in the reference (one device). */
 int     exl3b200_ep_window_alloc(int64_t bytes, void** ptr);
 int     exl3b200_ep_window_free(void* ptr);
@@ -168,6 +172,14 @@ int     exl3b200_p2p_combine(const uint16_t* y_rows, int64_t y_pitch, const int3
                              uint32_t epoch, void* stream);
 int     exl3b200_p2p_wait_combine(const void* own, const int64_t* offs, int64_t world, uint32_t epoch,
                                   int32_t* status, void* stream);
+int     exl3b200_p2p_row_dst(const int32_t* sorted_pair, int64_t n_rows, const int32_t* dst_rank,
+                             const int32_t* dst_pos, const uint64_t* peers, const int64_t* offs, int64_t self,
+                             int64_t world, int64_t p_cap, int64_t hidden, uint64_t* row_dst, void* stream);
+int     exl3b200_p2p_signal_combine(const uint64_t* peers, const int64_t* offs, int64_t self, int64_t world,
+                                    uint32_t epoch, void* stream);
+/* moe_exl3_down (same RadArgs and checks as the row's launch) writing output row i at row_dst[i] (a device table
+ * of row addresses, possibly in a peer's memory) instead of y + i * pitch. No counterpart in the reference. */
+int     exl3b200_moe_down_rows(const RadArgs* args, const uint64_t* row_dst, void* stream);
 int     exl3b200_ep_map(const int32_t* idx, int64_t n, const int32_t* table, int64_t n_table, int32_t* out,
                         void* stream);
 

@@ -321,6 +321,24 @@ __device__ __forceinline__ ExpertView expert_view(const Exl3bOp& op, int64_t e) 
     v.C = op.cls[v.c].cols;
     return v;
 }
+// Four bf16 values stored as one 8-byte word where the address allows (a row written over NVLink then moves in
+// full 256-byte warp stores), else one by one.
+__device__ __forceinline__ void st4_bf16(uint16_t* y, const float v[4]) {
+    const uint16_t b0 = f2bf(v[0]), b1 = f2bf(v[1]), b2 = f2bf(v[2]), b3 = f2bf(v[3]);
+    if ((reinterpret_cast<uintptr_t>(y) & 7) == 0) {
+        uint2 u;
+        u.x = (uint32_t)b0 | ((uint32_t)b1 << 16);
+        u.y = (uint32_t)b2 | ((uint32_t)b3 << 16);
+        *reinterpret_cast<uint2*>(y) = u;
+    } else {
+        y[0] = b0; y[1] = b1; y[2] = b2; y[3] = b3;
+    }
+}
+// Where output row i goes: y + i * pitch, or -- when the caller gave a row table (the expert-parallel combine
+// writing straight into the sources' memory) -- row_dst[i].
+__device__ __forceinline__ uint16_t* out_row(const Exl3bOp& op, int64_t i) {
+    return op.row_dst ? reinterpret_cast<uint16_t*>(op.row_dst[i]) : static_cast<uint16_t*>(op.y) + i * op.y_pitch;
+}
 __device__ __forceinline__ bool row_live(const Exl3bOp& op, int64_t i) {
     return i >= op.expert_offset[0] && i < op.expert_offset[op.n_expert] && op.sorted_tok[i] >= 0;
 }

@@ -225,6 +225,19 @@ static int launch_op(const RadArgs* a, RadStream s, int op) {
     return run_op(&k, a->scratch, a->scratch_bytes, s);
 }
 
+/* moe_exl3_down whose output row i is written at row_dst[i] (a device table of row addresses) instead of y + i*pitch:
+ * the expert-parallel combine fused into down -- each pair's row goes straight into its source rank's memory. The
+ * RadArgs are the down row's, checked the same way (the y operand still names the rows' dtype and width). */
+int exl3b200_moe_down_rows(const RadArgs* a, const uint64_t* row_dst, void* stream) {
+    Exl3bGeom g;
+    Exl3bOp k;
+    if (!a || !row_dst) return RAD_E_INVAL;
+    const int rc = build_op(a, EXL3B_DOWN, &g, &k);
+    if (rc != RAD_OK) return rc;
+    k.row_dst = row_dst;
+    return run_op(&k, a->scratch, a->scratch_bytes, stream);
+}
+
 static int64_t op_scratch(const RadArgs* a, int op) {
     Exl3bGeom g;
     Exl3bOp k;

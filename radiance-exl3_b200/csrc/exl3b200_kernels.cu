@@ -295,10 +295,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_skinny(const Exl3bOp op, i
         for (int64_t i = gcta; i < op.T; i += ncta) {
             if (row_live(op, i)) continue;
             if (GU) {
-                uint16_t* y = static_cast<uint16_t*>(op.y) + i * op.y_pitch;
+                uint16_t* y = out_row(op, i);
                 for (int64_t c = tid; c < op.y_cols; c += kThreads) y[c] = 0;
             } else {
-                uint16_t* y = static_cast<uint16_t*>(op.y) + i * op.y_pitch;
+                uint16_t* y = out_row(op, i);
                 for (int64_t c = tid; c < op.y_cols; c += kThreads) y[c] = 0;
             }
         }
@@ -327,7 +327,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_skinny(const Exl3bOp op, i
                 for (int m = warp; m < nr; m += kConsumerWarps) {
                     const int64_t i = r0 + m;
                     if (!row_live(op, i)) continue;
-                    uint16_t* y = static_cast<uint16_t*>(op.y) + i * op.y_pitch + blk * 128;
+                    uint16_t* y = out_row(op, i) + blk * 128;
                     for (int q = lane; q < 128; q += 32) y[q] = 0;
                 }
             continue;
@@ -490,7 +490,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_skinny(const Exl3bOp op, i
                         const float sg = __fmul_rn(gte, __frcp_rn(__fadd_rn(1.0f, expf(-gte))));
                         h[q] = __fmul_rn(sg, up);
                     }
-                    uint16_t* y = static_cast<uint16_t*>(op.y) + i * op.y_pitch + n0;
+                    uint16_t* y = out_row(op, i) + n0;
                     if (op.h_rot) {
                         const uint16_t* dn = static_cast<const uint16_t*>(tab_entry(cl.dn_suh, ev.j)) + blk * 128;
 #pragma unroll
@@ -501,11 +501,14 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_skinny(const Exl3bOp op, i
                     for (int q = 0; q < 4; ++q) y[q] = f2h(h[q]);
                 } else {
                     const int64_t n0 = blk * 128 + 4 * lane;
-                    uint16_t* y = static_cast<uint16_t*>(op.y) + i * op.y_pitch + n0;
+                    uint16_t* y = out_row(op, i) + n0;
+                    float o[4];
 #pragma unroll
-                    for (int q = 0; q < 4; ++q) y[q] = f2bf(__fmul_rn(v[0][q], h2f(svh[n0 + q])));
+                    for (int q = 0; q < 4; ++q) o[q] = __fmul_rn(v[0][q], h2f(svh[n0 + q]));
+                    st4_bf16(y, o);
                 }
             }
+            if (op.row_dst) __threadfence_system();   // rows in another GPU's memory: visible before the kernel ends
         }
         if (S > 1) cluster_sync_all(); else __syncthreads();
     }

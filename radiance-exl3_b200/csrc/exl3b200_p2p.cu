@@ -11,6 +11,7 @@
 //   ctl    [world][8] u32               from rank s: [0] dispatch epoch, [1] rows, [2] pairs, [3] the pairs' base in
 //                                       s's sorted order, [4] combine epoch
 //   done   [2] u32                      last-block counters of the dispatch and the combine kernels
+//   sink   [hidden] bf16                one spare row: where a row that would fall outside a window goes instead
 // A step: k_p2p_dispatch (rows + metas + counts, then the flag) -> k_p2p_wait_dispatch (every source's flag, bounded)
 // -> the local ops -> k_p2p_combine (each pair's down row to its source, then the flag) -> k_p2p_wait_combine.
 //
@@ -26,7 +27,7 @@ namespace {
 constexpr uint64_t kP2pWaitNs = 5000000000ull;   // a rank waits at most 5 s for its peers, then reports
 
 struct Win {
-    int64_t rows, meta, yback, ctl, done;      // byte offsets in every window
+    int64_t rows, meta, yback, ctl, done, sink;   // byte offsets in every window (sink: one spare row)
 };
 
 __device__ __forceinline__ uint64_t gtimer() {
@@ -208,6 +209,36 @@ __global__ void k_p2p_wait_combine(const uint8_t* own, Win w, int world, uint32_
     }
 }
 
+// The combine fused into down: row_dst[i] = where sorted row i's down row goes -- source s's yback at the pair's
+// position (an address in s's window as this rank maps it); a pair outside the windows goes to this rank's sink row
+// (error word set).
+__global__ void k_p2p_row_dst(const int32_t* __restrict__ sorted_pair, int64_t n_rows,
+                              const int32_t* __restrict__ dst_rank, const int32_t* __restrict__ dst_pos,
+                              const uint64_t* __restrict__ peers, Win w, int self, int world, int64_t p_cap,
+                              int64_t hidden, uint64_t* __restrict__ row_dst, int32_t* err) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n_rows) return;
+    const int32_t q = sorted_pair[i];
+    const int s = q >= 0 && q < n_rows ? dst_rank[q] : -1;
+    const int64_t pos = q >= 0 && q < n_rows ? dst_pos[q] : -1;
+    if (s < 0 || s >= world || pos < 0 || pos >= p_cap) {
+        atomicOr(err, 4);
+        row_dst[i] = peers[self] + (uint64_t)w.sink;
+        return;
+    }
+    row_dst[i] = peers[s] + (uint64_t)w.yback + (uint64_t)(pos * hidden * 2);
+}
+
+// After the down launch that wrote through the row table (its threads fenced their stores at system scope before
+// completing): every source's combine flag for this epoch.
+__global__ void k_p2p_signal_combine(const uint64_t* __restrict__ peers, Win w, int self, int world, uint32_t epoch) {
+    const int s = threadIdx.x;
+    if (s >= world) return;
+    __threadfence_system();
+    uint32_t* ctl = reinterpret_cast<uint32_t*>(wbase(peers, s) + w.ctl) + self * 8;
+    st_release_sys(&ctl[4], epoch);
+}
+
 inline bool al16(const void* p) { return ((uintptr_t)p & 15u) == 0; }
 constexpr int kWarps = 8;
 
@@ -263,7 +294,7 @@ int exl3b200_p2p_dispatch(const uint16_t* x, int64_t x_pitch, const int32_t* row
     int sm = 0;
     int32_t* err = nullptr;
     if (exl3b_cuda_device_info(&sm, &err) != 0) return -6;
-    const Win w = { offs[0], offs[1], offs[2], offs[3], offs[4] };
+    const Win w = { offs[0], offs[1], offs[2], offs[3], offs[4], offs[5] };
     k_p2p_dispatch<<<grid_for(n_slots, sm), kWarps * 32, 0, static_cast<cudaStream_t>(stream)>>>(
         reinterpret_cast<const uint4*>(x), x_pitch / 8, row_tok, meta, dest_off, counts, n_slots, peers, w, (int)self,
         (int)world, t_cap, p_cap, (int)(hidden / 8), epoch, err);
@@ -276,7 +307,7 @@ int exl3b200_p2p_wait_dispatch(void* own, const int64_t* offs, int64_t world, ui
     int sm = 0;
     int32_t* err = nullptr;
     if (exl3b_cuda_device_info(&sm, &err) != 0) return -6;
-    const Win w = { offs[0], offs[1], offs[2], offs[3], offs[4] };
+    const Win w = { offs[0], offs[1], offs[2], offs[3], offs[4], offs[5] };
     k_p2p_wait_dispatch<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(static_cast<uint8_t*>(own), w, (int)world,
                                                                         epoch, hdr, err);
     return cudaGetLastError() == cudaSuccess ? 0 : -6;
@@ -287,7 +318,7 @@ int exl3b200_p2p_unpack(const void* own, const int64_t* offs, const int32_t* hdr
                         int32_t* dst_pos, void* stream) {
     if (!own || !offs || !hdr || !expert || !row || !dst_rank || !dst_pos || world < 1 || n_pairs < 0) return -12;
     if (n_pairs == 0) return 0;
-    const Win w = { offs[0], offs[1], offs[2], offs[3], offs[4] };
+    const Win w = { offs[0], offs[1], offs[2], offs[3], offs[4], offs[5] };
     k_p2p_unpack<<<(unsigned)((n_pairs + 255) / 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
         static_cast<const uint8_t*>(own), w, hdr, (int)world, t_cap, p_cap, n_pairs, expert, row, dst_rank, dst_pos);
     return cudaGetLastError() == cudaSuccess ? 0 : -6;
@@ -302,10 +333,34 @@ int exl3b200_p2p_combine(const uint16_t* y_rows, int64_t y_pitch, const int32_t*
     int sm = 0;
     int32_t* err = nullptr;
     if (exl3b_cuda_device_info(&sm, &err) != 0) return -6;
-    const Win w = { offs[0], offs[1], offs[2], offs[3], offs[4] };
+    const Win w = { offs[0], offs[1], offs[2], offs[3], offs[4], offs[5] };
     k_p2p_combine<<<grid_for(n_rows, sm), kWarps * 32, 0, static_cast<cudaStream_t>(stream)>>>(
         reinterpret_cast<const uint4*>(y_rows), y_pitch / 8, sorted_pair, n_rows, dst_rank, dst_pos, peers, w,
         (int)self, (int)world, p_cap, (int)(hidden / 8), epoch, err);
+    return cudaGetLastError() == cudaSuccess ? 0 : -6;
+}
+
+int exl3b200_p2p_row_dst(const int32_t* sorted_pair, int64_t n_rows, const int32_t* dst_rank, const int32_t* dst_pos,
+                         const uint64_t* peers, const int64_t* offs, int64_t self, int64_t world, int64_t p_cap,
+                         int64_t hidden, uint64_t* row_dst, void* stream) {
+    if (!sorted_pair || !dst_rank || !dst_pos || !peers || !offs || !row_dst || world < 1 || world > 32 || self < 0 ||
+        self >= world || n_rows < 0 || hidden < 8)
+        return -12;
+    if (n_rows == 0) return 0;
+    int sm = 0;
+    int32_t* err = nullptr;
+    if (exl3b_cuda_device_info(&sm, &err) != 0) return -6;
+    const Win w = { offs[0], offs[1], offs[2], offs[3], offs[4], offs[5] };
+    k_p2p_row_dst<<<(unsigned)((n_rows + 255) / 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        sorted_pair, n_rows, dst_rank, dst_pos, peers, w, (int)self, (int)world, p_cap, hidden, row_dst, err);
+    return cudaGetLastError() == cudaSuccess ? 0 : -6;
+}
+
+int exl3b200_p2p_signal_combine(const uint64_t* peers, const int64_t* offs, int64_t self, int64_t world,
+                                uint32_t epoch, void* stream) {
+    if (!peers || !offs || world < 1 || world > 32 || self < 0 || self >= world) return -12;
+    const Win w = { offs[0], offs[1], offs[2], offs[3], offs[4], offs[5] };
+    k_p2p_signal_combine<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(peers, w, (int)self, (int)world, epoch);
     return cudaGetLastError() == cudaSuccess ? 0 : -6;
 }
 
@@ -315,7 +370,7 @@ int exl3b200_p2p_wait_combine(const void* own, const int64_t* offs, int64_t worl
     int sm = 0;
     int32_t* err = nullptr;
     if (exl3b_cuda_device_info(&sm, &err) != 0) return -6;
-    const Win w = { offs[0], offs[1], offs[2], offs[3], offs[4] };
+    const Win w = { offs[0], offs[1], offs[2], offs[3], offs[4], offs[5] };
     k_p2p_wait_combine<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(static_cast<const uint8_t*>(own), w,
                                                                        (int)world, epoch, status, err);
     return cudaGetLastError() == cudaSuccess ? 0 : -6;

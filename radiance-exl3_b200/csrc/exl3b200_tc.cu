@@ -254,9 +254,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const int64_t lo = op.expert_offset[0], hi = op.expert_offset[n_exp];
         for (int64_t i = (int64_t)blockIdx.x * nthr + lt; i < op.T; i += (int64_t)gridDim.x * nthr) {
             if (i >= lo && i < hi && op.sorted_tok[i] >= 0) continue;
-            uint16_t* y = static_cast<uint16_t*>(op.y) + i * op.y_pitch;
+            uint16_t* y = out_row(op, i);
             for (int64_t c = 0; c < op.y_cols; ++c) y[c] = 0;
         }
+        if (op.row_dst) __threadfence_system();
     }
 
     if (warp == kRecWarp || warp == kBWarp) {
@@ -405,7 +406,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 for (int m = 0; m < u.nr; ++m) {
                     const int64_t i = u.r0 + m;
                     if (op.sorted_tok[i] < 0) continue;
-                    uint16_t* y = static_cast<uint16_t*>(op.y) + i * op.y_pitch + c0;
+                    uint16_t* y = out_row(op, i) + c0;
                     for (int64_t c = tid; c < nc; c += kEpiWarps * 32) y[c] = 0;
                 }
                 continue;
@@ -451,7 +452,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     float a[4] = { av.x, av.y, av.z, av.w }, b[4] = { bv.x, bv.y, bv.z, bv.w };
                     had128_warp(a, lane);
                     had128_warp(b, lane);
-                    uint16_t* y = static_cast<uint16_t*>(op.y) + i * op.y_pitch + n0;
+                    uint16_t* y = out_row(op, i) + n0;
                     if (GU) {
                         float h[4];
 #pragma unroll
@@ -476,11 +477,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                             for (int e = 0; e < 4; ++e) y[e] = f2h(h[e]);
                         }
                     } else {
+                        float lo[4], hi[4];
 #pragma unroll
                         for (int e = 0; e < 4; ++e) {
-                            y[e] = f2bf(__fmul_rn(a[e], s0[e]));
-                            y[128 + e] = f2bf(__fmul_rn(b[e], s1[e]));
+                            lo[e] = __fmul_rn(a[e], s0[e]);
+                            hi[e] = __fmul_rn(b[e], s1[e]);
                         }
+                        st4_bf16(y, lo);
+                        st4_bf16(y + 128, hi);
                     }
                 }
                 asm volatile("bar.sync 2, %0;" ::"n"(kEpiWarps * 32) : "memory");
@@ -490,6 +494,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             if (lane == 0) mbar_arrive(&acc_empty[buf]);
             ++ui;
         }
+        // rows written through a row table may live in another GPU's memory: make them visible system-wide before
+        // this thread (and so the kernel) completes, ahead of whatever flag the caller raises next
+        if (op.row_dst) __threadfence_system();
     }
 
     tc_fence_before();

@@ -81,9 +81,9 @@ class DeviceOps:
     def map(self, idx, n, table, n_table, out):
         self.nat.ep_map(idx.data_ptr(), n, table.data_ptr(), n_table, out.data_ptr(), self._stream())
 
-    def experts(self, recv_x, n_rows, n_pairs, events=None, x_ptr=None):
+    def experts(self, recv_x, n_rows, n_pairs, events=None, x_ptr=None, down_row_dst=None):
         self.local.experts(n_rows, n_pairs, self._stream(), x_ptr=x_ptr or recv_x.data_ptr(), top_k=1, M=n_rows,
-                           events=events)
+                           events=events, down_row_dst=down_row_dst)
 
     def rows_scatter(self, src, idx, n_rows, dst, n_dst):
         rb = src.shape[1] * src.element_size()
@@ -109,7 +109,7 @@ class DeviceOps:
 class P2pWindow:
     """This rank's peer-memory window (exl3b200_ep_window_*: device memory exported by CUDA IPC) and every peer's,
     mapped here. Layout (the same on every rank, byte offsets): rows [world][t_cap][H] f16 | meta [world][p_cap]
-    u32 | yback [p_cap][H] bf16 | ctl [world][8] u32 | done [2] u32."""
+    u32 | yback [p_cap][H] bf16 | ctl [world][8] u32 | done [2] u32 | sink [H] bf16."""
 
     def __init__(self, nat, dist, group, rank, world, t_cap, p_cap, hidden, device):
         import torch
@@ -120,8 +120,9 @@ class P2pWindow:
         o_yback = o_meta + al(world * p_cap * 4)
         o_ctl = o_yback + al(p_cap * hidden * 2)
         o_done = o_ctl + al(world * 32)
-        self.offs = (C.c_int64 * 5)(o_rows, o_meta, o_yback, o_ctl, o_done)
-        self.base = nat.window_alloc(o_done + 256)
+        o_sink = o_done + 256
+        self.offs = (C.c_int64 * 6)(o_rows, o_meta, o_yback, o_ctl, o_done, o_sink)
+        self.base = nat.window_alloc(o_sink + al(hidden * 2))
         handles = [None] * world
         dist.all_gather_object(handles, nat.window_handle(self.base), group=group)
         self.ptrs = [self.base if r == rank else nat.window_open(handles[r]) for r in range(world)]
@@ -152,7 +153,7 @@ class EpLayer:
 
     def __init__(self, plugin=None, *, rank, world, n_expert, hidden, width, top_k, bits_gu=3, bits_dn=4,
                  codebook="mul1", max_tokens=2048, seed=0, group=None, device="cuda", ops=None, full=None,
-                 transport="nccl"):
+                 transport="nccl", fuse_combine=True):
         import torch
         import torch.distributed as dist
         if n_expert % world:
@@ -200,6 +201,9 @@ class EpLayer:
             self.hdr_p = torch.zeros(3 * world + 1, dtype=i32, device=dev)
             self.status_p = torch.zeros(1, dtype=i32, device=dev)
             self.dst_rank, self.dst_pos = e(self.Rcap, dt=i32), e(self.Rcap, dt=i32)
+            # the combine fused into down: each sorted row's destination in its source's window
+            self.fuse_combine = fuse_combine
+            self.row_dst = torch.empty(self.Rcap, dtype=torch.int64, device=dev)
 
     # ------------------------------------------------------------------ the exchange
     def _a2a(self, out, inp, out_splits, in_splits):
@@ -285,11 +289,22 @@ class EpLayer:
         o.scatter(self.pair_e[:R], R, self.nl, self.sorted_pair[:R], self.off_loc)
         o.map(self.sorted_pair, R, self.pair_row, R, self.sorted_row)
         mark(3)
-        o.experts(None, G * self.max_tokens, R, events, x_ptr=win.rows_ptr())
-        mark(4)
-        nat.p2p_combine(self.y_rows.data_ptr(), self.H, self.sorted_pair.data_ptr(), R, self.dst_rank.data_ptr(),
-                        self.dst_pos.data_ptr(), win.peers.data_ptr(), win.offs, self.rank, G, self.max_tokens * k,
-                        self.H, ep, st)
+        if self.fuse_combine:
+            # down's epilogue writes each pair's row straight into its source's window (NVLink stores overlapping
+            # the decode of the next units), then the flags
+            nat.p2p_row_dst(self.sorted_pair.data_ptr(), R, self.dst_rank.data_ptr(), self.dst_pos.data_ptr(),
+                            win.peers.data_ptr(), win.offs, self.rank, G, self.max_tokens * k, self.H,
+                            self.row_dst.data_ptr(), st)
+            o.experts(None, G * self.max_tokens, R, events, x_ptr=win.rows_ptr(),
+                      down_row_dst=self.row_dst.data_ptr() if R > 0 else None)
+            mark(4)
+            nat.p2p_signal_combine(win.peers.data_ptr(), win.offs, self.rank, G, ep, st)
+        else:
+            o.experts(None, G * self.max_tokens, R, events, x_ptr=win.rows_ptr())
+            mark(4)
+            nat.p2p_combine(self.y_rows.data_ptr(), self.H, self.sorted_pair.data_ptr(), R, self.dst_rank.data_ptr(),
+                            self.dst_pos.data_ptr(), win.peers.data_ptr(), win.offs, self.rank, G,
+                            self.max_tokens * k, self.H, ep, st)
         nat.p2p_wait_combine(win.base, win.offs, G, ep, self.status_p.data_ptr(), st)
         mark(5)
         o.gather(None, self.sorted_pairs, P, self.w, T, k, out, rows_ptr=win.yback_ptr())

@@ -162,7 +162,7 @@ class MoeLayer:
         return res
 
     # ------------------------------------------------------------------ one pass
-    def experts(self, T, rows, stream, x_ptr=None, top_k=None, M=None, events=None):
+    def experts(self, T, rows, stream, x_ptr=None, top_k=None, M=None, events=None, down_row_dst=None):
         """gate_up then down over the sorted rows already in sorted_tok / offset. `events`: three
         torch.cuda.Event recorded before gate_up, between the two and after down (on the current stream)."""
         if rows == 0:                 # nothing routed here: no launch, the events still mark the (empty) ops
@@ -177,9 +177,13 @@ class MoeLayer:
             raise RuntimeError(f"moe_exl3_gate_up launch: {rc}")
         if events:
             events[1].record()
-        rc = self.plugin.row("moe_exl3_down").launch(C.byref(a_dn), stream)
-        if rc != 0:
-            raise RuntimeError(f"moe_exl3_down launch: {rc}")
+        if down_row_dst:
+            # down writing each output row at its address in a device table (the expert-parallel combine)
+            self.native.moe_down_rows(C.addressof(a_dn), down_row_dst, stream)
+        else:
+            rc = self.plugin.row("moe_exl3_down").launch(C.byref(a_dn), stream)
+            if rc != 0:
+                raise RuntimeError(f"moe_exl3_down launch: {rc}")
         if events:
             events[2].record()
 

@@ -42,6 +42,9 @@ class Native:
         L.exl3b200_p2p_unpack.argtypes = [_VP, _VP, _VP, _I64, _I64, _I64, _I64, _VP, _VP, _VP, _VP, _VP]
         L.exl3b200_p2p_combine.argtypes = [_VP, _I64, _VP, _I64, _VP, _VP, _VP, _VP, _I64, _I64, _I64, _I64, _U32, _VP]
         L.exl3b200_p2p_wait_combine.argtypes = [_VP, _VP, _I64, _U32, _VP, _VP]
+        L.exl3b200_p2p_row_dst.argtypes = [_VP, _I64, _VP, _VP, _VP, _VP, _I64, _I64, _I64, _I64, _VP, _VP]
+        L.exl3b200_p2p_signal_combine.argtypes = [_VP, _VP, _I64, _I64, _U32, _VP]
+        L.exl3b200_moe_down_rows.argtypes = [_VP, _VP, _VP]
 
     @staticmethod
     def _check(rc, what):
@@ -159,3 +162,15 @@ class Native:
     def p2p_wait_combine(self, own, offs, world, epoch, status, stream=0):
         self._check(self.lib.exl3b200_p2p_wait_combine(own, offs, world, epoch, status, stream),
                     "exl3b200_p2p_wait_combine")
+
+    def p2p_row_dst(self, sorted_pair, n_rows, dst_rank, dst_pos, peers, offs, rank, world, p_cap, hidden, row_dst,
+                    stream=0):
+        self._check(self.lib.exl3b200_p2p_row_dst(sorted_pair, n_rows, dst_rank, dst_pos, peers, offs, rank, world,
+                                                  p_cap, hidden, row_dst, stream), "exl3b200_p2p_row_dst")
+
+    def p2p_signal_combine(self, peers, offs, rank, world, epoch, stream=0):
+        self._check(self.lib.exl3b200_p2p_signal_combine(peers, offs, rank, world, epoch, stream),
+                    "exl3b200_p2p_signal_combine")
+
+    def moe_down_rows(self, args_ref, row_dst, stream=0):
+        self._check(self.lib.exl3b200_moe_down_rows(args_ref, row_dst, stream), "exl3b200_moe_down_rows")

@@ -342,11 +342,13 @@ def _ep_gpu_rank(rank, world, port, q):
         plugin = load_plugin()
         E, H, W, k = 64, 2048, 512, 8
         res = []
-        for T, transport in ((3, "nccl"), (256, "nccl"), (3, "p2p"), (256, "p2p")):
+        for T, transport, fuse in ((3, "nccl", False), (256, "nccl", False), (3, "p2p", False), (256, "p2p", False),
+                                   (3, "p2p", True), (256, "p2p", True)):
             full = MoeLayer(plugin, n_expert=E, hidden=H, width=W, top_k=k, bits_gu=3, bits_dn=4, max_tokens=T,
                             seed=7, device=dev)
             ep = EpLayer(plugin, rank=rank, world=world, n_expert=E, hidden=H, width=W, top_k=k, bits_gu=3,
-                         bits_dn=4, max_tokens=T, seed=7, device=dev, full=full, transport=transport)
+                         bits_dn=4, max_tokens=T, seed=7, device=dev, full=full, transport=transport,
+                         fuse_combine=fuse)
             g = torch.Generator(device=dev)
             g.manual_seed(50 + rank + T)
             x = torch.randn((T, H), generator=g, device=dev).to(torch.float16)
