@@ -215,9 +215,21 @@ def bench_ours(args, rank, world, local_rank):
         layer.forward(T, sh)
     barrier()
     clocks.start()
-    soak_t0 = time.perf_counter()
-    while not args.profile and time.perf_counter() - soak_t0 < 1.0:
+    if world > 1:
+        # every rank must run the same number of steps (each step exchanges with every peer): the soak length is
+        # one rank-agreed count, about a second's worth, not each rank's own clock
+        t0 = time.perf_counter()
         layer.forward(T, sh)
+        torch.cuda.synchronize()
+        n_soak = torch.tensor([0 if args.profile else max(1, int(1.0 / max(time.perf_counter() - t0, 1e-4)))],
+                              device=dev)
+        torch.distributed.all_reduce(n_soak, op=torch.distributed.ReduceOp.MAX)
+        for _ in range(int(n_soak.item())):
+            layer.forward(T, sh)
+    else:
+        soak_t0 = time.perf_counter()
+        while not args.profile and time.perf_counter() - soak_t0 < 1.0:
+            layer.forward(T, sh)
     torch.cuda.synchronize()
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
     kev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
@@ -467,7 +479,7 @@ def main():
         import torch
         torch.cuda.set_device(local_rank)
         os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
-        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=60),
                                              device_id=torch.device("cuda", local_rank))
     try:
         line = bench_ours(args, rank, world, local_rank)
