@@ -235,11 +235,11 @@ def bench_ours(args, rank, world, local_rank):
     kev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
     pev = ([[torch.cuda.Event(enable_timing=True) for _ in range(len(layer.PHASES) + 1)] for _ in range(args.steps)]
            if world > 1 else None)
-    # one GPU: the step captured once in a CUDA graph and replayed (no per-launch host cost between steps); the
-    # per-op times come from an eager pass with events around the two ops. N > 1: eager (a step reads the received
-    # counts on the host).
+    # The step captured once in a CUDA graph and replayed (no per-launch host cost between steps) -- one GPU, and
+    # N > 1 over peer memory (a step there never synchronises with the host); the per-op (and per-phase) times come
+    # from an eager pass with events. N > 1 over NCCL: eager (a step reads the split sizes on the host).
     graph = None
-    if world == 1 and not args.profile:
+    if (world == 1 or args.transport == "p2p") and not args.profile:
         try:
             g = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g):
@@ -254,10 +254,10 @@ def bench_ours(args, rank, world, local_rank):
     wall0 = time.perf_counter()
     ev[0].record(stream)
     for s in range(args.steps):
-        if world > 1:
-            layer.forward(T, sh, events=kev[s], phases=pev[s])
-        elif graph is not None:
+        if graph is not None:
             graph.replay()
+        elif world > 1:
+            layer.forward(T, sh, events=kev[s], phases=pev[s])
         else:
             layer.forward(T, sh, events=kev[s])
     ev[1].record(stream)
@@ -267,7 +267,10 @@ def bench_ours(args, rank, world, local_rank):
     ms = ev[0].elapsed_time(ev[1]) / args.steps
     if graph is not None:
         for s in range(args.steps):
-            layer.forward(T, sh, events=kev[s])
+            if world > 1:
+                layer.forward(T, sh, events=kev[s], phases=pev[s])
+            else:
+                layer.forward(T, sh, events=kev[s])
         torch.cuda.synchronize()
     gu_ms = float(np.mean([k[0].elapsed_time(k[1]) for k in kev]))
     dn_ms = float(np.mean([k[1].elapsed_time(k[2]) for k in kev]))

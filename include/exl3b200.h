@@ -151,7 +151,8 @@ int     exl3b200_ep_dedup_scan(const int32_t* ids, int64_t top_k, const int32_t*
  *   The combine fused into down instead of p2p_combine: p2p_row_dst (each sorted row's destination address in
  *   its source's window), exl3b200_moe_down_rows with that table (down's epilogue stores each row straight into
  *   the source over NVLink, fenced at system scope), then p2p_signal_combine (the flags).
- * Ranks call the same steps with the same epoch (1, 2, ...). No counterpart in the reference (one device). */
+ * Ranks call the same steps in the same order (the epoch advances once a step on every rank). No counterpart in the
+ * reference (one device). */
 int     exl3b200_ep_window_alloc(int64_t bytes, void** ptr);
 int     exl3b200_ep_window_free(void* ptr);
 int     exl3b200_ep_window_handle(void* ptr, void* handle64);
@@ -160,23 +161,30 @@ int     exl3b200_ep_window_close(void* ptr);
 int     exl3b200_p2p_dispatch(const uint16_t* x, int64_t x_pitch, const int32_t* row_tok, const uint32_t* meta,
                               const int32_t* dest_off, const int32_t* counts, int64_t n_slots, const uint64_t* peers,
                               const int64_t* offs, int64_t self, int64_t world, int64_t t_cap, int64_t p_cap,
-                              int64_t hidden, uint32_t epoch, void* stream);
-int     exl3b200_p2p_wait_dispatch(void* own, const int64_t* offs, int64_t world, uint32_t epoch, int32_t* hdr,
-                                   void* stream);
+                              int64_t hidden, const uint32_t* epoch, void* stream);
+int     exl3b200_p2p_wait_dispatch(void* own, const int64_t* offs, int64_t world, const uint32_t* epoch,
+                                   int32_t* hdr, void* stream);
 int     exl3b200_p2p_unpack(const void* own, const int64_t* offs, const int32_t* hdr, int64_t world, int64_t t_cap,
                             int64_t p_cap, int64_t n_pairs, int32_t* expert, int32_t* row, int32_t* dst_rank,
                             int32_t* dst_pos, void* stream);
 int     exl3b200_p2p_combine(const uint16_t* y_rows, int64_t y_pitch, const int32_t* sorted_pair, int64_t n_rows,
                              const int32_t* dst_rank, const int32_t* dst_pos, const uint64_t* peers,
                              const int64_t* offs, int64_t self, int64_t world, int64_t p_cap, int64_t hidden,
-                             uint32_t epoch, void* stream);
-int     exl3b200_p2p_wait_combine(const void* own, const int64_t* offs, int64_t world, uint32_t epoch,
+                             const uint32_t* epoch, void* stream);
+int     exl3b200_p2p_wait_combine(const void* own, const int64_t* offs, int64_t world, const uint32_t* epoch,
                                   int32_t* status, void* stream);
 int     exl3b200_p2p_row_dst(const int32_t* sorted_pair, int64_t n_rows, const int32_t* dst_rank,
                              const int32_t* dst_pos, const uint64_t* peers, const int64_t* offs, int64_t self,
                              int64_t world, int64_t p_cap, int64_t hidden, uint64_t* row_dst, void* stream);
 int     exl3b200_p2p_signal_combine(const uint64_t* peers, const int64_t* offs, int64_t self, int64_t world,
-                                    uint32_t epoch, void* stream);
+                                    const uint32_t* epoch, void* stream);
+/* The step's epoch lives in device memory (epoch[0], zero at set-up): p2p_begin bumps it first thing a step, and
+ * every p2p step reads it there -- so a step captured in a CUDA graph replays with a fresh epoch each time. */
+int     exl3b200_p2p_begin(uint32_t* epoch, void* stream);
+/* moe_exl3_gate_up (down = 0) / moe_exl3_down (down = 1) over the live rows only: rows outside
+ * [expert_offset[0], expert_offset[n_expert]) are left untouched instead of zeroed, so a caller may pass a
+ * capacity-sized pass whose live count is known only on the device; down may write through row_dst. */
+int     exl3b200_moe_op_live(const RadArgs* args, int down, const uint64_t* row_dst, void* stream);
 /* moe_exl3_down (same RadArgs and checks as the row's launch) writing output row i at row_dst[i] (a device table
  * of row addresses, possibly in a peer's memory) instead of y + i * pitch. No counterpart in the reference. */
 int     exl3b200_moe_down_rows(const RadArgs* args, const uint64_t* row_dst, void* stream);

@@ -43,7 +43,7 @@ typedef struct Exl3bOp {
     const int32_t* expert_offset;
     int32_t*       err;                 /* device word: set nonzero when a bounded wait gives up */
     const uint64_t* row_dst;            /* optional (down): output row i is written at row_dst[i], not y + i*pitch */
-    int32_t        pad1;
+    int32_t        live_only;           /* 1: rows outside the runs are left untouched, not zeroed */
     Exl3bClass     cls[EXL3B_MAX_CLS];
 } Exl3bOp;
 

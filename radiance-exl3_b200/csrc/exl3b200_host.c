@@ -238,6 +238,20 @@ int exl3b200_moe_down_rows(const RadArgs* a, const uint64_t* row_dst, void* stre
     return run_op(&k, a->scratch, a->scratch_bytes, stream);
 }
 
+/* moe_exl3_gate_up (down = 0) or moe_exl3_down (down = 1) over the live rows only: rows outside the runs are left
+ * untouched instead of zeroed, so a caller may pass a capacity-sized sorted_tok whose live count is known only on the
+ * device (expert_offset[n_expert]). down may also write through a row-address table (row_dst, else NULL). */
+int exl3b200_moe_op_live(const RadArgs* a, int down, const uint64_t* row_dst, void* stream) {
+    Exl3bGeom g;
+    Exl3bOp k;
+    if (!a || (row_dst && !down)) return RAD_E_INVAL;
+    const int rc = build_op(a, down ? EXL3B_DOWN : EXL3B_GATE_UP, &g, &k);
+    if (rc != RAD_OK) return rc;
+    k.live_only = 1;
+    k.row_dst = row_dst;
+    return run_op(&k, a->scratch, a->scratch_bytes, stream);
+}
+
 static int64_t op_scratch(const RadArgs* a, int op) {
     Exl3bGeom g;
     Exl3bOp k;

@@ -289,8 +289,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_skinny(const Exl3bOp op, i
     if (S > 1) cluster_sync_all();
     const int64_t n_units = s_misc[0];
 
-    // ---- rows no unit writes: zero (outside the runs, or a dropped slot), across the whole width
-    {
+    // ---- rows no unit writes: zero (outside the runs, or a dropped slot), across the whole width (unless the
+    // caller asked for the live rows only)
+    if (!op.live_only) {
         const int64_t gcta = cluster_id * S + rank, ncta = n_clusters * S;
         for (int64_t i = gcta; i < op.T; i += ncta) {
             if (row_live(op, i)) continue;

@@ -53,8 +53,8 @@ __device__ __forceinline__ uint8_t* wbase(const uint64_t* peers, int r) {
 __global__ void k_p2p_dispatch(const uint4* __restrict__ x, int64_t x_pitch16, const int32_t* __restrict__ row_tok,
                                const uint32_t* __restrict__ meta, const int32_t* __restrict__ dest_off,
                                const int32_t* __restrict__ counts, int64_t n_slots, const uint64_t* __restrict__ peers,
-                               Win w, int self, int world, int64_t t_cap, int64_t p_cap, int row16, uint32_t epoch,
-                               int32_t* err) {
+                               Win w, int self, int world, int64_t t_cap, int64_t p_cap, int row16,
+                               const uint32_t* __restrict__ epoch_p, int32_t* err) {
     const int lane = threadIdx.x & 31;
     for (int64_t j = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32; j < n_slots;
          j += (int64_t)gridDim.x * (blockDim.x / 32)) {
@@ -94,15 +94,17 @@ __global__ void k_p2p_dispatch(const uint4* __restrict__ x, int64_t x_pitch16, c
         ctl[2] = (uint32_t)counts[2 * d + 1];
         ctl[3] = (uint32_t)dest_off[d];
         __threadfence_system();
-        st_release_sys(&ctl[0], epoch);
+        st_release_sys(&ctl[0], *epoch_p);
     }
     if (threadIdx.x == 0) reinterpret_cast<uint32_t*>(wbase(peers, self) + w.done)[0] = 0;
 }
 
 // Lane s waits (bounded) for source s's dispatch flag of this epoch, then hands its counts to the host:
 // hdr[3s] = rows, hdr[3s + 1] = pairs, hdr[3s + 2] = base; hdr[3 world] = 0, or -1 when a wait gave up.
-__global__ void k_p2p_wait_dispatch(uint8_t* own, Win w, int world, uint32_t epoch, int32_t* hdr, int32_t* err) {
+__global__ void k_p2p_wait_dispatch(uint8_t* own, Win w, int world, const uint32_t* epoch_p, int32_t* hdr,
+                                    int32_t* err) {
     const int s = threadIdx.x;
+    const uint32_t epoch = *epoch_p;
     bool ok = true;
     if (s < world) {
         const uint32_t* ctl = reinterpret_cast<const uint32_t*>(own + w.ctl) + s * 8;
@@ -136,7 +138,13 @@ __global__ void k_p2p_unpack(const uint8_t* own, Win w, const int32_t* __restric
         if (q < pb + np) break;
         pb += np;
     }
-    if (s >= world) return;
+    if (s >= world) {                   // past the received pairs (a capacity-sized pass): a dropped entry
+        expert[q] = -1;
+        row[q] = -1;
+        dst_rank[q] = -1;
+        dst_pos[q] = -1;
+        return;
+    }
     const int64_t j = q - pb;
     const uint32_t m = j < p_cap ? __ldcv(reinterpret_cast<const uint32_t*>(own + w.meta) + (int64_t)s * p_cap + j) : 0u;
     if (j >= p_cap || (int64_t)(m >> 12) >= t_cap) {   // outside the segments: the pair is dropped (expert -1)
@@ -157,7 +165,7 @@ __global__ void k_p2p_unpack(const uint8_t* own, Win w, const int32_t* __restric
 __global__ void k_p2p_combine(const uint4* __restrict__ y_rows, int64_t y_pitch16, const int32_t* __restrict__ sorted_pair,
                               int64_t n_rows, const int32_t* __restrict__ dst_rank, const int32_t* __restrict__ dst_pos,
                               const uint64_t* __restrict__ peers, Win w, int self, int world, int64_t p_cap, int row16,
-                              uint32_t epoch, int32_t* err) {
+                              const uint32_t* __restrict__ epoch_p, int32_t* err) {
     const int lane = threadIdx.x & 31;
     for (int64_t i = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32; i < n_rows;
          i += (int64_t)gridDim.x * (blockDim.x / 32)) {
@@ -184,15 +192,16 @@ __global__ void k_p2p_combine(const uint4* __restrict__ y_rows, int64_t y_pitch1
     if (!last) return;
     if ((int)threadIdx.x < world) {
         uint32_t* ctl = reinterpret_cast<uint32_t*>(wbase(peers, threadIdx.x) + w.ctl) + self * 8;
-        st_release_sys(&ctl[4], epoch);
+        st_release_sys(&ctl[4], *epoch_p);
     }
     if (threadIdx.x == 0) reinterpret_cast<uint32_t*>(wbase(peers, self) + w.done)[1] = 0;
 }
 
 // Lane d waits (bounded) for owner d's combine flag of this epoch; status[0] = 0, or -1 when a wait gave up.
-__global__ void k_p2p_wait_combine(const uint8_t* own, Win w, int world, uint32_t epoch, int32_t* status,
+__global__ void k_p2p_wait_combine(const uint8_t* own, Win w, int world, const uint32_t* epoch_p, int32_t* status,
                                    int32_t* err) {
     const int d = threadIdx.x;
+    const uint32_t epoch = *epoch_p;
     bool ok = true;
     if (d < world) {
         const uint32_t* ctl = reinterpret_cast<const uint32_t*>(own + w.ctl) + d * 8;
@@ -219,8 +228,12 @@ __global__ void k_p2p_row_dst(const int32_t* __restrict__ sorted_pair, int64_t n
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n_rows) return;
     const int32_t q = sorted_pair[i];
-    const int s = q >= 0 && q < n_rows ? dst_rank[q] : -1;
-    const int64_t pos = q >= 0 && q < n_rows ? dst_pos[q] : -1;
+    if (q < 0) {                        // past the live rows of a capacity-sized pass: never written
+        row_dst[i] = peers[self] + (uint64_t)w.sink;
+        return;
+    }
+    const int s = q < n_rows ? dst_rank[q] : -1;
+    const int64_t pos = q < n_rows ? dst_pos[q] : -1;
     if (s < 0 || s >= world || pos < 0 || pos >= p_cap) {
         atomicOr(err, 4);
         row_dst[i] = peers[self] + (uint64_t)w.sink;
@@ -231,13 +244,17 @@ __global__ void k_p2p_row_dst(const int32_t* __restrict__ sorted_pair, int64_t n
 
 // After the down launch that wrote through the row table (its threads fenced their stores at system scope before
 // completing): every source's combine flag for this epoch.
-__global__ void k_p2p_signal_combine(const uint64_t* __restrict__ peers, Win w, int self, int world, uint32_t epoch) {
+__global__ void k_p2p_signal_combine(const uint64_t* __restrict__ peers, Win w, int self, int world,
+                                     const uint32_t* __restrict__ epoch_p) {
     const int s = threadIdx.x;
     if (s >= world) return;
     __threadfence_system();
     uint32_t* ctl = reinterpret_cast<uint32_t*>(wbase(peers, s) + w.ctl) + self * 8;
-    st_release_sys(&ctl[4], epoch);
+    st_release_sys(&ctl[4], *epoch_p);
 }
+
+// A step's epoch lives in device memory (so a captured step replays with a new one): bumped first thing a step.
+__global__ void k_p2p_begin(uint32_t* epoch_p) { epoch_p[0] += 1u; }
 
 inline bool al16(const void* p) { return ((uintptr_t)p & 15u) == 0; }
 constexpr int kWarps = 8;
@@ -287,7 +304,7 @@ int exl3b200_ep_window_close(void* ptr) { return cudaIpcCloseMemHandle(ptr) == c
 int exl3b200_p2p_dispatch(const uint16_t* x, int64_t x_pitch, const int32_t* row_tok, const uint32_t* meta,
                           const int32_t* dest_off, const int32_t* counts, int64_t n_slots, const uint64_t* peers,
                           const int64_t* offs, int64_t self, int64_t world, int64_t t_cap, int64_t p_cap,
-                          int64_t hidden, uint32_t epoch, void* stream) {
+                          int64_t hidden, const uint32_t* epoch, void* stream) {
     if (!x || !row_tok || !meta || !dest_off || !counts || !peers || !offs || world < 1 || world > 32 || self < 0 ||
         self >= world || n_slots < 0 || hidden < 8 || hidden % 8 || x_pitch % 8 || !al16(x))
         return -12;
@@ -301,9 +318,9 @@ int exl3b200_p2p_dispatch(const uint16_t* x, int64_t x_pitch, const int32_t* row
     return cudaGetLastError() == cudaSuccess ? 0 : -6;
 }
 
-int exl3b200_p2p_wait_dispatch(void* own, const int64_t* offs, int64_t world, uint32_t epoch, int32_t* hdr,
+int exl3b200_p2p_wait_dispatch(void* own, const int64_t* offs, int64_t world, const uint32_t* epoch, int32_t* hdr,
                                void* stream) {
-    if (!own || !offs || !hdr || world < 1 || world > 32) return -12;
+    if (!own || !offs || !hdr || !epoch || world < 1 || world > 32) return -12;
     int sm = 0;
     int32_t* err = nullptr;
     if (exl3b_cuda_device_info(&sm, &err) != 0) return -6;
@@ -326,7 +343,8 @@ int exl3b200_p2p_unpack(const void* own, const int64_t* offs, const int32_t* hdr
 
 int exl3b200_p2p_combine(const uint16_t* y_rows, int64_t y_pitch, const int32_t* sorted_pair, int64_t n_rows,
                          const int32_t* dst_rank, const int32_t* dst_pos, const uint64_t* peers, const int64_t* offs,
-                         int64_t self, int64_t world, int64_t p_cap, int64_t hidden, uint32_t epoch, void* stream) {
+                         int64_t self, int64_t world, int64_t p_cap, int64_t hidden, const uint32_t* epoch,
+                         void* stream) {
     if (!y_rows || !sorted_pair || !dst_rank || !dst_pos || !peers || !offs || world < 1 || world > 32 || self < 0 ||
         self >= world || n_rows < 0 || hidden < 8 || hidden % 8 || y_pitch % 8 || !al16(y_rows))
         return -12;
@@ -337,6 +355,12 @@ int exl3b200_p2p_combine(const uint16_t* y_rows, int64_t y_pitch, const int32_t*
     k_p2p_combine<<<grid_for(n_rows, sm), kWarps * 32, 0, static_cast<cudaStream_t>(stream)>>>(
         reinterpret_cast<const uint4*>(y_rows), y_pitch / 8, sorted_pair, n_rows, dst_rank, dst_pos, peers, w,
         (int)self, (int)world, p_cap, (int)(hidden / 8), epoch, err);
+    return cudaGetLastError() == cudaSuccess ? 0 : -6;
+}
+
+int exl3b200_p2p_begin(uint32_t* epoch, void* stream) {
+    if (!epoch) return -12;
+    k_p2p_begin<<<1, 1, 0, static_cast<cudaStream_t>(stream)>>>(epoch);
     return cudaGetLastError() == cudaSuccess ? 0 : -6;
 }
 
@@ -357,16 +381,16 @@ int exl3b200_p2p_row_dst(const int32_t* sorted_pair, int64_t n_rows, const int32
 }
 
 int exl3b200_p2p_signal_combine(const uint64_t* peers, const int64_t* offs, int64_t self, int64_t world,
-                                uint32_t epoch, void* stream) {
-    if (!peers || !offs || world < 1 || world > 32 || self < 0 || self >= world) return -12;
+                                const uint32_t* epoch, void* stream) {
+    if (!peers || !offs || !epoch || world < 1 || world > 32 || self < 0 || self >= world) return -12;
     const Win w = { offs[0], offs[1], offs[2], offs[3], offs[4], offs[5] };
     k_p2p_signal_combine<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(peers, w, (int)self, (int)world, epoch);
     return cudaGetLastError() == cudaSuccess ? 0 : -6;
 }
 
-int exl3b200_p2p_wait_combine(const void* own, const int64_t* offs, int64_t world, uint32_t epoch, int32_t* status,
-                              void* stream) {
-    if (!own || !offs || !status || world < 1 || world > 32) return -12;
+int exl3b200_p2p_wait_combine(const void* own, const int64_t* offs, int64_t world, const uint32_t* epoch,
+                              int32_t* status, void* stream) {
+    if (!own || !offs || !status || !epoch || world < 1 || world > 32) return -12;
     int sm = 0;
     int32_t* err = nullptr;
     if (exl3b_cuda_device_info(&sm, &err) != 0) return -6;

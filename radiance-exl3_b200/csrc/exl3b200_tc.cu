@@ -248,7 +248,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
     // rows no unit writes are zeroed (outside the runs, dropped slots): the grid's threads test the rows in
     // parallel; a thread clears the (rare) dead row it finds
-    if (warp < kEpiWarps || warp >= kDecWarp0) {
+    if (!op.live_only && (warp < kEpiWarps || warp >= kDecWarp0)) {
         const int64_t lt = warp < kEpiWarps ? tid : tid - (kDecWarp0 - kEpiWarps) * 32;   // 0 .. nthr-1
         const int64_t nthr = (kEpiWarps + kDecWarps) * 32;
         const int64_t lo = op.expert_offset[0], hi = op.expert_offset[n_exp];

@@ -81,9 +81,9 @@ class DeviceOps:
     def map(self, idx, n, table, n_table, out):
         self.nat.ep_map(idx.data_ptr(), n, table.data_ptr(), n_table, out.data_ptr(), self._stream())
 
-    def experts(self, recv_x, n_rows, n_pairs, events=None, x_ptr=None, down_row_dst=None):
+    def experts(self, recv_x, n_rows, n_pairs, events=None, x_ptr=None, down_row_dst=None, live=False):
         self.local.experts(n_rows, n_pairs, self._stream(), x_ptr=x_ptr or recv_x.data_ptr(), top_k=1, M=n_rows,
-                           events=events, down_row_dst=down_row_dst)
+                           events=events, down_row_dst=down_row_dst, live=live)
 
     def rows_scatter(self, src, idx, n_rows, dst, n_dst):
         rb = src.shape[1] * src.element_size()
@@ -199,6 +199,7 @@ class EpLayer:
             self.dest_off_p = e(world + 1, dt=i32)
             self.counts_p = e(2 * world, dt=i32)
             self.hdr_p = torch.zeros(3 * world + 1, dtype=i32, device=dev)
+            self.epoch_dev = torch.zeros(1, dtype=i32, device=dev)     # the step's epoch, bumped on the device
             self.status_p = torch.zeros(1, dtype=i32, device=dev)
             self.dst_rank, self.dst_pos = e(self.Rcap, dt=i32), e(self.Rcap, dt=i32)
             # the combine fused into down: each sorted row's destination in its source's window
@@ -260,13 +261,17 @@ class EpLayer:
                      "recv_counts": pairs_r, "send_rows": rows_s, "recv_rows": rows_r}
 
     def _forward_p2p(self, T, events, phases, x, logits, out):
-        """The same step with the exchange over peer memory: no collective, one host read (the received counts)."""
+        """The same step with the exchange over peer memory and no host synchronisation at all: the local pass runs
+        at capacity (world * T * top_k received pairs) with its live count on the device (entries past it are
+        dropped pairs, rows past it untouched), and the epoch lives on the device -- so the step can be captured in
+        a CUDA graph and replayed."""
         o, nat, win, G, k, P = self.ops, self.nat, self.win, self.G, self.k, T * self.k
         st = o._stream()
-        self.epoch += 1
-        ep = self.epoch & 0xFFFFFFFF
+        Q, Tc, Pc = self.Rcap, self.max_tokens, self.max_tokens * k
+        ep = self.epoch_dev.data_ptr()
         mark = (lambda i: phases[i].record()) if phases else (lambda i: None)
         mark(0)
+        nat.p2p_begin(ep, st)
         o.router(logits, T, self.E, k, self.ids, self.w)
         o.dest(self.ids, P, self.nl, G, self.dest)
         o.scatter(self.dest, P, G, self.sorted_pairs[:P], self.dest_off_p)
@@ -275,46 +280,52 @@ class EpLayer:
         mark(1)
         nat.p2p_dispatch(x.data_ptr(), x.shape[1], self.row_tok.data_ptr(), self.send_meta.data_ptr(),
                          self.dest_off_p.data_ptr(), self.counts_p.data_ptr(), P, win.peers.data_ptr(), win.offs,
-                         self.rank, G, self.max_tokens, self.max_tokens * k, self.H, ep, st)
+                         self.rank, G, Tc, Pc, self.H, ep, st)
         nat.p2p_wait_dispatch(win.base, win.offs, G, ep, self.hdr_p.data_ptr(), st)
-        h = self.hdr_p.cpu().tolist()            # the received counts: the one host read of a step
-        if h[3 * G] != 0:
-            raise RuntimeError("expert parallelism: a peer's dispatch did not arrive within the wait limit")
-        rows_r, pairs_r = h[0:3 * G:3], h[1:3 * G:3]
-        R, Rr = sum(pairs_r), sum(rows_r)
         mark(2)
-        nat.p2p_unpack(win.base, win.offs, self.hdr_p.data_ptr(), G, self.max_tokens, self.max_tokens * k, R,
-                       self.pair_e.data_ptr(), self.pair_row.data_ptr(), self.dst_rank.data_ptr(),
-                       self.dst_pos.data_ptr(), st)
-        o.scatter(self.pair_e[:R], R, self.nl, self.sorted_pair[:R], self.off_loc)
-        o.map(self.sorted_pair, R, self.pair_row, R, self.sorted_row)
+        nat.p2p_unpack(win.base, win.offs, self.hdr_p.data_ptr(), G, Tc, Pc, Q, self.pair_e.data_ptr(),
+                       self.pair_row.data_ptr(), self.dst_rank.data_ptr(), self.dst_pos.data_ptr(), st)
+        o.scatter(self.pair_e[:Q], Q, self.nl, self.sorted_pair[:Q], self.off_loc)
+        o.map(self.sorted_pair, Q, self.pair_row, Q, self.sorted_row)
         mark(3)
         if self.fuse_combine:
             # down's epilogue writes each pair's row straight into its source's window (NVLink stores overlapping
             # the decode of the next units), then the flags
-            nat.p2p_row_dst(self.sorted_pair.data_ptr(), R, self.dst_rank.data_ptr(), self.dst_pos.data_ptr(),
-                            win.peers.data_ptr(), win.offs, self.rank, G, self.max_tokens * k, self.H,
-                            self.row_dst.data_ptr(), st)
-            o.experts(None, G * self.max_tokens, R, events, x_ptr=win.rows_ptr(),
-                      down_row_dst=self.row_dst.data_ptr() if R > 0 else None)
+            nat.p2p_row_dst(self.sorted_pair.data_ptr(), Q, self.dst_rank.data_ptr(), self.dst_pos.data_ptr(),
+                            win.peers.data_ptr(), win.offs, self.rank, G, Pc, self.H, self.row_dst.data_ptr(), st)
+            o.experts(None, G * Tc, Q, events, x_ptr=win.rows_ptr(), down_row_dst=self.row_dst.data_ptr(), live=True)
             mark(4)
             nat.p2p_signal_combine(win.peers.data_ptr(), win.offs, self.rank, G, ep, st)
         else:
-            o.experts(None, G * self.max_tokens, R, events, x_ptr=win.rows_ptr())
+            o.experts(None, G * Tc, Q, events, x_ptr=win.rows_ptr(), live=True)
             mark(4)
-            nat.p2p_combine(self.y_rows.data_ptr(), self.H, self.sorted_pair.data_ptr(), R, self.dst_rank.data_ptr(),
-                            self.dst_pos.data_ptr(), win.peers.data_ptr(), win.offs, self.rank, G,
-                            self.max_tokens * k, self.H, ep, st)
+            nat.p2p_combine(self.y_rows.data_ptr(), self.H, self.sorted_pair.data_ptr(), Q, self.dst_rank.data_ptr(),
+                            self.dst_pos.data_ptr(), win.peers.data_ptr(), win.offs, self.rank, G, Pc, self.H, ep, st)
         nat.p2p_wait_combine(win.base, win.offs, G, ep, self.status_p.data_ptr(), st)
         mark(5)
         o.gather(None, self.sorted_pairs, P, self.w, T, k, out, rows_ptr=win.yback_ptr())
         mark(6)
-        self.last = {"R": R, "rows_recv": Rr, "sent": P, "recv_counts": pairs_r, "recv_rows": rows_r, "p2p": True}
+        self.last = {"p2p": True, "sent": P}
+
+    def _p2p_counts(self):
+        """The last step's received counts, read from the device (synchronises): rows and pairs from each source."""
+        h = self.hdr_p.cpu().tolist()
+        G = self.G
+        rows_r, pairs_r = h[0:3 * G:3], h[1:3 * G:3]
+        self.last.update({"R": sum(pairs_r), "rows_recv": sum(rows_r), "recv_counts": pairs_r,
+                          "recv_rows": rows_r, "dispatch_status": h[3 * G]})
+        return self.last
 
     def check(self):
-        """Raise if a peer's combine never arrived in the last step (reads the status word: synchronises)."""
-        if self.transport == "p2p" and int(self.status_p.item()) != 0:
-            raise RuntimeError("expert parallelism: a peer's combine did not arrive within the wait limit")
+        """Raise if a peer's dispatch or combine did not arrive within the wait limit in the last step, or a row fell
+        outside a window (reads the status words and the device error word: synchronises)."""
+        if self.transport != "p2p":
+            return
+        if self._p2p_counts()["dispatch_status"] != 0 or int(self.status_p.item()) != 0:
+            raise RuntimeError("expert parallelism: a peer's exchange did not arrive within the wait limit")
+        err = self.nat.read_error(clear=False)
+        if err & 12:
+            raise RuntimeError(f"expert parallelism: device error word {err:#x}")
 
     def close(self):
         """Collective: release the peer-memory window (p2p transport)."""
@@ -332,7 +343,8 @@ class EpLayer:
 
     def time_prep_step(self, T, n=5):
         """The local pass's gate_up input rotation alone (ms), over the rows the last step received."""
-        R, Rr = self.last["R"], self.last.get("rows_recv", self.last["R"])
+        R = self._R()
+        Rr = self.last.get("rows_recv", R)
         if self.transport == "p2p":
             return self.ops.local.time_prep(self.G * self.max_tokens, R, x_ptr=self.win.rows_ptr(), top_k=1, n=n)
         return self.ops.local.time_prep(Rr, R, x_ptr=self.recv_x.data_ptr(), top_k=1, n=n)
@@ -340,11 +352,23 @@ class EpLayer:
     def expert_flops(self, rows):
         return self.ops.local.expert_flops(rows)
 
+    def _R(self):
+        if self.last.get("p2p") and "R" not in self.last:
+            self._p2p_counts()
+        return self.last.get("R", 0)
+
     def band_name(self, op, T):
-        return self.ops.local.band_name(op, self.last["R"]) + " (rows received by this rank)"
+        return self.ops.local.band_name(op, self._R()) + " (rows received by this rank)"
 
     def launches_per_step(self, T):
-        return self.ops.kernels(T, self.k, self.E, self.last["R"])
+        if self.transport == "p2p":
+            # begin, router, ep_dest, rank scatter, dedup scan, dispatch, wait, unpack, local scatter (capacity),
+            # map, row table, gate_up (+ prep), down, signal (or combine), wait, the gather's two
+            Q = self.Rcap
+            tc = self.ops.local._tc("gate_up", Q)
+            return 1 + 1 + 1 + (1 if T * self.k <= 8192 else 3) + 1 + 2 + 1 + (1 if Q <= 8192 else 3) + 1 + \
+                (1 if self.fuse_combine else 0) + 2 + (1 if tc else 0) + 1 + 1 + 2
+        return self.ops.kernels(T, self.k, self.E, self._R())
 
     def exchange_bytes(self):
         """Bytes this rank sent to other ranks in the last step: token rows and pair metas out, the down rows of the
@@ -354,7 +378,8 @@ class EpLayer:
             r = self.rank
             rows_out = sum(c[0::2]) - c[2 * r]
             metas_out = sum(c[1::2]) - c[2 * r + 1]
-            rows_back = self.last["R"] - self.last["recv_counts"][r]
+            L = self._p2p_counts()
+            rows_back = L["R"] - L["recv_counts"][r]
             return rows_out * 2 * self.H + metas_out * 4 + rows_back * 2 * self.H
         if "send_counts" not in self.last:
             return 0

@@ -162,7 +162,7 @@ class MoeLayer:
         return res
 
     # ------------------------------------------------------------------ one pass
-    def experts(self, T, rows, stream, x_ptr=None, top_k=None, M=None, events=None, down_row_dst=None):
+    def experts(self, T, rows, stream, x_ptr=None, top_k=None, M=None, events=None, down_row_dst=None, live=False):
         """gate_up then down over the sorted rows already in sorted_tok / offset. `events`: three
         torch.cuda.Event recorded before gate_up, between the two and after down (on the current stream)."""
         if rows == 0:                 # nothing routed here: no launch, the events still mark the (empty) ops
@@ -172,6 +172,15 @@ class MoeLayer:
         a_gu, a_dn, _ = self._build(T, rows, x_ptr, top_k, M)
         if events:
             events[0].record()
+        if live:
+            # the live rows only (a capacity-sized pass whose live count is on the device): nothing else is touched
+            self.native.moe_op_live(C.addressof(a_gu), 0, None, stream)
+            if events:
+                events[1].record()
+            self.native.moe_op_live(C.addressof(a_dn), 1, down_row_dst, stream)
+            if events:
+                events[2].record()
+            return
         rc = self.plugin.row("moe_exl3_gate_up").launch(C.byref(a_gu), stream)
         if rc != 0:
             raise RuntimeError(f"moe_exl3_gate_up launch: {rc}")

@@ -37,14 +37,16 @@ class Native:
         L.exl3b200_ep_window_close.argtypes = [_VP]
         _U32 = C.c_uint32
         L.exl3b200_p2p_dispatch.argtypes = [_VP, _I64, _VP, _VP, _VP, _VP, _I64, _VP, _VP, _I64, _I64, _I64, _I64,
-                                            _I64, _U32, _VP]
-        L.exl3b200_p2p_wait_dispatch.argtypes = [_VP, _VP, _I64, _U32, _VP, _VP]
+                                            _I64, _VP, _VP]
+        L.exl3b200_p2p_wait_dispatch.argtypes = [_VP, _VP, _I64, _VP, _VP, _VP]
         L.exl3b200_p2p_unpack.argtypes = [_VP, _VP, _VP, _I64, _I64, _I64, _I64, _VP, _VP, _VP, _VP, _VP]
-        L.exl3b200_p2p_combine.argtypes = [_VP, _I64, _VP, _I64, _VP, _VP, _VP, _VP, _I64, _I64, _I64, _I64, _U32, _VP]
-        L.exl3b200_p2p_wait_combine.argtypes = [_VP, _VP, _I64, _U32, _VP, _VP]
+        L.exl3b200_p2p_combine.argtypes = [_VP, _I64, _VP, _I64, _VP, _VP, _VP, _VP, _I64, _I64, _I64, _I64, _VP, _VP]
+        L.exl3b200_p2p_wait_combine.argtypes = [_VP, _VP, _I64, _VP, _VP, _VP]
         L.exl3b200_p2p_row_dst.argtypes = [_VP, _I64, _VP, _VP, _VP, _VP, _I64, _I64, _I64, _I64, _VP, _VP]
-        L.exl3b200_p2p_signal_combine.argtypes = [_VP, _VP, _I64, _I64, _U32, _VP]
+        L.exl3b200_p2p_signal_combine.argtypes = [_VP, _VP, _I64, _I64, _VP, _VP]
         L.exl3b200_moe_down_rows.argtypes = [_VP, _VP, _VP]
+        L.exl3b200_p2p_begin.argtypes = [_VP, _VP]
+        L.exl3b200_moe_op_live.argtypes = [_VP, _I, _VP, _VP]
 
     @staticmethod
     def _check(rc, what):
@@ -174,3 +176,9 @@ class Native:
 
     def moe_down_rows(self, args_ref, row_dst, stream=0):
         self._check(self.lib.exl3b200_moe_down_rows(args_ref, row_dst, stream), "exl3b200_moe_down_rows")
+
+    def p2p_begin(self, epoch, stream=0):
+        self._check(self.lib.exl3b200_p2p_begin(epoch, stream), "exl3b200_p2p_begin")
+
+    def moe_op_live(self, args_ref, down, row_dst, stream=0):
+        self._check(self.lib.exl3b200_moe_op_live(args_ref, down, row_dst, stream), "exl3b200_moe_op_live")
