@@ -1,11 +1,14 @@
-// exl3b200_ep.cu -- the device steps of expert parallelism around the routed-expert ops, sm_100a CUDA, extern "C".
+// exl3b200_ep.cu -- the device bookkeeping of expert parallelism around the routed-expert ops, sm_100a CUDA,
+// extern "C". Experts are held in contiguous blocks: expert e lives on rank e / n_local.
 //
-// Experts are held in contiguous blocks: expert e lives on rank e / n_local. A step on each rank:
-//   router -> stable scatter of its (token, slot) pairs over ALL experts (so the sorted pairs are grouped by the
-//   rank that holds their expert) -> k_ep_pack (the token row of every sorted pair, its local expert id, the
-//   per-rank counts) -> all-to-all of the rows -> stable scatter of the received rows over the local experts ->
-//   gate_up, down -> k_rows_scatter (the down rows back into arrival order) -> all-to-all back -> the gather over
-//   the sorted pairs, which sums each token's slots in ascending order exactly as on one GPU.
+//   k_ep_dest          the owning rank of each (token, slot) pair
+//   k_ep_dedup_scan    per owner rank (its pairs sorted stably by rank, so in token order): one row a distinct
+//                      token, a meta word a pair (the row within that rank's block, the local expert), the counts
+//   k_ep_dedup_copy    those rows packed contiguously a rank (for a collective library's all-to-all)
+//   k_ep_unpack        received pairs: local expert and row index (rows before its source + its row)
+//   k_ep_map           sorted pair -> its token row (the sorted_tok the ops read, top_k 1)
+//   k_ep_pack          the non-deduplicated pack (one row a pair), k_rows_scatter (rows into arrival order)
+// The peer-memory exchange itself is exl3b200_p2p.cu.
 #include <cuda_runtime.h>
 #include <stdint.h>
 
