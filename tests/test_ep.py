@@ -397,3 +397,58 @@ def test_ep_layer_over_nccl_equals_one_gpu():
                 assert same, f"rank {rank} T {T}: same band {band1}, max err {err}"
             else:
                 assert err <= 1e-2 * scale and cos >= 0.9999, (rank, T, err, scale, cos, band1, band2)
+
+
+def _ep_single_rank(port, q):
+    """World size 1 over peer memory: the window maps only itself, and every p2p kernel runs (dispatch, waits,
+    unpack, the capacity-sized local pass, the row table, the fused combine, the flags)."""
+    import datetime
+
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"], os.environ["MASTER_PORT"] = "127.0.0.1", str(port)
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    dist.init_process_group("nccl", rank=0, world_size=1, timeout=datetime.timedelta(seconds=60), device_id=dev)
+    try:
+        from exl3b200 import load_plugin
+        from exl3b200.ep import EpLayer
+        from exl3b200.layer import MoeLayer
+        plugin = load_plugin()
+        E, H, W, k, T = 32, 2048, 512, 6, 192
+        full = MoeLayer(plugin, n_expert=E, hidden=H, width=W, top_k=k, bits_gu=3, bits_dn=4, max_tokens=T, seed=9,
+                        device=dev)
+        res = []
+        for fuse in (False, True):
+            ep = EpLayer(plugin, rank=0, world=1, n_expert=E, hidden=H, width=W, top_k=k, bits_gu=3, bits_dn=4,
+                         max_tokens=T, seed=9, device=dev, full=full, transport="p2p", fuse_combine=fuse)
+            g = torch.Generator(device=dev)
+            g.manual_seed(77)
+            x = torch.randn((T, H), generator=g, device=dev).to(torch.float16)
+            lg = torch.randn((T, E), generator=g, device=dev)
+            full.x[:T], full.logits[:T], ep.x[:T], ep.logits[:T] = x, lg, x, lg
+            s = torch.cuda.current_stream().cuda_stream
+            full.forward(T, s)
+            for _ in range(3):
+                ep.forward(T, s)
+            torch.cuda.synchronize()
+            ep.check()
+            res.append(bool(torch.equal(full.out[:T], ep.out[:T])))
+            ep.close()
+        q.put(res)
+    except Exception as exc:
+        import traceback
+        q.put(repr(exc) + traceback.format_exc()[-1500:])
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.gpu
+def test_ep_single_rank_over_peer_memory_equals_the_layer():
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    p = ctx.Process(target=_ep_single_rank, args=(_free_port(), q))
+    p.start()
+    r = q.get(timeout=600)
+    p.join(timeout=120)
+    assert r == [True, True], r

@@ -261,3 +261,56 @@ def test_gather(dev, native, orc):
                       work.data_ptr())
     torch.cuda.synchronize()
     assert np.array_equal(y.cpu().numpy(), want)
+
+
+# ---------------------------------------------------------------------------------------------- the EP forms of the ops
+def _small_layer(plugin, T, seed=3, max_rows=None):
+    from exl3b200.layer import MoeLayer
+    lay = MoeLayer(plugin, n_expert=16, hidden=2048, width=512, top_k=4, bits_gu=3, bits_dn=4, max_tokens=T,
+                   seed=seed, max_rows=max_rows)
+    g = torch.Generator(device="cuda")
+    g.manual_seed(seed + 1)
+    lay.x.copy_(torch.randn(lay.x.shape, generator=g, device="cuda").to(torch.float16))
+    lay.logits.copy_(torch.randn(lay.logits.shape, generator=g, device="cuda"))
+    return lay
+
+
+@pytest.mark.parametrize("T", [2, 64])
+def test_down_rows_writes_through_the_row_table(dev, plugin, T):
+    """exl3b200_moe_down_rows: row i of down's output lands at row_dst[i] -- here a permutation of a second buffer --
+    bit for bit the row the plugin's down row writes at y + i * pitch."""
+    import ctypes as C
+    lay = _small_layer(plugin, T)
+    s = torch.cuda.current_stream().cuda_stream
+    lay.forward(T, s)
+    R = T * lay.k
+    _, a_dn, _ = lay._build(T, R)
+    perm = torch.randperm(R, generator=torch.Generator().manual_seed(T)).to(dev)
+    alt = torch.full((R, lay.H), 7, dtype=torch.int16, device=dev)
+    row_dst = (alt.data_ptr() + perm.to(torch.int64) * lay.H * 2).contiguous()
+    lay.native.moe_down_rows(C.addressof(a_dn), row_dst.data_ptr(), s)
+    torch.cuda.synchronize()
+    assert torch.equal(alt[perm], lay.y_rows[:R].view(torch.int16))
+
+
+@pytest.mark.parametrize("T,pad", [(3, 3), (128, 96)])   # the padding keeps each op in the same band
+def test_live_only_pass_leaves_padding_untouched(dev, plugin, T, pad):
+    """exl3b200_moe_op_live over a capacity-sized pass (sorted_tok padded with -1, the live count in expert_offset):
+    the live rows equal the plugin rows' result bit for bit, the padding rows keep what was there."""
+    lay = _small_layer(plugin, T, max_rows=T * 4 + pad)
+    s = torch.cuda.current_stream().cuda_stream
+    R = T * lay.k
+    lay.forward(T, s)
+    torch.cuda.synchronize()
+    h_ref, y_ref = lay.h[:R].clone(), lay.y_rows[:R].clone()
+    lay.sorted_tok[R:R + pad] = -1
+    lay.h[R:R + pad].view(torch.int16).fill_(0x1234)
+    lay.y_rows[R:R + pad].view(torch.int16).fill_(0x2345)
+    lay.h[:R].zero_()
+    lay.y_rows[:R].zero_()
+    lay.experts(T, R + pad, s, live=True)
+    torch.cuda.synchronize()
+    assert torch.equal(lay.h[:R].view(torch.int16), h_ref.view(torch.int16))
+    assert torch.equal(lay.y_rows[:R].view(torch.int16), y_ref.view(torch.int16))
+    assert bool((lay.h[R:R + pad].view(torch.int16) == 0x1234).all())
+    assert bool((lay.y_rows[R:R + pad].view(torch.int16) == 0x2345).all())
