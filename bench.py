@@ -189,7 +189,14 @@ def bench_ours(args, rank, world, local_rank):
     dev = torch.device("cuda", local_rank)
     plugin = load_plugin()
     T = args.tokens
-    if world > 1:
+    tp_mode = world > 1 and args.mode == "tp"
+    if tp_mode:
+        # the width split: every rank holds half (a quarter, ...) of every expert's width and serves ALL T tokens
+        # (replicated), so the group's throughput is T a step (strong scaling)
+        from exl3b200.tp import TpLayer
+        layer = TpLayer(plugin, rank=rank, world=world, n_expert=E, hidden=H, width=W, top_k=TOPK, bits_gu=KGU,
+                        bits_dn=KDN, codebook=CB, max_tokens=T, seed=1, transport=args.transport)
+    elif world > 1:
         from exl3b200.ep import EpLayer
         layer = EpLayer(plugin, rank=rank, world=world, n_expert=E, hidden=H, width=W, top_k=TOPK, bits_gu=KGU,
                         bits_dn=KDN, codebook=CB, max_tokens=T, seed=1 + rank, transport=args.transport)
@@ -197,7 +204,7 @@ def bench_ours(args, rank, world, local_rank):
         layer = MoeLayer(plugin, n_expert=E, hidden=H, width=W, top_k=TOPK, bits_gu=KGU, bits_dn=KDN, codebook=CB,
                          max_tokens=T, seed=1)
     g = torch.Generator(device=dev)
-    g.manual_seed(1000 + rank)
+    g.manual_seed(1000 + (0 if tp_mode else rank))      # width split: the same tokens on every rank
     layer.x.copy_(torch.randn(layer.x.shape, generator=g, device=dev).to(torch.float16))
     layer.logits.copy_(torch.randn(layer.logits.shape, generator=g, device=dev))
     stream = torch.cuda.current_stream()
@@ -285,7 +292,7 @@ def bench_ours(args, rank, world, local_rank):
         ep_phases = {n: round(float(v), 4) for n, v in zip(layer.PHASES, ph.cpu())}
     live = layer.live_experts()
     gu_b, dn_b = layer.expert_bytes()
-    tokens_total = T * world
+    tokens_total = T if tp_mode else T * world
     value = tokens_total / (ms / 1e3)
     step_bytes = live * (gu_b + dn_b)
     # the dominant kernel's roofline (the weight bytes it must read once / its measured duration). On the
@@ -423,21 +430,24 @@ def bench_ours(args, rank, world, local_rank):
 
     if world > 1:
         layer.check()
-        exch = layer.exchange_bytes()
+        exch = layer.exchange_bytes(T) if tp_mode else layer.exchange_bytes()
         if ep_phases is not None:
             ep_phases["exchange_bytes_rank0"] = exch
             ep_phases["transport"] = args.transport
+            ep_phases["mode"] = args.mode
         layer.close()          # collective: every rank releases its peer-memory window
     if rank != 0:
         return None
-    flops = layer.expert_flops(T * TOPK) * world
+    flops = layer.expert_flops(T * TOPK) * world      # (width split: every rank's slice of all T * TOPK rows)
     line = {
         "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "fp16 operands (decoded trellis), f32 accumulate", "data": "synthetic",
-        "config": {"workload": WORKLOAD, "tokens_per_gpu": T, "n_expert": E, "hidden": H, "width": W, "top_k": TOPK,
+        "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
+        "scaling": "strong" if tp_mode else "weak", "vs_baseline": None,
+        "dtype": "fp16 operands (decoded trellis), f32 accumulate", "data": "synthetic",
+        "config": {"workload": WORKLOAD, ("tokens_per_step" if tp_mode else "tokens_per_gpu"): T, "n_expert": E,
+                   "hidden": H, "width": W, "top_k": TOPK,
                    "bits": {"gate_up": KGU, "down": KDN}, "codebook": CB,
-                   "parallelism": f"ep{world} ({args.transport})" if world > 1 else "single",
+                   "parallelism": f"{args.mode}{world} ({args.transport})" if world > 1 else "single",
                    "launch": "cuda graph replay" if graph is not None else "eager",
                    "l2": "no flush: the packed weights (679 MB) exceed the 126 MB L2 and stream every step",
                    "inputs": "codes uniform random record words, suh +-1, svh +-|N(0,1)|*0.02, x and logits N(0,1)"},
@@ -469,6 +479,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--transport", default="p2p", choices=["p2p", "nccl"],
                     help="N > 1: the expert-parallel exchange over peer memory (default) or NCCL all-to-alls")
+    ap.add_argument("--mode", default="ep", choices=["ep", "tp"],
+                    help="N > 1: expert parallelism (default) or the width split of every expert (tp, N <= 4)")
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")

@@ -191,6 +191,32 @@ int     exl3b200_moe_down_rows(const RadArgs* args, const uint64_t* row_dst, voi
 int     exl3b200_ep_map(const int32_t* idx, int64_t n, const int32_t* table, int64_t n_table, int32_t* out,
                         void* stream);
 
+/* The width ("column-block") tensor split over peer memory: the engine's all_reduce after the layer's partial
+ * gather (architectures/qwen4exp_exl3/rad_block_moe_exl3.h:438-470, every rank holding whole 128-column blocks of
+ * every expert's width and gathering a PARTIAL of the output), fused into the gather as a reduce-scatter then an
+ * all-gather over NVLink. Windows come from exl3b200_ep_window_* as above; layout offs[4] = {part, red, ctl, done}:
+ *   part [world][s_cap][H] f32   each source's partials of this rank's token slice
+ *   red  [s_cap][H] f32          this rank's slice, reduced
+ *   ctl  [world][8] u32, done [4] u32
+ * Tokens are cut into world slices of s = ceil(n_tok / world) rows (s <= s_cap); rank o reduces slice o.
+ *   tp_gather_rs: the gather (exl3b200_moe_gather's arithmetic over this rank's y rows), each token's partial
+ *                 stored into its owner's part segment; then every owner's partials flag. status[0] = 0.
+ *   tp_reduce:    waits (at most 5 s) for every source's flag; sums this rank's slice over the sources in
+ *                 ascending order into red; then every rank's reduced flag (held back if a wait gave up).
+ *   tp_pull:      waits (at most 5 s) for every owner's reduced flag; out[t] = the owner's red row (f32, row pitch
+ *                 out_pitch floats); status[0] = -1 if a wait gave up (the error word is set too).
+ * Every rank ends with the same bits; at world 1 they are exl3b200_moe_gather's. Ranks pass the same n_tok and call
+ * the steps in the same order, after exl3b200_p2p_begin on their own epoch word. */
+int     exl3b200_tp_gather_rs(const uint16_t* rows, int64_t row_pitch, const int32_t* sorted_tok, int64_t n_rows,
+                              const float* w, int64_t n_tok, int64_t top_k, int64_t width, void* work,
+                              const uint64_t* peers, const int64_t* offs, int64_t self, int64_t world, int64_t s_cap,
+                              const uint32_t* epoch, int32_t* status, void* stream);
+int     exl3b200_tp_reduce(const uint64_t* peers, const int64_t* offs, int64_t self, int64_t world, int64_t n_tok,
+                           int64_t width, int64_t s_cap, const uint32_t* epoch, void* stream);
+int     exl3b200_tp_pull(const uint64_t* peers, const int64_t* offs, int64_t self, int64_t world, int64_t n_tok,
+                         int64_t width, int64_t s_cap, float* out, int64_t out_pitch, const uint32_t* epoch,
+                         int32_t* status, void* stream);
+
 /* The device error word of the current device: nonzero once a bounded wait inside a kernel gave up (the
  * launch then finished without a valid result). Reading it synchronises the device; `clear` resets it. Not
  * for a launch path. */

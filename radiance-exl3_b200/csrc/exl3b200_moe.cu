@@ -10,6 +10,7 @@
 #include <stdint.h>
 
 #include "exl3b200_dev.h"
+#include "exl3b200_gather.cuh"
 
 namespace {
 
@@ -237,14 +238,6 @@ __global__ void k_scatter_place(const int32_t* __restrict__ ids, int64_t n_pairs
 }
 
 // ------------------------------------------------------------------------------------------ gather
-__global__ void k_invert(const int32_t* __restrict__ sorted_tok, int64_t n_rows, int64_t n_pairs,
-                         int32_t* __restrict__ pos) {
-    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= n_rows) return;
-    const int32_t f = sorted_tok[i];
-    if (f >= 0 && f < n_pairs) pos[f] = (int32_t)i;
-}
-
 // One block a token; thread columns 4 at a time; slots in ascending order.
 __global__ void k_gather(const uint16_t* __restrict__ rows, int64_t pitch, const int32_t* __restrict__ pos,
                          const float* __restrict__ w, int top_k, int64_t width, float* __restrict__ y) {
@@ -266,40 +259,15 @@ __global__ void k_gather(const uint16_t* __restrict__ rows, int64_t pitch, const
     }
 }
 
-// One block a token, a thread 8 columns (16-byte loads of bf16 rows); each slot's row is loaded before any is
-// summed, then the slots are summed in ascending order exactly as k_gather does. rows 16-byte aligned with a pitch
-// of a multiple of 8 elements, width a multiple of 8, y 16-byte aligned (the host checks).
-constexpr int kGatherSlots = 16;
+// One block a token, a thread 8 columns (16-byte loads of bf16 rows): exl3b::gather_row8, the slots summed in
+// ascending order exactly as k_gather does. rows 16-byte aligned with a pitch of a multiple of 8 elements, width a
+// multiple of 8, y 16-byte aligned (the host checks).
 __global__ void k_gather_v8(const uint16_t* __restrict__ rows, int64_t pitch, const int32_t* __restrict__ pos,
                             const float* __restrict__ w, int top_k, int64_t width, float* __restrict__ y) {
     const int64_t t = blockIdx.x;
     for (int64_t n = 8 * (int64_t)threadIdx.x; n < width; n += 8 * (int64_t)blockDim.x) {
-        float acc[8] = { 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f };
-        for (int s0 = 0; s0 < top_k; s0 += kGatherSlots) {
-            uint4 r[kGatherSlots];
-            float ws[kGatherSlots];
-            bool live[kGatherSlots];
-#pragma unroll
-            for (int q = 0; q < kGatherSlots; ++q) {
-                live[q] = false;
-                if (s0 + q >= top_k) continue;
-                const int32_t i = pos[t * top_k + s0 + q];
-                if (i < 0) continue;
-                live[q] = true;
-                ws[q] = w[t * top_k + s0 + q];
-                r[q] = *reinterpret_cast<const uint4*>(rows + (int64_t)i * pitch + n);
-            }
-#pragma unroll
-            for (int q = 0; q < kGatherSlots; ++q) {
-                if (!live[q]) continue;
-                const uint32_t u[4] = { r[q].x, r[q].y, r[q].z, r[q].w };
-#pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    const uint16_t b = (uint16_t)(u[j >> 1] >> (16 * (j & 1)));
-                    acc[j] = __fadd_rn(acc[j], __fmul_rn(ws[q], __bfloat162float(__ushort_as_bfloat16(b))));
-                }
-            }
-        }
+        float acc[8];
+        exl3b::gather_row8(rows, pitch, pos, w, top_k, t, n, acc);
         float4* o = reinterpret_cast<float4*>(y + t * width + n);
         o[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
         o[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
@@ -399,7 +367,7 @@ int exl3b200_moe_gather(const uint16_t* rows, int64_t row_pitch, const int32_t* 
     int32_t* pos = static_cast<int32_t*>(work);
     if (cudaMemsetAsync(pos, 0xFF, (size_t)(n_tok * top_k) * 4, st) != cudaSuccess) return -6;
     if (n_rows > 0)
-        k_invert<<<(unsigned)((n_rows + 255) / 256), 256, 0, st>>>(sorted_tok, n_rows, n_tok * top_k, pos);
+        exl3b::k_invert<<<(unsigned)((n_rows + 255) / 256), 256, 0, st>>>(sorted_tok, n_rows, n_tok * top_k, pos);
     if (aligned16(rows) && row_pitch % 8 == 0 && width % 8 == 0 && aligned16(y))
         k_gather_v8<<<(unsigned)n_tok, 256, 0, st>>>(rows, row_pitch, pos, w, (int)top_k, width, y);
     else
@@ -435,7 +403,7 @@ int exl3b200_moe_gather_noalloc(const uint16_t* rows, int64_t row_pitch, const i
     // the map starts as "no row" (-1) for every pair of this call; the array keeps the last call's contents
     if (cudaMemsetAsync(pos, 0xFF, (size_t)(n_tok * top_k) * 4, st) != cudaSuccess) return -6;
     if (n_rows > 0)
-        k_invert<<<(unsigned)((n_rows + 255) / 256), 256, 0, st>>>(sorted_tok, n_rows, n_tok * top_k, pos);
+        exl3b::k_invert<<<(unsigned)((n_rows + 255) / 256), 256, 0, st>>>(sorted_tok, n_rows, n_tok * top_k, pos);
     if (aligned16(rows) && row_pitch % 8 == 0 && width % 8 == 0 && aligned16(y))
         k_gather_v8<<<(unsigned)n_tok, 256, 0, st>>>(rows, row_pitch, pos, w, (int)top_k, width, y);
     else

@@ -22,6 +22,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "exl3b200_sys.cuh"
+
 namespace {
 
 constexpr uint64_t kP2pWaitNs = 5000000000ull;   // a rank waits at most 5 s for its peers, then reports
@@ -30,19 +32,10 @@ struct Win {
     int64_t rows, meta, yback, ctl, done, sink;   // byte offsets in every window (sink: one spare row)
 };
 
-__device__ __forceinline__ uint64_t gtimer() {
-    uint64_t t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    return t;
-}
-__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
-    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
-    uint32_t v;
-    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
+using exl3b::gtimer;
+using exl3b::ld_acquire_sys;
+using exl3b::st_release_sys;
+
 __device__ __forceinline__ uint8_t* wbase(const uint64_t* peers, int r) {
     return reinterpret_cast<uint8_t*>(peers[r]);
 }

@@ -106,34 +106,21 @@ class DeviceOps:
         return n + 2
 
 
-class P2pWindow:
-    """This rank's peer-memory window (exl3b200_ep_window_*: device memory exported by CUDA IPC) and every peer's,
-    mapped here. Layout (the same on every rank, byte offsets): rows [world][t_cap][H] f16 | meta [world][p_cap]
-    u32 | yback [p_cap][H] bf16 | ctl [world][8] u32 | done [2] u32 | sink [H] bf16."""
+class IpcWindow:
+    """This rank's peer-memory window (exl3b200_ep_window_*: device memory, zeroed, exported by CUDA IPC) and every
+    peer's, mapped here: `ptrs[r]` rank r's base as this rank sees it (its own for itself), `peers` the same as a
+    device int64 table. `offs` the layout's byte offsets (the same on every rank). Built and closed collectively."""
 
-    def __init__(self, nat, dist, group, rank, world, t_cap, p_cap, hidden, device):
+    def __init__(self, nat, dist, group, rank, world, offs, nbytes, device):
         import torch
-        al = lambda n: (n + 255) // 256 * 256  # noqa: E731
         self.nat, self.dist, self.group, self.rank, self.world = nat, dist, group, rank, world
-        o_rows = 0
-        o_meta = al(world * t_cap * hidden * 2)
-        o_yback = o_meta + al(world * p_cap * 4)
-        o_ctl = o_yback + al(p_cap * hidden * 2)
-        o_done = o_ctl + al(world * 32)
-        o_sink = o_done + 256
-        self.offs = (C.c_int64 * 6)(o_rows, o_meta, o_yback, o_ctl, o_done, o_sink)
-        self.base = nat.window_alloc(o_sink + al(hidden * 2))
+        self.offs = (C.c_int64 * len(offs))(*offs)
+        self.base = nat.window_alloc(nbytes)
         handles = [None] * world
         dist.all_gather_object(handles, nat.window_handle(self.base), group=group)
         self.ptrs = [self.base if r == rank else nat.window_open(handles[r]) for r in range(world)]
         self.peers = torch.tensor(self.ptrs, dtype=torch.int64, device=device)
         dist.barrier(group=group)
-
-    def rows_ptr(self):
-        return self.base + self.offs[0]
-
-    def yback_ptr(self):
-        return self.base + self.offs[2]
 
     def close(self):
         """Collective: unmap the peers' windows, then (after every rank has) free this one."""
@@ -145,6 +132,31 @@ class P2pWindow:
         self.dist.barrier(group=self.group)
         self.nat.window_free(self.base)
         self.base = None
+
+
+def _al(n):
+    return (n + 255) // 256 * 256
+
+
+class P2pWindow(IpcWindow):
+    """The expert-parallel window. Layout (byte offsets): rows [world][t_cap][H] f16 | meta [world][p_cap] u32 |
+    yback [p_cap][H] bf16 | ctl [world][8] u32 | done [2] u32 | sink [H] bf16."""
+
+    def __init__(self, nat, dist, group, rank, world, t_cap, p_cap, hidden, device):
+        o_rows = 0
+        o_meta = _al(world * t_cap * hidden * 2)
+        o_yback = o_meta + _al(world * p_cap * 4)
+        o_ctl = o_yback + _al(p_cap * hidden * 2)
+        o_done = o_ctl + _al(world * 32)
+        o_sink = o_done + 256
+        super().__init__(nat, dist, group, rank, world, (o_rows, o_meta, o_yback, o_ctl, o_done, o_sink),
+                         o_sink + _al(hidden * 2), device)
+
+    def rows_ptr(self):
+        return self.base + self.offs[0]
+
+    def yback_ptr(self):
+        return self.base + self.offs[2]
 
 
 class EpLayer:

@@ -47,6 +47,10 @@ class Native:
         L.exl3b200_moe_down_rows.argtypes = [_VP, _VP, _VP]
         L.exl3b200_p2p_begin.argtypes = [_VP, _VP]
         L.exl3b200_moe_op_live.argtypes = [_VP, _I, _VP, _VP]
+        L.exl3b200_tp_gather_rs.argtypes = [_VP, _I64, _VP, _I64, _VP, _I64, _I64, _I64, _VP, _VP, _VP, _I64, _I64,
+                                            _I64, _VP, _VP, _VP]
+        L.exl3b200_tp_reduce.argtypes = [_VP, _VP, _I64, _I64, _I64, _I64, _I64, _VP, _VP]
+        L.exl3b200_tp_pull.argtypes = [_VP, _VP, _I64, _I64, _I64, _I64, _I64, _VP, _I64, _VP, _VP, _VP]
 
     @staticmethod
     def _check(rc, what):
@@ -182,3 +186,18 @@ class Native:
 
     def moe_op_live(self, args_ref, down, row_dst, stream=0):
         self._check(self.lib.exl3b200_moe_op_live(args_ref, down, row_dst, stream), "exl3b200_moe_op_live")
+
+    # ---- the width split over peer memory (exl3b200_tp.cu)
+    def tp_gather_rs(self, rows, row_pitch, sorted_tok, n_rows, w, n_tok, top_k, width, work, peers, offs, rank,
+                     world, s_cap, epoch, status, stream=0):
+        self._check(self.lib.exl3b200_tp_gather_rs(rows, row_pitch, sorted_tok, n_rows, w, n_tok, top_k, width, work,
+                                                   peers, offs, rank, world, s_cap, epoch, status, stream),
+                    "exl3b200_tp_gather_rs")
+
+    def tp_reduce(self, peers, offs, rank, world, n_tok, width, s_cap, epoch, stream=0):
+        self._check(self.lib.exl3b200_tp_reduce(peers, offs, rank, world, n_tok, width, s_cap, epoch, stream),
+                    "exl3b200_tp_reduce")
+
+    def tp_pull(self, peers, offs, rank, world, n_tok, width, s_cap, out, out_pitch, epoch, status, stream=0):
+        self._check(self.lib.exl3b200_tp_pull(peers, offs, rank, world, n_tok, width, s_cap, out, out_pitch, epoch,
+                                              status, stream), "exl3b200_tp_pull")
