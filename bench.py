@@ -181,6 +181,50 @@ def time_reference(threads, steps, warmup, n_experts=4, T=2048):
 
 
 # ------------------------------------------------------------------------------------------ our arm
+def bitrate_sweep(plugin, hbm, tflops):
+    """Config 4: one EXL3 linear of out 4096 x in 1536 (and its transpose), K = 2..8, batch 1 and 256, each call the
+    moe_exl3_down row (n_expert 1, top_k 1, h_rot 0). Every timed call reads its own copy of the weights (copies
+    totalling over 3x the 126 MB L2, replayed as one CUDA graph), so each streams its record from HBM. Reports
+    microseconds a call, algorithmic GB/s (record + suh + svh) and TFLOP/s (2 * batch * out * in)."""
+    import torch
+    from exl3b200.layer import Linears
+    res = {}
+    st = torch.cuda.current_stream()
+    for R, Cc in ((4096, 1536), (1536, 4096)):
+        shape = {}
+        for K in range(2, 9):
+            for B in (1, 256):
+                n = int(np.ceil(3 * 126e6 / (R * Cc * K / 8)))
+                lin = Linears(plugin, R, Cc, K, B, n, seed=100 * K + B)
+                for i in range(n):
+                    lin.run(i, st.cuda_stream)
+                torch.cuda.synchronize()
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g):
+                    cs = torch.cuda.current_stream().cuda_stream
+                    for i in range(n):
+                        lin.run(i, cs)
+                for _ in range(3):
+                    g.replay()
+                reps = 5
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                for _ in range(reps):
+                    g.replay()
+                e1.record()
+                torch.cuda.synchronize()
+                us = e0.elapsed_time(e1) * 1e3 / (reps * n)
+                gbs = lin.bytes_per_call() / (us / 1e6) / 1e9
+                tf = lin.flops_per_call() / (us / 1e6) / 1e12
+                shape[f"K{K}_B{B}"] = {"us": round(us, 2), "gbs": round(gbs, 1), "frac_hbm": round(gbs / hbm, 3),
+                                       "tflops": round(tf, 2), "frac_tensor": round(tf / tflops, 4),
+                                       "band": "k_gemm_tc" if B >= 16 else "k_gemm_skinny", "copies": n}
+                del g, lin
+                torch.cuda.synchronize()
+        res[f"out{R}_in{Cc}"] = shape
+    return res
+
+
 def bench_ours(args, rank, world, local_rank):
     import torch
     torch.cuda.set_device(local_rank)
@@ -418,6 +462,11 @@ def bench_ours(args, rank, world, local_rank):
             if graph_ok:
                 del gph
 
+    # ---- config 4: the bitrate sweep of one linear (1 GPU)
+    bitrates = None
+    if world == 1 and not args.no_sweep:
+        bitrates = bitrate_sweep(plugin, hbm, tflops)
+
     # ---- the CPU baseline (rank 0, one GPU): the reference library on a bounded sample
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -464,7 +513,7 @@ def bench_ours(args, rank, world, local_rank):
                      "other": {"gate_up_op_ms": round(gu_ms, 4), "k_prep_ms": round(prep_ms, 4),
                                "down_op_ms": round(dn_ms, 4)}},
         "clocks": clk, "gpu_launches": int(launches_per_step * args.steps),
-        "e2e": e2e, "cpu_baseline": cpu, "sweep": sweep, "wall_s": round(wall, 3),
+        "e2e": e2e, "cpu_baseline": cpu, "sweep": sweep, "bitrate_sweep": bitrates, "wall_s": round(wall, 3),
         "ep_phases_ms": ep_phases,
     }
     return line

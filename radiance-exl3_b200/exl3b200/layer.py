@@ -242,10 +242,11 @@ class MoeLayer:
         pairs = (2 * self.W if op == "gate_up" else self.H) // 256
         return rows // live >= 16 or live * pairs >= 64
 
-    def band_name(self, op, T):
-        """Which kernels serve one op at T tokens (gate_up's input rotation runs once a row in k_prep on the
-        tensor-core band)."""
-        tc = self._tc(op, T * self.k)
+    def band_name(self, op, T, rows=None):
+        """Which kernels serve one op at T tokens, or over `rows` sorted rows (gate_up's input rotation runs once a
+        row in k_prep on the tensor-core band)."""
+        rows = T * self.k if rows is None else rows
+        tc = self._tc(op, rows)
         if op == "gate_up":
             return "moe_exl3_gate_up row: k_prep + k_gemm_tc" if tc else "moe_exl3_gate_up row: k_gemm_skinny"
         return "moe_exl3_down row: k_gemm_tc" if tc else "moe_exl3_down row: k_gemm_skinny"
@@ -287,3 +288,77 @@ class MoeLayer:
     def live_experts(self):
         off = self.offset.cpu().numpy()
         return int((np.diff(off) > 0).sum())
+
+
+class Linears:
+    """`n` independent EXL3 linears of one shape (config 4: out `rows`, in `cols`, K bits), each served by one call of
+    the moe_exl3_down row as the engine issues a single linear (n_expert 1, top_k 1, every input row routed to it,
+    h_rot 0: the input rotation inside the op), over `batch` input rows. The copies exist so a timed loop over them
+    streams every call's weights from HBM rather than L2. Weights as the layer's: uniform random record words, suh
+    +-1, svh +-|N(0,1)| * 0.02."""
+
+    def __init__(self, plugin, rows, cols, bits, batch, n, codebook="mul1", seed=0, device="cuda"):
+        import torch
+        self.torch, self.plugin = torch, plugin
+        self.rows, self.cols, self.bits, self.B, self.n, self.codebook = rows, cols, bits, batch, n, codebook
+        dev = self.dev = torch.device(device)
+        g = torch.Generator(device=dev)
+        g.manual_seed(seed)
+        self.rec_bytes = rows * cols * bits // 8
+        self.rec = torch.randint(-32768, 32768, (n, self.rec_bytes // 2), generator=g, device=dev,
+                                 dtype=torch.int32).to(torch.int16)
+        sign = (torch.randint(0, 2, (n, 1, cols), generator=g, device=dev) * 2 - 1).to(torch.float16)
+        self.suh = sign
+        s2 = (torch.randint(0, 2, (n, rows, 1), generator=g, device=dev) * 2 - 1).float()
+        self.svh = (s2 * torch.randn((n, rows, 1), generator=g, device=dev).abs() * 0.02).to(torch.float16)
+        self.tab = torch.tensor([[self.rec[i].data_ptr()] for i in range(n)], dtype=torch.int64, device=dev)
+        self.x = torch.randn((batch, cols), generator=g, device=dev).to(torch.float16)
+        self.y = torch.empty((batch, rows), dtype=torch.bfloat16, device=dev)
+        self.sorted_tok = torch.arange(batch, dtype=torch.int32, device=dev)
+        self.offset = torch.tensor([0, batch], dtype=torch.int32, device=dev)
+        self.row = plugin.row("moe_exl3_down")
+        params = {"M": batch, "N": rows, "K": cols, "n_expert": 1, "top_k": 1, "dtype": f"exl3k{bits}",
+                  "codebook": codebook, "h_rot": 0}
+        P, nP, kp = rad.make_params(params)
+        enc = X.encoding(bits, codebook, stacked=False)
+        sel = C.c_int(0)
+        pt = rad.tensor(0, rad.DT_UK[bits], [rows, cols])
+        L = rad.RadLayout()
+        rc = self.row.layout(P, nP, 1, C.byref(enc), C.byref(sel), C.byref(pt), 1, C.byref(L))
+        if rc != 0 or L.bytes != self.rec_bytes:
+            raise RuntimeError(f"layout hook: rc {rc}, bytes {L.bytes} (expected {self.rec_bytes})")
+        rec_dtype = int(L.dtype)
+        absent = rad.RadTensor()
+        self._keep, self.args = [kp], []
+        for i in range(n):
+            P, nP, kp = rad.make_params(params)
+            ts = [rad.tensor(self.x.data_ptr(), rad.DT["f16"], [batch, cols]),
+                  rad.tensor(self.tab[i].data_ptr(), rec_dtype, [1, rows, cols], [0, cols, 1]),
+                  rad.tensor(self.suh[i].data_ptr(), rad.DT["f16"], [1, 1, cols]),
+                  rad.tensor(self.svh[i].data_ptr(), rad.DT["f16"], [1, rows, 1]),
+                  rad.tensor(self.sorted_tok.data_ptr(), rad.DT["i32"], [batch]),
+                  rad.tensor(self.offset.data_ptr(), rad.DT["i32"], [2]),
+                  absent, absent, absent,
+                  rad.tensor(self.y.data_ptr(), rad.DT["bf16"], [batch, rows])]
+            arr = (rad.RadTensor * len(ts))(*ts)
+            a = rad.RadArgs()
+            a.t, a.n_t, a.p, a.n_p, a.world_size = arr, len(ts), P, nP, 1
+            need = int(self.row.scratch(C.byref(a))) if self.row.scratch else 0
+            if need > 0:
+                buf = torch.empty(need, dtype=torch.uint8, device=dev)
+                self._keep.append(buf)
+                a.scratch, a.scratch_bytes = buf.data_ptr(), need
+            self._keep.extend([P, kp, arr])
+            self.args.append(a)
+
+    def run(self, i, stream):
+        rc = self.row.launch(C.byref(self.args[i]), stream)
+        if rc != 0:
+            raise RuntimeError(f"moe_exl3_down launch: {rc}")
+
+    def bytes_per_call(self):
+        """Algorithmic bytes of one call: the record plus suh and svh (read once)."""
+        return self.rec_bytes + 2 * self.cols + 2 * self.rows
+
+    def flops_per_call(self):
+        return 2 * self.B * self.rows * self.cols

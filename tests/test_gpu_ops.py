@@ -122,6 +122,16 @@ OPS = [
     dict(op="moe_exl3_down", M=200, top_k=10, n_expert=64, geom=[(2048, 512)], bits=4, codebook="mul1", h_rot=1),
     dict(op="moe_exl3_down_mod4", M=64, top_k=2, n_expert=8, geom=[(256, 128), (512, 128), (256, 256), (256, 128)],
          bits=7, codebook="mcg"),
+] + [
+    # config 4, the bitrate sweep's linear: out 4096 x in 1536 (and the transpose), K = 2..8, one expert, every row
+    # routed to it (the decode band at batch 1, the tensor-core band at batch 32 / 256)
+    dict(op="moe_exl3_down", M=M, top_k=1, n_expert=1, geom=[geom], bits=K, codebook="mul1")
+    for K in range(2, 9) for M, geom in ((1, (4096, 1536)), (32, (4096, 1536)))
+] + [
+    dict(op="moe_exl3_down", M=1, top_k=1, n_expert=1, geom=[(1536, 4096)], bits=4, codebook="mul1"),
+    dict(op="moe_exl3_down", M=256, top_k=1, n_expert=1, geom=[(1536, 4096)], bits=4, codebook="mul1"),
+    dict(op="moe_exl3_down", M=256, top_k=1, n_expert=1, geom=[(4096, 1536)], bits=2, codebook="mul1"),
+    dict(op="moe_exl3_down", M=256, top_k=1, n_expert=1, geom=[(4096, 1536)], bits=8, codebook="mul1"),
 ]
 
 
