@@ -164,6 +164,40 @@ __device__ __forceinline__ void place_chunk(const int32_t* ids, int64_t c0, int6
     }
 }
 
+// The same placement without the warp-by-warp walk: each warp's leader lanes record their expert's count in the
+// warp's row of `wcnt` ([32 warps][n_expert], shared, all zero on entry), one pass turns every expert's column into
+// the warps' first positions (and advances `run`), and every pair is then stored at once. Leaves `wcnt` zero.
+__device__ __forceinline__ void place_chunk_fast(const int32_t* ids, int64_t c0, int64_t n_pairs, int64_t base,
+                                                 int n_expert, int* run, int* wcnt, int32_t* sorted_tok) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
+    const int64_t f = c0 + tid;
+    const int e = f < n_pairs ? local_expert(ids[f], base, n_expert) : -1;
+    const unsigned peers = __match_any_sync(0xFFFFFFFFu, e);
+    const int rank = __popc(peers & ((1u << lane) - 1u));
+    const bool leader = lane == __ffs(peers) - 1;
+    if (e >= 0 && leader) wcnt[warp * n_expert + e] = __popc(peers);
+    __syncthreads();
+    for (int x = tid; x < n_expert; x += blockDim.x) {
+        int acc = run[x];
+        for (int w = 0; w < nw; ++w) {
+            const int c = wcnt[w * n_expert + x];
+            if (c) {
+                wcnt[w * n_expert + x] = acc;
+                acc += c;
+            }
+        }
+        run[x] = acc;
+    }
+    __syncthreads();
+    if (e >= 0) sorted_tok[wcnt[warp * n_expert + e] + rank] = (int32_t)f;
+    __syncthreads();
+    if (e >= 0 && leader) wcnt[warp * n_expert + e] = 0;
+    __syncthreads();
+}
+
+// The fast placement's table fits shared memory up to this many experts ([32][n_expert] ints).
+constexpr int kPlaceFastExperts = 1024;
+
 // The whole sort in one block (few pairs): histogram, scan, stable placement, tail of -1.
 __global__ void k_scatter_small(const int32_t* __restrict__ ids, int64_t n_pairs, int n_expert, int64_t base,
                                 int32_t* __restrict__ sorted_tok, int32_t* __restrict__ off) {
@@ -182,7 +216,16 @@ __global__ void k_scatter_small(const int32_t* __restrict__ ids, int64_t n_pairs
     for (int e = tid; e < n_expert; e += blockDim.x) off[e] = cnt[e];
     if (tid == 0) off[n_expert] = live;
     for (int64_t f = live + tid; f < n_pairs; f += blockDim.x) sorted_tok[f] = -1;
-    for (int64_t c0 = 0; c0 < n_pairs; c0 += blockDim.x) place_chunk(ids, c0, n_pairs, base, n_expert, cnt, sorted_tok);
+    if (n_expert <= kPlaceFastExperts) {
+        int* wcnt = sm + n_expert + 1;   // [32][n_expert]
+        for (int x = tid; x < 32 * n_expert; x += blockDim.x) wcnt[x] = 0;
+        __syncthreads();
+        for (int64_t c0 = 0; c0 < n_pairs; c0 += blockDim.x)
+            place_chunk_fast(ids, c0, n_pairs, base, n_expert, cnt, wcnt, sorted_tok);
+    } else {
+        for (int64_t c0 = 0; c0 < n_pairs; c0 += blockDim.x)
+            place_chunk(ids, c0, n_pairs, base, n_expert, cnt, sorted_tok);
+    }
 }
 
 // Large path, step 1: per-chunk histograms hist[b][e].
@@ -205,12 +248,19 @@ __global__ void k_scatter_hist(const int32_t* __restrict__ ids, int64_t n_pairs,
 __global__ void k_scatter_scan(int32_t* __restrict__ hist, int nb, int n_expert, int32_t* __restrict__ off) {
     extern __shared__ int sm[];   // [n_expert] totals
     const int tid = threadIdx.x;
+    constexpr int kB = 8;         // chunks a thread loads before it stores any (the loads overlap)
     for (int e = tid; e < n_expert; e += blockDim.x) {
         int acc = 0;
-        for (int b = 0; b < nb; ++b) {
-            const int v = hist[(int64_t)b * n_expert + e];
-            hist[(int64_t)b * n_expert + e] = acc;
-            acc += v;
+        for (int b0 = 0; b0 < nb; b0 += kB) {
+            int v[kB];
+#pragma unroll
+            for (int q = 0; q < kB; ++q) v[q] = b0 + q < nb ? hist[(int64_t)(b0 + q) * n_expert + e] : 0;
+#pragma unroll
+            for (int q = 0; q < kB; ++q)
+                if (b0 + q < nb) {
+                    hist[(int64_t)(b0 + q) * n_expert + e] = acc;
+                    acc += v[q];
+                }
         }
         sm[e] = acc;
     }
@@ -219,8 +269,17 @@ __global__ void k_scatter_scan(int32_t* __restrict__ hist, int nb, int n_expert,
     const int live = block_scan_excl(sm, n_expert, wtot);
     for (int e = tid; e < n_expert; e += blockDim.x) off[e] = sm[e];
     if (tid == 0) off[n_expert] = live;
-    for (int e = tid; e < n_expert; e += blockDim.x)
-        for (int b = 0; b < nb; ++b) hist[(int64_t)b * n_expert + e] += sm[e];
+    for (int e = tid; e < n_expert; e += blockDim.x) {
+        const int add = sm[e];
+        for (int b0 = 0; b0 < nb; b0 += kB) {
+            int v[kB];
+#pragma unroll
+            for (int q = 0; q < kB; ++q) v[q] = b0 + q < nb ? hist[(int64_t)(b0 + q) * n_expert + e] : 0;
+#pragma unroll
+            for (int q = 0; q < kB; ++q)
+                if (b0 + q < nb) hist[(int64_t)(b0 + q) * n_expert + e] = v[q] + add;
+        }
+    }
 }
 
 // Step 3: stable placement of each chunk from its first positions; the tail of -1.
@@ -230,8 +289,15 @@ __global__ void k_scatter_place(const int32_t* __restrict__ ids, int64_t n_pairs
     extern __shared__ int sm[];
     const int tid = threadIdx.x;
     for (int e = tid; e < n_expert; e += blockDim.x) sm[e] = hist[(int64_t)blockIdx.x * n_expert + e];
-    __syncthreads();
-    place_chunk(ids, (int64_t)blockIdx.x * kScatterChunk, n_pairs, base, n_expert, sm, sorted_tok);
+    if (n_expert <= kPlaceFastExperts) {
+        int* wcnt = sm + n_expert + 1;   // [32][n_expert]
+        for (int x = tid; x < 32 * n_expert; x += blockDim.x) wcnt[x] = 0;
+        __syncthreads();
+        place_chunk_fast(ids, (int64_t)blockIdx.x * kScatterChunk, n_pairs, base, n_expert, sm, wcnt, sorted_tok);
+    } else {
+        __syncthreads();
+        place_chunk(ids, (int64_t)blockIdx.x * kScatterChunk, n_pairs, base, n_expert, sm, sorted_tok);
+    }
     const int64_t live = off[n_expert];
     const int64_t f = (int64_t)blockIdx.x * kScatterChunk + tid;
     if (f >= live && f < n_pairs) sorted_tok[f] = -1;
@@ -342,8 +408,17 @@ int exl3b200_moe_scatter(const int32_t* ids, int64_t n_pairs, int64_t n_expert, 
     if (!ids || !sorted_tok || !expert_offset || n_pairs < 0 || n_expert < 1 || n_expert > 16384) return -12;
     cudaStream_t st = as_stream(stream);
     const size_t smem = (size_t)(n_expert + 1) * 4;
+    // the small sort and the placement also hold the fast placement's [32][n_expert] table when it fits
+    const size_t smem_place = smem + (n_expert <= kPlaceFastExperts ? (size_t)32 * n_expert * 4 : 0);
+    if (smem_place > 48 * 1024 &&
+        (cudaFuncSetAttribute(k_scatter_small, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_place) !=
+             cudaSuccess ||
+         cudaFuncSetAttribute(k_scatter_place, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_place) !=
+             cudaSuccess))
+        return -6;
     if (n_pairs <= kSmallPairs) {
-        k_scatter_small<<<1, 1024, smem, st>>>(ids, n_pairs, (int)n_expert, expert_base, sorted_tok, expert_offset);
+        k_scatter_small<<<1, 1024, smem_place, st>>>(ids, n_pairs, (int)n_expert, expert_base, sorted_tok,
+                                                     expert_offset);
         return cudaGetLastError() == cudaSuccess ? 0 : -6;
     }
     if (!work) return -5;
@@ -351,8 +426,8 @@ int exl3b200_moe_scatter(const int32_t* ids, int64_t n_pairs, int64_t n_expert, 
     int32_t* hist = static_cast<int32_t*>(work);
     k_scatter_hist<<<nb, kScatterChunk, smem, st>>>(ids, n_pairs, (int)n_expert, expert_base, hist);
     k_scatter_scan<<<1, 1024, smem, st>>>(hist, nb, (int)n_expert, expert_offset);
-    k_scatter_place<<<nb, kScatterChunk, smem, st>>>(ids, n_pairs, (int)n_expert, expert_base, hist, expert_offset,
-                                                     sorted_tok);
+    k_scatter_place<<<nb, kScatterChunk, smem_place, st>>>(ids, n_pairs, (int)n_expert, expert_base, hist,
+                                                           expert_offset, sorted_tok);
     return cudaGetLastError() == cudaSuccess ? 0 : -6;
 }
 

@@ -253,6 +253,30 @@ def test_router_and_scatter(dev, native, T, E, k):
     assert np.array_equal(st.cpu().numpy(), st_want)
 
 
+@pytest.mark.parametrize("n_pairs,E,base,skew", [(8192, 512, 0, 0.0), (8193, 512, 0, 0.0), (5000, 64, 32, 0.5),
+                                                 (163840, 64, 0, 0.0), (20000, 512, 0, 0.6), (50000, 2048, 100, 0.0),
+                                                 (3000, 1024, 0, 0.9), (1, 512, 0, 0.0)])
+def test_scatter_is_the_stable_sort(dev, native, n_pairs, E, base, skew):
+    """The counting sort to the bit on both paths (one block up to 8192 pairs, chunked beyond), the table-based
+    placement (up to 1024 experts) and the warp-by-warp one (more), skewed routing (most pairs on one expert),
+    ids outside [base, base + E) and -1 dropped."""
+    rng = np.random.default_rng(n_pairs + E)
+    ids = rng.integers(base - 4, base + E + 4, size=n_pairs).astype(np.int32)
+    hot = rng.random(n_pairs) < skew
+    ids[hot] = base + 3
+    ids[rng.random(n_pairs) < 0.03] = -1
+    st_want, off_want = X.stable_scatter(ids, E, expert_base=base)
+    ids_d = torch.from_numpy(ids).to(dev)
+    st = torch.empty(n_pairs, dtype=torch.int32, device=dev)
+    off = torch.empty(E + 1, dtype=torch.int32, device=dev)
+    work = torch.empty(max(1, native.scatter_work_bytes(n_pairs, E)), dtype=torch.uint8, device=dev)
+    for _ in range(2):     # twice: the same bits again
+        native.moe_scatter(ids_d.data_ptr(), n_pairs, E, base, st.data_ptr(), off.data_ptr(), work.data_ptr())
+        torch.cuda.synchronize()
+        assert np.array_equal(off.cpu().numpy(), off_want)
+        assert np.array_equal(st.cpu().numpy(), st_want)
+
+
 def test_gather(dev, native, orc):
     rng = np.random.default_rng(9)
     T, k, E, width = 37, 4, 16, 256
