@@ -11,7 +11,7 @@
 
 namespace exl3b {
 
-constexpr int kGatherSlots = 16;
+constexpr int kGatherSlots = 8;
 
 // pos[f] = the sorted row of flat (token, slot) pair f (pos prefilled with -1: a pair no row holds stays -1).
 static __global__ void k_invert(const int32_t* __restrict__ sorted_tok, int64_t n_rows, int64_t n_pairs,

@@ -58,8 +58,9 @@ __global__ void k_decode_what(const uint32_t* __restrict__ record, int64_t rows,
 }
 
 // ------------------------------------------------------------------------------------------ prep
-// A grid-stride pass over (sorted row, group of four 128-blocks) tasks, one warp a task and eight lanes a block, the
-// expert offsets staged once a CTA in shared memory (the owner of a row is a binary search there). gate_up
+// A pass over (sorted row, group of four 128-blocks) tasks, one warp a task and eight lanes a block, each warp a
+// contiguous run of tasks; the expert offsets staged once a CTA in shared memory (the owner of a row is a binary
+// search there, once a row). gate_up
 // (moe_exl3_prep_gu, and the tensor-core path's xr): the token row a[sorted_tok / top_k] rotated with suh into
 // [0, C) and with suh.1 into [C, 2C) of row i; rows outside the runs are not written; a row whose sorted_tok is
 // negative is zero across 2C (docs/OPS-exl3.md:128-142). down (h_rot 0 on the tensor-core path): row i of h rotated
@@ -151,20 +152,38 @@ __global__ void __launch_bounds__(kPrepWarps * 32) k_prep(const Exl3bOp op, uint
     const bool xvec = al16(op.x) && (op.x_pitch % 8) == 0;
     const bool yvec = al16(dst_base) && (dst_pitch % 8) == 0;
     const uint32_t n_task = (uint32_t)((hi - lo) * ngrp);      // < 2^31 (the host checks)
-    for (uint32_t task = blockIdx.x * kPrepWarps + w; task < n_task; task += gridDim.x * kPrepWarps) {
+    // each warp a contiguous run of tasks (group fastest), so consecutive tasks share their row and the row's set-up
+    // (owner search, pointers, token) is done once a row; the runs differ by at most one task
+    const uint64_t n_warps = (uint64_t)gridDim.x * kPrepWarps, gw = (uint64_t)blockIdx.x * kPrepWarps + w;
+    const uint32_t t_begin = (uint32_t)(gw * n_task / n_warps), t_end = (uint32_t)((gw + 1) * n_task / n_warps);
+    int64_t row = -1;
+    ExpertView ev{};
+    const uint16_t *src = nullptr, *s0 = nullptr, *s1 = nullptr;
+    uint16_t* y = nullptr;
+    int32_t tok = -1;
+    bool svec = false;
+    for (uint32_t task = t_begin; task < t_end; ++task) {
         const uint32_t rr = task / (uint32_t)ngrp;
         const int64_t i = lo + rr;
-        int a = 0, b = (int)op.n_expert;               // the owner: largest e with off[e] <= i
-        while (b - a > 1) {
-            const int mid = (a + b) >> 1;
-            if (s_off[mid] <= i) a = mid; else b = mid;
+        if (i != row) {
+            row = i;
+            int a = 0, b = (int)op.n_expert;           // the owner: largest e with off[e] <= i
+            while (b - a > 1) {
+                const int mid = (a + b) >> 1;
+                if (s_off[mid] <= i) a = mid; else b = mid;
+            }
+            ev = expert_view(op, a);
+            y = dst_base + i * dst_pitch;
+            tok = op.sorted_tok[i];
+            const int64_t src_row = gu ? (int64_t)(tok / op.top_k) : i;
+            src = static_cast<const uint16_t*>(op.x) + src_row * op.x_pitch;
+            s0 = static_cast<const uint16_t*>(tab_entry(op.cls[ev.c].suh, ev.j));
+            s1 = gu ? static_cast<const uint16_t*>(tab_entry(op.cls[ev.c].suh1, ev.j)) : s0;
+            svec = al16(s0) && al16(s1);
         }
-        const ExpertView ev = expert_view(op, a);
         const int64_t blk = (int64_t)(task - rr * (uint32_t)ngrp) * 4 + bq;
         const bool mine = blk * 128 < ev.C;            // lanes past the class's width idle (shuffles stay whole)
         const int64_t c = (mine ? blk : 0) * 128 + 16 * l8;
-        uint16_t* y = dst_base + i * dst_pitch;
-        const int32_t tok = op.sorted_tok[i];
         if (tok < 0) {
             float z[16];
 #pragma unroll
@@ -175,11 +194,6 @@ __global__ void __launch_bounds__(kPrepWarps * 32) k_prep(const Exl3bOp op, uint
             }
             continue;
         }
-        const int64_t src_row = gu ? (int64_t)(tok / op.top_k) : i;
-        const uint16_t* src = static_cast<const uint16_t*>(op.x) + src_row * op.x_pitch;
-        const uint16_t* s0 = static_cast<const uint16_t*>(tab_entry(op.cls[ev.c].suh, ev.j));
-        const uint16_t* s1 = gu ? static_cast<const uint16_t*>(tab_entry(op.cls[ev.c].suh1, ev.j)) : s0;
-        const bool svec = al16(s0) && al16(s1);
         // the two halves one after the other: 16 values live a lane, 4 CTAs an SM
         uint32_t hx[8], hs[8];
         float va[16];

@@ -17,7 +17,7 @@ namespace {
 __device__ int32_t g_err_word;   // set by a kernel whose bounded wait gave up
 
 constexpr int kScatterChunk = 1024;   // pairs a block of the large-sort path
-constexpr int kSmallPairs = 8192;     // at most this many pairs: one block does the whole sort
+constexpr int kSmallPairs = 2048;     // at most this many pairs: one block does the whole sort
 
 // ------------------------------------------------------------------------------------------ router
 // One warp a token: softmax over n_expert logits (max, then sum of exp in lane-strided order reduced by a
@@ -59,8 +59,22 @@ __global__ void k_router_topk(const float* __restrict__ logits, int64_t n_tok, i
     }
 }
 
+// An order-preserving 32-bit key of a logit: larger value, larger key; -0 keyed as +0 (they compare equal); NaN 0,
+// never chosen (a NaN compares false, as in k_router_topk). fkey_inv gives the value back.
+__device__ __forceinline__ uint32_t fkey(float f) {
+    if (f != f) return 0u;
+    const uint32_t b = __float_as_uint(f == 0.f ? 0.f : f);
+    return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+__device__ __forceinline__ float fkey_inv(uint32_t k) {
+    return __uint_as_float((k & 0x80000000u) ? (k & 0x7FFFFFFFu) : ~k);
+}
+
 // The same router with the token's logits held in registers (RPL a lane, n_expert <= 32 * RPL): one read of the
-// row, then softmax and the top_k rounds on registers. Same reductions in the same order as k_router_topk.
+// row, the softmax's max and sum in k_router_topk's order, then top_k rounds of a warp-wide redux over the lanes'
+// current bests -- the largest key, then the lowest expert id holding it (the same choice as k_router_topk's
+// argmax: larger logit first, lower id on a tie). Only the lane that gave up its best looks for its next one; lane r
+// keeps round r's pick and the lanes write the ids and weights together at the end.
 template <int RPL>
 __global__ void k_router_topk_reg(const float* __restrict__ logits, int64_t n_tok, int n_expert, int top_k,
                                   int32_t* __restrict__ ids, float* __restrict__ w) {
@@ -84,26 +98,47 @@ __global__ void k_router_topk_reg(const float* __restrict__ logits, int64_t n_to
     for (int q = 0; q < RPL; ++q)
         if (lane + 32 * q < n_expert) s += expf(v[q] - mx);
     for (int m = 16; m; m >>= 1) s += __shfl_xor_sync(0xFFFFFFFFu, s, m);
-    uint32_t taken = 0;                     // bit q: expert lane + 32 q already chosen
-    for (int r = 0; r < top_k; ++r) {
-        float best = -INFINITY;
-        int bid = 0x7FFFFFFF;
+    uint32_t key[RPL];
 #pragma unroll
-        for (int q = 0; q < RPL; ++q) {
-            const int e = lane + 32 * q;
-            if (e >= n_expert || ((taken >> q) & 1u)) continue;
-            if (v[q] > best || (v[q] == best && e < bid)) { best = v[q]; bid = e; }
+    for (int q = 0; q < RPL; ++q) key[q] = lane + 32 * q < n_expert ? fkey(v[q]) : 0u;
+    // this lane's best: the largest key (a pairwise tree), then the lowest q holding it
+    uint32_t bk;
+    int bq;
+    auto local_best = [&]() {
+        uint32_t m[RPL];
+#pragma unroll
+        for (int q = 0; q < RPL; ++q) m[q] = key[q];
+#pragma unroll
+        for (int h = RPL / 2; h > 0; h >>= 1)
+#pragma unroll
+            for (int q = 0; q < h; ++q) m[q] = max(m[q], m[q + h]);
+        bk = m[0];
+        bq = 0;
+#pragma unroll
+        for (int q = RPL - 1; q >= 0; --q)
+            if (key[q] == bk) bq = q;
+    };
+    local_best();
+    int my_id = -1;
+    float my_val = 0.f;
+    for (int r = 0; r < top_k; ++r) {
+        const uint32_t gk = __reduce_max_sync(0xFFFFFFFFu, bk);
+        const uint32_t cand = (bk == gk && gk != 0u) ? (uint32_t)(lane + 32 * bq) : 0xFFFFFFFFu;
+        const uint32_t gid = __reduce_min_sync(0xFFFFFFFFu, cand);
+        if (lane == r) {
+            my_id = gid == 0xFFFFFFFFu ? -1 : (int)gid;
+            my_val = fkey_inv(gk);
         }
-        for (int m = 16; m; m >>= 1) {
-            const float ov = __shfl_xor_sync(0xFFFFFFFFu, best, m);
-            const int oid = __shfl_xor_sync(0xFFFFFFFFu, bid, m);
-            if (ov > best || (ov == best && oid < bid)) { best = ov; bid = oid; }
+        if (gid != 0xFFFFFFFFu && (int)(gid & 31u) == lane) {
+#pragma unroll
+            for (int q = 0; q < RPL; ++q)
+                if (q == (int)(gid >> 5)) key[q] = 0u;
+            local_best();
         }
-        if (bid != 0x7FFFFFFF && (bid & 31) == lane) taken |= 1u << (bid >> 5);
-        if (lane == 0) {
-            ids[t * top_k + r] = bid == 0x7FFFFFFF ? -1 : bid;
-            w[t * top_k + r] = bid == 0x7FFFFFFF ? 0.f : expf(best - mx) / s;
-        }
+    }
+    if (lane < top_k) {
+        ids[t * top_k + lane] = my_id;
+        w[t * top_k + lane] = my_id < 0 ? 0.f : expf(my_val - mx) / s;
     }
 }
 

@@ -253,7 +253,29 @@ def test_router_and_scatter(dev, native, T, E, k):
     assert np.array_equal(st.cpu().numpy(), st_want)
 
 
-@pytest.mark.parametrize("n_pairs,E,base,skew", [(8192, 512, 0, 0.0), (8193, 512, 0, 0.0), (5000, 64, 32, 0.5),
+@pytest.mark.parametrize("T,E,k", [(7, 512, 10), (300, 1024, 32), (5, 256, 8), (9, 2000, 4), (64, 40, 32)])
+def test_router_ties_zeros_and_infinities(dev, native, T, E, k):
+    """The top-k choice on ties (logits on a coarse grid), +0 and -0 (equal: the lower id first), -inf logits, and
+    every register width (256 / 512 / 1024 experts) plus the generic kernel (2000): ids exactly numpy's stable
+    argsort of -logits, weights the softmax."""
+    rng = np.random.default_rng(T * E + k)
+    logits = (np.round(rng.standard_normal((T, E)) * 2) / 2).astype(np.float32)
+    logits[rng.random((T, E)) < 0.05] = 0.0
+    logits[rng.random((T, E)) < 0.05] = -0.0
+    logits[rng.random((T, E)) < 0.02] = -np.inf
+    lg = torch.from_numpy(logits).to(dev)
+    ids = torch.empty((T, k), dtype=torch.int32, device=dev)
+    w = torch.empty((T, k), dtype=torch.float32, device=dev)
+    native.router_topk(lg.data_ptr(), T, E, k, ids.data_ptr(), w.data_ptr())
+    torch.cuda.synchronize()
+    want_ids = np.argsort(-logits, axis=1, kind="stable")[:, :k]
+    assert np.array_equal(ids.cpu().numpy(), want_ids)
+    p = np.exp(logits.astype(np.float64) - logits.max(1, keepdims=True))
+    p /= p.sum(1, keepdims=True)
+    assert np.allclose(w.cpu().numpy(), np.take_along_axis(p, want_ids, 1), rtol=1e-5, atol=1e-7)
+
+
+@pytest.mark.parametrize("n_pairs,E,base,skew",[(8192, 512, 0, 0.0), (8193, 512, 0, 0.0), (5000, 64, 32, 0.5),
                                                  (163840, 64, 0, 0.0), (20000, 512, 0, 0.6), (50000, 2048, 100, 0.0),
                                                  (3000, 1024, 0, 0.9), (1, 512, 0, 0.0)])
 def test_scatter_is_the_stable_sort(dev, native, n_pairs, E, base, skew):
