@@ -1,5 +1,5 @@
 // exl3b200_p2p.cu -- expert parallelism over peer memory: the dispatch and the combine write straight into the
-// other ranks' memory over NVLink (plain stores to CUDA-IPC-mapped pointers; no TMA, no multicast), and each rank
+// other ranks' memory over NVLink (plain stores to CUDA-IPC-mapped pointers, no TMA), and each rank
 // learns that its peers' data has landed from per-(source, destination) epoch flags. sm_100a CUDA, extern "C".
 //
 // Every rank owns one "window" (cudaMalloc'ed here, exported by IPC handle, mapped by every peer), the same layout

@@ -4,7 +4,7 @@
 // (architectures/qwen4exp_exl3/rad_block_moe_exl3.h:438-470: "each rank computes its gate/up rows and its K slice of
 // down for every routed expert; the routing weight scales each partial and the all-reduce sums them"). The reference
 // engine sums with its all_reduce op; here the sum is fused into the gather as a reduce-scatter over NVLink followed
-// by an all-gather, all plain loads and stores to CUDA-IPC-mapped windows (no TMA, no multicast). sm_100a CUDA,
+// by an all-gather, all plain loads and stores to CUDA-IPC-mapped windows (no TMA). sm_100a CUDA,
 // extern "C".
 //
 // Tokens are cut into `world` contiguous slices of s = ceil(T / world) rows; rank o reduces slice o. Every rank's
