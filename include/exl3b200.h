@@ -73,6 +73,13 @@ int     exl3b200_router_topk(const float* logits, int64_t n_tok, int64_t n_exper
 int64_t exl3b200_moe_scatter_work_bytes(int64_t n_pairs, int64_t n_expert);
 int     exl3b200_moe_scatter(const int32_t* ids, int64_t n_pairs, int64_t n_expert, int64_t expert_base,
                              int32_t* sorted_tok, int32_t* expert_offset, void* work, void* stream);
+/* router_topk over n_route experts then moe_scatter of its ids over [expert_base, expert_base + n_expert), as the
+ * two calls above (the same results to the bit), in ONE launch when the tokens are few (n_tok <= 32, n_route <=
+ * 512, n_expert <= 1024): the decode-size step's router and sort in one block. `work` as moe_scatter's. No
+ * counterpart in the reference (the engine issues the two ops). */
+int     exl3b200_router_scatter(const float* logits, int64_t n_tok, int64_t n_route, int64_t top_k, int32_t* ids,
+                                float* w, int64_t n_expert, int64_t expert_base, int32_t* sorted_tok,
+                                int32_t* expert_offset, void* work, void* stream);
 int64_t exl3b200_moe_gather_work_bytes(int64_t n_tok, int64_t top_k);
 int     exl3b200_moe_gather(const uint16_t* rows, int64_t row_pitch, const int32_t* sorted_tok, int64_t n_rows,
                             const float* w, int64_t n_tok, int64_t top_k, int64_t width, float* y, void* work,

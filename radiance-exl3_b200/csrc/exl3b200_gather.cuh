@@ -22,9 +22,10 @@ static __global__ void k_invert(const int32_t* __restrict__ sorted_tok, int64_t 
     if (f >= 0 && f < n_pairs) pos[f] = (int32_t)i;
 }
 
+// pos_t, w_t: the token's top_k sorted rows (-1: no row) and weights.
 __device__ __forceinline__ void gather_row8(const uint16_t* __restrict__ rows, int64_t pitch,
-                                            const int32_t* __restrict__ pos, const float* __restrict__ w, int top_k,
-                                            int64_t t, int64_t n, float acc[8]) {
+                                            const int32_t* __restrict__ pos_t, const float* __restrict__ w_t,
+                                            int top_k, int64_t n, float acc[8]) {
 #pragma unroll
     for (int j = 0; j < 8; ++j) acc[j] = 0.f;
     for (int s0 = 0; s0 < top_k; s0 += kGatherSlots) {
@@ -35,10 +36,10 @@ __device__ __forceinline__ void gather_row8(const uint16_t* __restrict__ rows, i
         for (int q = 0; q < kGatherSlots; ++q) {
             live[q] = false;
             if (s0 + q >= top_k) continue;
-            const int32_t i = pos[t * top_k + s0 + q];
+            const int32_t i = pos_t[s0 + q];
             if (i < 0) continue;
             live[q] = true;
-            ws[q] = w[t * top_k + s0 + q];
+            ws[q] = w_t[s0 + q];
             r[q] = *reinterpret_cast<const uint4*>(rows + (int64_t)i * pitch + n);
         }
 #pragma unroll

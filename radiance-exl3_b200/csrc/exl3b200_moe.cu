@@ -76,12 +76,8 @@ __device__ __forceinline__ float fkey_inv(uint32_t k) {
 // argmax: larger logit first, lower id on a tie). Only the lane that gave up its best looks for its next one; lane r
 // keeps round r's pick and the lanes write the ids and weights together at the end.
 template <int RPL>
-__global__ void k_router_topk_reg(const float* __restrict__ logits, int64_t n_tok, int n_expert, int top_k,
-                                  int32_t* __restrict__ ids, float* __restrict__ w) {
-    const int lane = threadIdx.x & 31;
-    const int64_t t = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
-    if (t >= n_tok) return;
-    const float* l = logits + t * n_expert;
+__device__ __forceinline__ void route_warp(const float* __restrict__ l, int n_expert, int top_k, int lane,
+                                           int32_t* __restrict__ ids_t, float* __restrict__ w_t) {
     float v[RPL];
 #pragma unroll
     for (int q = 0; q < RPL; ++q) {
@@ -137,9 +133,17 @@ __global__ void k_router_topk_reg(const float* __restrict__ logits, int64_t n_to
         }
     }
     if (lane < top_k) {
-        ids[t * top_k + lane] = my_id;
-        w[t * top_k + lane] = my_id < 0 ? 0.f : expf(my_val - mx) / s;
+        ids_t[lane] = my_id;
+        w_t[lane] = my_id < 0 ? 0.f : expf(my_val - mx) / s;
     }
+}
+
+template <int RPL>
+__global__ void k_router_topk_reg(const float* __restrict__ logits, int64_t n_tok, int n_expert, int top_k,
+                                  int32_t* __restrict__ ids, float* __restrict__ w) {
+    const int64_t t = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+    if (t >= n_tok) return;
+    route_warp<RPL>(logits + t * n_expert, n_expert, top_k, threadIdx.x & 31, ids + t * top_k, w + t * top_k);
 }
 
 // Exclusive scan of cnt[0 .. n) in place (block-wide: each thread a run, warp shuffles, warp totals); returns the
@@ -234,9 +238,9 @@ __device__ __forceinline__ void place_chunk_fast(const int32_t* ids, int64_t c0,
 constexpr int kPlaceFastExperts = 1024;
 
 // The whole sort in one block (few pairs): histogram, scan, stable placement, tail of -1.
-__global__ void k_scatter_small(const int32_t* __restrict__ ids, int64_t n_pairs, int n_expert, int64_t base,
-                                int32_t* __restrict__ sorted_tok, int32_t* __restrict__ off) {
-    extern __shared__ int sm[];
+__device__ __forceinline__ void scatter_block(const int32_t* __restrict__ ids, int64_t n_pairs, int n_expert,
+                                              int64_t base, int32_t* __restrict__ sorted_tok,
+                                              int32_t* __restrict__ off, int* sm) {
     int* cnt = sm;                 // [n_expert + 1]
     const int tid = threadIdx.x;
     for (int e = tid; e <= n_expert; e += blockDim.x) cnt[e] = 0;
@@ -261,6 +265,29 @@ __global__ void k_scatter_small(const int32_t* __restrict__ ids, int64_t n_pairs
         for (int64_t c0 = 0; c0 < n_pairs; c0 += blockDim.x)
             place_chunk(ids, c0, n_pairs, base, n_expert, cnt, sorted_tok);
     }
+}
+
+__global__ void k_scatter_small(const int32_t* __restrict__ ids, int64_t n_pairs, int n_expert, int64_t base,
+                                int32_t* __restrict__ sorted_tok, int32_t* __restrict__ off) {
+    extern __shared__ int sm[];
+    scatter_block(ids, n_pairs, n_expert, base, sorted_tok, off, sm);
+}
+
+// A few tokens (at most one a warp): the router and the whole sort in one block -- the tokens routed by the warps,
+// then (their ids visible to the block after the barrier) the small sort. The same results as k_router_topk_reg
+// followed by k_scatter_small, one launch instead of two.
+constexpr int kFusedTokens = 32;
+template <int RPL>
+__global__ void __launch_bounds__(1024, 1) k_route_scatter_small(const float* __restrict__ logits, int64_t n_tok, int n_route, int top_k,
+                                      int32_t* __restrict__ ids, float* __restrict__ w, int n_expert, int64_t base,
+                                      int32_t* __restrict__ sorted_tok, int32_t* __restrict__ off) {
+    extern __shared__ int sm[];
+    const int warp = threadIdx.x >> 5;
+    if (warp < n_tok)
+        route_warp<RPL>(logits + (int64_t)warp * n_route, n_route, top_k, threadIdx.x & 31, ids + warp * top_k,
+                        w + warp * top_k);
+    __syncthreads();
+    scatter_block(ids, n_tok * top_k, n_expert, base, sorted_tok, off, sm);
 }
 
 // Large path, step 1: per-chunk histograms hist[b][e].
@@ -368,7 +395,33 @@ __global__ void k_gather_v8(const uint16_t* __restrict__ rows, int64_t pitch, co
     const int64_t t = blockIdx.x;
     for (int64_t n = 8 * (int64_t)threadIdx.x; n < width; n += 8 * (int64_t)blockDim.x) {
         float acc[8];
-        exl3b::gather_row8(rows, pitch, pos, w, top_k, t, n, acc);
+        exl3b::gather_row8(rows, pitch, pos + t * top_k, w + t * top_k, top_k, n, acc);
+        float4* o = reinterpret_cast<float4*>(y + t * width + n);
+        o[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+        o[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+    }
+}
+
+// A few tokens: one block a token finds its own slots' rows in sorted_tok (no inverse map, so no memset and no
+// k_invert launch), then sums them exactly as k_gather_v8 does. At most kGatherSmallSlots slots a token.
+constexpr int kGatherSmallSlots = 32;
+constexpr int64_t kGatherSmallRows = 4096;
+__global__ void k_gather_small(const uint16_t* __restrict__ rows, int64_t pitch, const int32_t* __restrict__ sorted_tok,
+                               int64_t n_rows, const float* __restrict__ w, int top_k, int64_t width,
+                               float* __restrict__ y) {
+    __shared__ int32_t pos[kGatherSmallSlots];
+    const int64_t t = blockIdx.x;
+    for (int s = threadIdx.x; s < top_k; s += blockDim.x) pos[s] = -1;
+    __syncthreads();
+    const int64_t f0 = t * top_k;
+    for (int64_t i = threadIdx.x; i < n_rows; i += blockDim.x) {
+        const int32_t f = sorted_tok[i];
+        if (f >= f0 && f < f0 + top_k) pos[f - f0] = (int32_t)i;
+    }
+    __syncthreads();
+    for (int64_t n = 8 * (int64_t)threadIdx.x; n < width; n += 8 * (int64_t)blockDim.x) {
+        float acc[8];
+        exl3b::gather_row8(rows, pitch, pos, w + t * top_k, top_k, n, acc);
         float4* o = reinterpret_cast<float4*>(y + t * width + n);
         o[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
         o[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
@@ -466,6 +519,36 @@ int exl3b200_moe_scatter(const int32_t* ids, int64_t n_pairs, int64_t n_expert, 
     return cudaGetLastError() == cudaSuccess ? 0 : -6;
 }
 
+int exl3b200_router_scatter(const float* logits, int64_t n_tok, int64_t n_route, int64_t top_k, int32_t* ids,
+                            float* w, int64_t n_expert, int64_t expert_base, int32_t* sorted_tok,
+                            int32_t* expert_offset, void* work, void* stream) {
+    if (!logits || !ids || !w || !sorted_tok || !expert_offset || n_tok < 0 || n_route < 1 || n_route > 4096 ||
+        top_k < 1 || top_k > 32 || top_k > n_route || n_expert < 1 || n_expert > 16384)
+        return -12;
+    if (n_tok == 0) return exl3b200_moe_scatter(ids, 0, n_expert, expert_base, sorted_tok, expert_offset, work, stream);
+    // fused for up to 32 tokens over at most 512 experts (a 1024-thread block holds 16 logits a lane in registers)
+    if (n_tok <= kFusedTokens && n_route <= 512 && n_tok * top_k <= kSmallPairs && n_expert <= kPlaceFastExperts) {
+        const size_t smem = (size_t)(n_expert + 1) * 4 + (size_t)32 * n_expert * 4;
+        cudaStream_t st = as_stream(stream);
+#define EXL3B_RS(R)                                                                                                  \
+    do {                                                                                                             \
+        auto kern = k_route_scatter_small<R>;                                                                        \
+        if (smem > 48 * 1024 &&                                                                                      \
+            cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)       \
+            return -6;                                                                                               \
+        kern<<<1, 1024, smem, st>>>(logits, n_tok, (int)n_route, (int)top_k, ids, w, (int)n_expert, expert_base,     \
+                                    sorted_tok, expert_offset);                                                      \
+    } while (0)
+        if (n_route <= 256) EXL3B_RS(8);
+        else EXL3B_RS(16);
+#undef EXL3B_RS
+        return cudaGetLastError() == cudaSuccess ? 0 : -6;
+    }
+    const int rc = exl3b200_router_topk(logits, n_tok, n_route, top_k, ids, w, stream);
+    if (rc != 0) return rc;
+    return exl3b200_moe_scatter(ids, n_tok * top_k, n_expert, expert_base, sorted_tok, expert_offset, work, stream);
+}
+
 int64_t exl3b200_moe_gather_work_bytes(int64_t n_tok, int64_t top_k) { return (n_tok * top_k > 0 ? n_tok * top_k : 1) * 4; }
 
 int exl3b200_moe_gather(const uint16_t* rows, int64_t row_pitch, const int32_t* sorted_tok, int64_t n_rows,
@@ -474,11 +557,17 @@ int exl3b200_moe_gather(const uint16_t* rows, int64_t row_pitch, const int32_t* 
     if (!rows || !sorted_tok || !w || !y || !work || n_tok < 0 || top_k < 1 || width < 1) return -12;
     if (n_tok == 0) return 0;
     cudaStream_t st = as_stream(stream);
+    const bool v8 = aligned16(rows) && row_pitch % 8 == 0 && width % 8 == 0 && aligned16(y);
+    if (v8 && n_rows <= kGatherSmallRows && top_k <= kGatherSmallSlots) {
+        // few rows: each token finds its own rows, one launch
+        k_gather_small<<<(unsigned)n_tok, 256, 0, st>>>(rows, row_pitch, sorted_tok, n_rows, w, (int)top_k, width, y);
+        return cudaGetLastError() == cudaSuccess ? 0 : -6;
+    }
     int32_t* pos = static_cast<int32_t*>(work);
     if (cudaMemsetAsync(pos, 0xFF, (size_t)(n_tok * top_k) * 4, st) != cudaSuccess) return -6;
     if (n_rows > 0)
         exl3b::k_invert<<<(unsigned)((n_rows + 255) / 256), 256, 0, st>>>(sorted_tok, n_rows, n_tok * top_k, pos);
-    if (aligned16(rows) && row_pitch % 8 == 0 && width % 8 == 0 && aligned16(y))
+    if (v8)
         k_gather_v8<<<(unsigned)n_tok, 256, 0, st>>>(rows, row_pitch, pos, w, (int)top_k, width, y);
     else
         k_gather<<<(unsigned)n_tok, 256, 0, st>>>(rows, row_pitch, pos, w, (int)top_k, width, y);

@@ -77,7 +77,7 @@ __global__ void k_tp_gather_rs(const uint16_t* __restrict__ rows, int64_t pitch,
     float* dst = reinterpret_cast<float*>(wbase(peers, o) + win.part) + ((int64_t)self * s_cap + j) * width;
     for (int64_t n = 8 * (int64_t)threadIdx.x; n < width; n += 8 * (int64_t)blockDim.x) {
         float acc[8];
-        exl3b::gather_row8(rows, pitch, pos, w, top_k, t, n, acc);
+        exl3b::gather_row8(rows, pitch, pos + t * top_k, w + t * top_k, top_k, n, acc);
         float4* d = reinterpret_cast<float4*>(dst + n);
         d[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
         d[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);

@@ -97,13 +97,14 @@ class DeviceOps:
 
     def kernels(self, T, k, E, R):
         """How many of the library's kernels one step launches: router, ep_dest, rank scatter, the two pack
-        kernels, ep_unpack, local scatter, ep_map, gate_up (+ prep), down, rows_scatter, the gather's two."""
+        kernels, ep_unpack, local scatter, ep_map, gate_up (+ prep), down, rows_scatter, the gather (one launch up to
+        4096 rows, else two)."""
         P = T * k
         tc = R > 0 and self.local._tc("gate_up", R)
-        n = 1 + 1 + (1 if P <= 8192 else 3) + 2
+        n = 1 + 1 + (1 if P <= 2048 else 3) + 2
         if R > 0:
-            n += 1 + (1 if R <= 8192 else 3) + 1 + 2 + (1 if tc else 0) + 1
-        return n + 2
+            n += 1 + (1 if R <= 2048 else 3) + 1 + 2 + (1 if tc else 0) + 1
+        return n + (1 if P <= 4096 and k <= 32 else 2)
 
 
 class IpcWindow:
@@ -378,8 +379,9 @@ class EpLayer:
             # map, row table, gate_up (+ prep), down, signal (or combine), wait, the gather's two
             Q = self.Rcap
             tc = self.ops.local._tc("gate_up", Q)
-            return 1 + 1 + 1 + (1 if T * self.k <= 8192 else 3) + 1 + 2 + 1 + (1 if Q <= 8192 else 3) + 1 + \
-                (1 if self.fuse_combine else 0) + 2 + (1 if tc else 0) + 1 + 1 + 2
+            P = T * self.k
+            return 1 + 1 + 1 + (1 if P <= 2048 else 3) + 1 + 2 + 1 + (1 if Q <= 2048 else 3) + 1 + \
+                (1 if self.fuse_combine else 0) + 2 + (1 if tc else 0) + 1 + 1 + (1 if P <= 4096 and self.k <= 32 else 2)
         return self.ops.kernels(T, self.k, self.E, self._R())
 
     def exchange_bytes(self):

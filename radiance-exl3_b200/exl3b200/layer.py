@@ -252,10 +252,22 @@ class MoeLayer:
         return "moe_exl3_down row: k_gemm_tc" if tc else "moe_exl3_down row: k_gemm_skinny"
 
     def launches_per_step(self, T):
-        """Kernels of this library one forward launches: router, scatter (1 small / 3 large), gate_up (+ prep on the
-        tensor-core band), down, the gather's inverse map and the gather."""
+        """Kernels of this library one forward launches: router and scatter (one fused launch at up to 32 tokens; else
+        the router and 1 small / 3 chunked sort launches), gate_up (+ prep on the tensor-core band), down, the gather
+        (one launch up to 4096 rows; else the inverse map and the gather)."""
+        return self.route_launches(T) + self.expert_launches(T) + self.gather_launches(T)
+
+    def route_launches(self, T):
         rows = T * self.k
-        return 1 + (1 if rows <= 8192 else 3) + 2 + 2 + (1 if self._tc("gate_up", rows) else 0)
+        if T <= 32 and rows <= 2048 and self.E <= 512 and self.n_local <= 1024:
+            return 1
+        return 1 + (1 if rows <= 2048 else 3)
+
+    def expert_launches(self, T):
+        return 2 + (1 if self._tc("gate_up", T * self.k) else 0)
+
+    def gather_launches(self, T):
+        return 1 if T * self.k <= 4096 and self.k <= 32 else 2
 
     def forward(self, T, stream, events=None, x=None, logits=None, out=None):
         """The whole layer over the first T tokens of self.x / self.logits into self.out (f32 [T, H]); `x`,
@@ -264,9 +276,8 @@ class MoeLayer:
         xp = x.data_ptr() if x is not None else None
         lp = (logits if logits is not None else self.logits).data_ptr()
         op_ = (out if out is not None else self.out).data_ptr()
-        nat.router_topk(lp, T, self.E, self.k, self.ids.data_ptr(), self.w.data_ptr(), stream)
-        nat.moe_scatter(self.ids.data_ptr(), rows, self.n_local, self.base, self.sorted_tok.data_ptr(),
-                        self.offset.data_ptr(), self.scatter_work.data_ptr(), stream)
+        nat.router_scatter(lp, T, self.E, self.k, self.ids.data_ptr(), self.w.data_ptr(), self.n_local, self.base,
+                           self.sorted_tok.data_ptr(), self.offset.data_ptr(), self.scatter_work.data_ptr(), stream)
         self.experts(T, rows, stream, x_ptr=xp, events=events)
         nat.moe_gather(self.y_rows.data_ptr(), self.H, self.sorted_tok.data_ptr(), rows, self.w.data_ptr(), T, self.k,
                        self.H, op_, self.gather_work.data_ptr(), stream)

@@ -19,6 +19,7 @@ class Native:
         L.exl3b200_moe_scatter_work_bytes.restype = _I64
         L.exl3b200_moe_scatter_work_bytes.argtypes = [_I64, _I64]
         L.exl3b200_moe_scatter.argtypes = [_VP, _I64, _I64, _I64, _VP, _VP, _VP, _VP]
+        L.exl3b200_router_scatter.argtypes = [_VP, _I64, _I64, _I64, _VP, _VP, _I64, _I64, _VP, _VP, _VP, _VP]
         L.exl3b200_moe_gather_work_bytes.restype = _I64
         L.exl3b200_moe_gather_work_bytes.argtypes = [_I64, _I64]
         L.exl3b200_moe_gather.argtypes = [_VP, _I64, _VP, _I64, _VP, _I64, _I64, _I64, _VP, _VP, _VP]
@@ -79,6 +80,12 @@ class Native:
     def moe_scatter(self, ids, n_pairs, n_expert, expert_base, sorted_tok, expert_offset, work, stream=0):
         self._check(self.lib.exl3b200_moe_scatter(ids, n_pairs, n_expert, expert_base, sorted_tok, expert_offset,
                                                   work, stream), "exl3b200_moe_scatter")
+
+    def router_scatter(self, logits, n_tok, n_route, top_k, ids, w, n_expert, expert_base, sorted_tok,
+                       expert_offset, work, stream=0):
+        self._check(self.lib.exl3b200_router_scatter(logits, n_tok, n_route, top_k, ids, w, n_expert, expert_base,
+                                                     sorted_tok, expert_offset, work, stream),
+                    "exl3b200_router_scatter")
 
     def gather_work_bytes(self, n_tok, top_k):
         return int(self.lib.exl3b200_moe_gather_work_bytes(n_tok, top_k))

@@ -182,9 +182,8 @@ class TpLayer:
         mark(0)
         if self.win is not None:
             nat.p2p_begin(self.epoch_dev.data_ptr(), st)
-        nat.router_topk(logits.data_ptr(), T, self.E, k, L.ids.data_ptr(), L.w.data_ptr(), st)
-        nat.moe_scatter(L.ids.data_ptr(), rows, self.E, 0, L.sorted_tok.data_ptr(), L.offset.data_ptr(),
-                        L.scatter_work.data_ptr(), st)
+        nat.router_scatter(logits.data_ptr(), T, self.E, k, L.ids.data_ptr(), L.w.data_ptr(), self.E, 0,
+                           L.sorted_tok.data_ptr(), L.offset.data_ptr(), L.scatter_work.data_ptr(), st)
         mark(1)
         L.experts(T, rows, st, x_ptr=x.data_ptr(), events=events)
         mark(2)
@@ -240,8 +239,10 @@ class TpLayer:
         return self.layer.band_name(op, T) + f" (width slice [{self.lo}, {self.hi}))"
 
     def launches_per_step(self, T):
-        n = self.layer.launches_per_step(T)        # router, scatter, gate_up (+ prep), down, the gather's two
-        return n + 3 if self.win is not None else n   # + begin, reduce, pull (gather_rs replaces the gather)
+        L = self.layer
+        n = L.route_launches(T) + L.expert_launches(T)
+        # peer memory: begin, the inverse map, gather_rs, reduce, pull; NCCL: the gather (its all-reduce is NCCL's)
+        return n + (5 if self.win is not None else L.gather_launches(T))
 
     def exchange_bytes(self, T):
         """Bytes this rank sends over NVLink a step (p2p): its partials of the other ranks' slices, then the other

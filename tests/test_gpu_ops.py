@@ -299,9 +299,12 @@ def test_scatter_is_the_stable_sort(dev, native, n_pairs, E, base, skew):
         assert np.array_equal(st.cpu().numpy(), st_want)
 
 
-def test_gather(dev, native, orc):
-    rng = np.random.default_rng(9)
-    T, k, E, width = 37, 4, 16, 256
+@pytest.mark.parametrize("T,k,E,width", [(37, 4, 16, 256), (1, 10, 512, 2048), (500, 10, 64, 512),
+                                         (1100, 4, 16, 256), (3, 33, 64, 256)])
+def test_gather(dev, native, orc, T, k, E, width):
+    """The gather against the restatement, to the bit: one launch (each token finds its rows) up to 4096 rows and 32
+    slots, the inverse map and the gather beyond."""
+    rng = np.random.default_rng(9 + T)
     ids = np.stack([rng.permutation(E)[:k] for _ in range(T)]).astype(np.int32)
     ids[rng.random(ids.shape) < 0.1] = -1
     st, off = X.stable_scatter(ids, E)
@@ -317,6 +320,31 @@ def test_gather(dev, native, orc):
                       work.data_ptr())
     torch.cuda.synchronize()
     assert np.array_equal(y.cpu().numpy(), want)
+
+
+@pytest.mark.parametrize("T,E,k,n_local,base", [(1, 512, 10, 512, 0), (8, 512, 10, 512, 0), (32, 256, 8, 64, 64),
+                                                 (33, 512, 10, 512, 0), (5, 1024, 32, 1024, 0), (4, 2048, 6, 512, 0)])
+def test_router_scatter_is_the_two_calls(dev, native, T, E, k, n_local, base):
+    """The fused router + sort (one launch for up to 32 tokens) equals router_topk then moe_scatter, to the bit."""
+    rng = np.random.default_rng(T * 7 + E)
+    lg = torch.from_numpy(rng.standard_normal((T, E)).astype(np.float32)).to(dev)
+    out = []
+    for fused in (True, False):
+        ids = torch.full((T, k), -7, dtype=torch.int32, device=dev)
+        w = torch.zeros((T, k), dtype=torch.float32, device=dev)
+        st = torch.full((T * k,), -7, dtype=torch.int32, device=dev)
+        off = torch.full((n_local + 1,), -7, dtype=torch.int32, device=dev)
+        work = torch.empty(max(16, native.scatter_work_bytes(T * k, n_local)), dtype=torch.uint8, device=dev)
+        if fused:
+            native.router_scatter(lg.data_ptr(), T, E, k, ids.data_ptr(), w.data_ptr(), n_local, base, st.data_ptr(),
+                                  off.data_ptr(), work.data_ptr())
+        else:
+            native.router_topk(lg.data_ptr(), T, E, k, ids.data_ptr(), w.data_ptr())
+            native.moe_scatter(ids.data_ptr(), T * k, n_local, base, st.data_ptr(), off.data_ptr(), work.data_ptr())
+        torch.cuda.synchronize()
+        out.append([t.cpu() for t in (ids, w, st, off)])
+    for a, b in zip(*out):
+        assert torch.equal(a, b)
 
 
 # ---------------------------------------------------------------------------------------------- the EP forms of the ops
