@@ -373,3 +373,141 @@ class Linears:
 
     def flops_per_call(self):
         return 2 * self.B * self.rows * self.cols
+
+
+class ClassMoeLayer(MoeLayer):
+    """The layer with its experts in classes by expert number mod n_class (2: the `_odd` tables, 4: the `_mod4`
+    ops), class c of intermediate width widths[c] -- the width split's uneven cut, where a rank holds different
+    slices of even and odd experts (architectures/qwen4exp_exl3/rad_block_moe_exl3.h:438-470). Expert e is entry
+    e // n_class of class e % n_class. h is the widest class's width; a narrower class's rows are zero past its own
+    (the ops' rule). Weights are filled by `tp.load_classes` (the width split's cut of a full-width layer)."""
+
+    def __init__(self, plugin, *, widths, **kw):
+        import torch
+        if len(widths) not in (2, 4):
+            raise ValueError("classes: 2 (by parity) or 4 (by number mod 4)")
+        super().__init__(plugin, width=max(widths), **kw)
+        self.widths = list(widths)
+        self.n_class = len(widths)
+        E, H, dev = self.n_local, self.H, self.dev
+        self.cls = []
+        for c, w in enumerate(self.widths):
+            ec = len(range(c, E, self.n_class))
+            t = {"n": ec, "w": w,
+                 "gu_rec": torch.empty((ec, 2 * w * H * self.bits_gu // 16), dtype=torch.int16, device=dev),
+                 "dn_rec": torch.empty((ec, H * w * self.bits_dn // 16), dtype=torch.int16, device=dev),
+                 "suh": torch.empty((ec, 1, H), dtype=torch.float16, device=dev),
+                 "suh1": torch.empty((ec, 1, H), dtype=torch.float16, device=dev),
+                 "svh_gu": torch.empty((ec, 2 * w, 1), dtype=torch.float16, device=dev),
+                 "dn_suh": torch.empty((ec, 1, w), dtype=torch.float16, device=dev),
+                 "svh_dn": torch.empty((ec, H, 1), dtype=torch.float16, device=dev)}
+            t["gu_tab"] = torch.tensor([t["gu_rec"][j].data_ptr() for j in range(ec)], dtype=torch.int64, device=dev)
+            t["dn_tab"] = torch.tensor([t["dn_rec"][j].data_ptr() for j in range(ec)], dtype=torch.int64, device=dev)
+            self.cls.append(t)
+        self.op_gu = "moe_exl3_gate_up_mod4" if self.n_class == 4 else "moe_exl3_gate_up"
+        self.op_dn = "moe_exl3_down_mod4" if self.n_class == 4 else "moe_exl3_down"
+        self._args = {}
+
+    def _class_params(self, p, down):
+        keys = [("N_1", "K_1"), ("N_2", "K_2"), ("N_3", "K_3")] if self.n_class == 4 else [("N_odd", "K_odd")]
+        w0 = self.widths[0]
+        p["N"], p["K"] = (self.H, w0) if down else (2 * w0, self.H)
+        for c, (kn, kk) in enumerate(keys, start=1):
+            w = self.widths[c]
+            p[kn], p[kk] = (self.H, w) if down else (2 * w, self.H)
+        p["n_expert"] = self.n_local
+        return p
+
+    def _build(self, T, rows, x_ptr=None, top_k=None, M=None):
+        key = (T, rows, x_ptr, top_k, M)
+        if key in self._args:
+            return self._args[key]
+        if len(self._args) >= 32:
+            self._args.clear()
+        from .cases import split_name
+        k = top_k or self.k
+        H, W = self.H, self.W
+        keep = []
+        schemas = {s["op"]: s for s in self.plugin.schemas()}
+        xp = x_ptr or self.x.data_ptr()
+
+        def table(plane, c, down):
+            t = self.cls[c]
+            n, w = t["n"], t["w"]
+            if plane == "codes":
+                return (rad.tensor(t["dn_tab"].data_ptr(), self.rec_dtype, [n, H, w], [0, w, 1]) if down else
+                        rad.tensor(t["gu_tab"].data_ptr(), self.rec_dtype, [n, 2 * w, H], [0, H, 1]))
+            if down:
+                ten = {"suh": t["dn_suh"], "svh": t["svh_dn"]}[plane]
+            else:
+                ten = {"suh": t["suh"], "suh1": t["suh1"], "svh": t["svh_gu"], "dn_suh": t["dn_suh"]}[plane]
+            return rad.tensor(ten.data_ptr(), rad.DT["f16"], list(ten.shape))
+
+        def args(op, down):
+            p = self._params_dn(M or T) if down else self._params_gu(M or T)
+            p["top_k"] = k
+            p = self._class_params(p, down)
+            P, nP, kp = rad.make_params(p)
+            ts = []
+            for name, role, optional in schemas[op]["operands"]:
+                plane, c = split_name(name)
+                if role == rad.OPD_WTAB:
+                    ts.append(table(plane, c, down))
+                elif name == "sorted_tok":
+                    ts.append(rad.tensor(self.sorted_tok.data_ptr(), rad.DT["i32"], [rows]))
+                elif name == "expert_offset":
+                    ts.append(rad.tensor(self.offset.data_ptr(), rad.DT["i32"], [self.n_local + 1]))
+                elif name == "a":
+                    ts.append(rad.tensor(xp, rad.DT["f16"], [T, H]))
+                elif name == "h":
+                    ts.append(rad.tensor(self.h.data_ptr(), rad.DT["f16"], [rows, W]))
+                elif name == "y":
+                    ts.append(rad.tensor(self.y_rows.data_ptr(), rad.DT["bf16"], [rows, H]))
+                else:
+                    ts.append(rad.RadTensor())
+            arr = (rad.RadTensor * len(ts))(*ts)
+            a = rad.RadArgs()
+            a.t, a.n_t, a.p, a.n_p, a.world_size = arr, len(ts), P, nP, 1
+            keep.extend([P, kp, arr])
+            row = self.plugin.row(op)
+            need = int(row.scratch(C.byref(a))) if row.scratch else 0
+            if need > 0:
+                buf = self.torch.empty(need, dtype=self.torch.uint8, device=self.dev)
+                keep.append(buf)
+                a.scratch, a.scratch_bytes = buf.data_ptr(), need
+            return a
+
+        res = (args(self.op_gu, False), args(self.op_dn, True), keep)
+        self._args[key] = res
+        return res
+
+    def experts(self, T, rows, stream, x_ptr=None, top_k=None, M=None, events=None, down_row_dst=None, live=False):
+        if down_row_dst is not None or live:
+            raise NotImplementedError("the class layer serves the plugin rows' plain launches")
+        if rows == 0:
+            for e in events or ():
+                e.record()
+            return
+        a_gu, a_dn, _ = self._build(T, rows, x_ptr, top_k, M)
+        if events:
+            events[0].record()
+        rc = self.plugin.row(self.op_gu).launch(C.byref(a_gu), stream)
+        if rc != 0:
+            raise RuntimeError(f"{self.op_gu} launch: {rc}")
+        if events:
+            events[1].record()
+        rc = self.plugin.row(self.op_dn).launch(C.byref(a_dn), stream)
+        if rc != 0:
+            raise RuntimeError(f"{self.op_dn} launch: {rc}")
+        if events:
+            events[2].record()
+
+    def expert_bytes(self):
+        """Algorithmic bytes of one expert, averaged over the classes (this rank's slices)."""
+        H, n = self.H, self.n_class
+        gu = sum(2 * w * H * self.bits_gu // 8 + 2 * H * 2 + 2 * w * 2 + w * 2 for w in self.widths) / n
+        dn = sum(H * w * self.bits_dn // 8 + H * 2 for w in self.widths) / n
+        return gu, dn
+
+    def expert_flops(self, rows):
+        return 2 * rows * sum(3 * w * self.H for w in self.widths) / self.n_class

@@ -107,6 +107,25 @@ def load_slice(dst, src, lo, hi):
     dst.svh_dn.copy_(src.svh_dn)
 
 
+def load_classes(dst, src, cuts):
+    """Fill `dst` (a ClassMoeLayer over src's experts) with the uneven cut: class c (experts c, c + n, ... of src,
+    n = len(cuts)) holds columns cuts[c] of those experts."""
+    import torch
+    n, W, H = len(cuts), src.W, src.H
+    if dst.n_class != n or dst.widths != [hi - lo for lo, hi in cuts] or dst.n_local != src.n_local:
+        raise ValueError("the class layer's shapes do not match the cut")
+    for c, (lo, hi) in enumerate(cuts):
+        t = dst.cls[c]
+        idx = torch.arange(c, src.n_local, n, device=src.dev)
+        t["gu_rec"].copy_(slice_gu_record(src.gu_rec[idx], H, W, src.bits_gu, lo, hi))
+        t["dn_rec"].copy_(slice_dn_record(src.dn_rec[idx], H, W, src.bits_dn, lo, hi))
+        t["suh"].copy_(src.suh[idx])
+        t["suh1"].copy_(src.suh1[idx])
+        t["svh_gu"].copy_(torch.cat([src.svh_gu[idx, lo:hi], src.svh_gu[idx, W + lo:W + hi]], 1))
+        t["dn_suh"].copy_(src.dn_suh[idx][:, :, lo:hi])
+        t["svh_dn"].copy_(src.svh_dn[idx])
+
+
 # ------------------------------------------------------------------------------------------ the layer
 class TpWindow:
     """Layout of the width split's window (byte offsets): part [world][s_cap][H] f32 | red [s_cap][H] f32 |
@@ -136,9 +155,7 @@ class TpLayer:
         from . import load_plugin
         from .layer import MoeLayer
         slices = width_slices(width, world, rank)
-        if len(slices) != 1:
-            raise NotImplementedError(f"width {width} over {world} ranks cuts the experts in {len(slices)} classes; "
-                                      "this layer serves the even cut (one class)")
+        self.cuts = slices
         self.lo, self.hi = slices[0]
         if transport not in ("nccl", "p2p"):
             raise ValueError(f"transport {transport!r}")
@@ -151,8 +168,15 @@ class TpLayer:
         kw = dict(n_expert=n_expert, hidden=hidden, top_k=top_k, bits_gu=bits_gu, bits_dn=bits_dn,
                   codebook=codebook, device=dev)
         src = full if full is not None else MoeLayer(plugin, width=width, max_tokens=1, seed=seed, **kw)
-        self.layer = MoeLayer(plugin, width=self.hi - self.lo, max_tokens=max_tokens, seed=seed + 7919, **kw)
-        load_slice(self.layer, src, self.lo, self.hi)
+        if len(slices) == 1:
+            self.layer = MoeLayer(plugin, width=self.hi - self.lo, max_tokens=max_tokens, seed=seed + 7919, **kw)
+            load_slice(self.layer, src, self.lo, self.hi)
+        else:
+            # the uneven cut: this rank's experts in classes (parity, or number mod 4) of different widths
+            from .layer import ClassMoeLayer
+            self.layer = ClassMoeLayer(plugin, widths=[hi - lo for lo, hi in slices], max_tokens=max_tokens,
+                                       seed=seed + 7919, **kw)
+            load_classes(self.layer, src, slices)
         del src
         L = self.layer
         self.nat = L.native
@@ -236,7 +260,7 @@ class TpLayer:
         return self.layer.time_prep_step(T, n=n)
 
     def band_name(self, op, T):
-        return self.layer.band_name(op, T) + f" (width slice [{self.lo}, {self.hi}))"
+        return self.layer.band_name(op, T) + f" (width slices {self.cuts})"
 
     def launches_per_step(self, T):
         L = self.layer

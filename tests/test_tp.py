@@ -3,9 +3,10 @@
 On CPU: the slice rule against the reference's (architectures/qwen4exp_exl3/qwen4exp_exl3.cpp:296-301, 576-634),
 the record cut against the cut of the canonical plane (through the oracle's relayout), and -- on gloo ranks -- the
 whole split through the oracle: each rank's sliced experts, its partial gather, the all-reduce, against the
-full-width layer within the expert-output tolerance. On the GPU: the slices' layers on one GPU summed against the
-full layer, the peer-memory sum at world size 1 (bit for bit the one-GPU gather), and two ranks over NVLink and
-over NCCL against the one-GPU layer."""
+full-width layer within the expert-output tolerance, and the uneven cuts' classes (parity, mod 4) through the
+oracle's class ops. On the GPU: the slices' layers on one GPU summed against the full layer (even cuts, and uneven
+cuts through the class layer and the `_odd` / `_mod4` rows), the peer-memory sum at world size 1 (bit for bit the
+one-GPU gather), and two ranks over NVLink and over NCCL against the one-GPU layer."""
 import os
 import socket
 
@@ -157,6 +158,32 @@ def test_partials_sum_to_the_layer_on_cpu_ranks(world):
     assert err <= 1e-2 * scale and cos >= 0.9999, (err, scale, cos)
 
 
+@pytest.mark.parametrize("width,world", [(640, 2), (512, 3), (640, 3), (640, 4)])
+def test_uneven_cut_classes_sum_to_the_layer(width, world):
+    """A width the ranks do not divide: each rank's experts fall in classes (by parity, or by number mod 4 at four
+    ranks) of different slice widths -- the class ops (`_odd` / `_mod4` tables) over the sliced planes, run by the
+    oracle for every rank and summed, equal the full-width layer within the expert-output tolerance."""
+    orc = Oracle()
+    M, k, E, H, bits = 5, 3, 8, 256, 4
+    full = _case(23, M, k, E, H, width, bits)
+    w = np.random.default_rng(7).random((M, k)).astype(np.float32)
+    want = _layer_out(orc, full, w)
+    acc = np.zeros_like(want, dtype=np.float64)
+    for r in range(world):
+        cuts = tp.width_slices(width, world, r)
+        n_class = len(cuts)
+        assert n_class in (2, 4)
+        planes = [tp.slice_planes(p, width, bits, bits, *cuts[e % n_class]) for e, p in enumerate(full.planes)]
+        op = "moe_exl3_gate_up_down_mod4" if n_class == 4 else "moe_exl3_gate_up_down"
+        mine = X.Case(op, 23, M=M, top_k=k, n_expert=E, geom=[(2 * (hi - lo), H) for lo, hi in cuts], n_class=n_class,
+                      bits=bits, planes=planes, sorted_tok=full.sorted_tok, expert_offset=full.expert_offset, x=full.x)
+        acc += _layer_out(orc, mine, w)
+    err = float(np.abs(acc - want).max())
+    scale = float(np.abs(want).max())
+    cos = float((acc * want).sum() / np.sqrt((acc ** 2).sum() * (want.astype(np.float64) ** 2).sum()))
+    assert err <= 1e-2 * scale and cos >= 0.9999, (err, scale, cos)
+
+
 # ------------------------------------------------------------------------------------------ on the GPU
 def _compare(a, b):
     a, b = a.double(), b.double()
@@ -189,6 +216,40 @@ def test_width_slices_on_one_gpu_sum_to_the_layer(world, T):
         (lo, hi), = tp.width_slices(W, world, r)
         part = MoeLayer(plugin, n_expert=E, hidden=H, width=hi - lo, top_k=k, max_tokens=T, seed=99, device=dev)
         tp.load_slice(part, full, lo, hi)
+        part.x[:T], part.logits[:T] = full.x[:T], full.logits[:T]
+        part.forward(T, s)
+        acc += part.out[:T].double()
+    torch.cuda.synchronize()
+    err, scale, cos = _compare(full.out[:T], acc)
+    assert err <= 1e-2 * scale and cos >= 0.9999, (err, scale, cos)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("width,world", [(512, 3), (640, 2), (640, 4)])
+@pytest.mark.parametrize("T", [4, 96])
+def test_uneven_cut_class_layers_on_one_gpu_sum_to_the_layer(width, world, T):
+    """The uneven cut on the device: each rank's experts in classes of different widths (ClassMoeLayer through the
+    `_odd` / `_mod4` plugin rows, weights cut by load_classes), run on one GPU; the partials summed equal the
+    full-width layer within the expert-output tolerance."""
+    from exl3b200 import load_plugin
+    from exl3b200.layer import ClassMoeLayer, MoeLayer
+    plugin = load_plugin()
+    dev = torch.device("cuda", 0)
+    E, H, k = 32, 2048, 8
+    full = MoeLayer(plugin, n_expert=E, hidden=H, width=width, top_k=k, max_tokens=T, seed=5, device=dev)
+    g = torch.Generator(device=dev)
+    g.manual_seed(T + width)
+    full.x[:T] = torch.randn((T, H), generator=g, device=dev).to(torch.float16)
+    full.logits[:T] = torch.randn((T, E), generator=g, device=dev)
+    s = torch.cuda.current_stream().cuda_stream
+    full.forward(T, s)
+    acc = torch.zeros((T, H), dtype=torch.float64, device=dev)
+    for r in range(world):
+        cuts = tp.width_slices(width, world, r)
+        assert len(cuts) in (2, 4)
+        part = ClassMoeLayer(plugin, widths=[hi - lo for lo, hi in cuts], n_expert=E, hidden=H, top_k=k,
+                             max_tokens=T, seed=99, device=dev)
+        tp.load_classes(part, full, cuts)
         part.x[:T], part.logits[:T] = full.x[:T], full.logits[:T]
         part.forward(T, s)
         acc += part.out[:T].double()
