@@ -176,3 +176,48 @@ def test_refusals_come_before_any_device_work(plugin):
     t[6] = rad.tensor(codes.ctypes.data, 1970, [1, 256, 128], [0, 128, 1])     # odd tables partly present
     assert _launch(plugin, op, p, t) == rad.RAD["INVAL"]
     assert (y == 0).all()
+
+
+@pytest.mark.parametrize("op,E,H,W,k", [("moe_exl3_gate_up", 512, 2048, 512, 10), ("moe_exl3_down", 512, 2048, 512, 10),
+                                        ("moe_exl3_gate_up", 64, 2048, 512, 8), ("moe_exl3_down", 32, 2048, 128, 8),
+                                        ("moe_exl3_gate_up", 1, 1536, 2048, 1), ("moe_exl3_down", 1, 1536, 4096, 1)])
+def test_layer_band_rule_mirrors_the_library(plugin, op, E, H, W, k):
+    """exl3b200/layer.py names the band each op runs on (bench lines, tests) by restating the library's rule; the
+    library's own scratch hook says the same thing (it asks for rotated-input scratch exactly on the tensor-core
+    band when the op rotates its own input), for every pass size from one token to prefill."""
+    from types import SimpleNamespace
+
+    from exl3b200.layer import MoeLayer
+    gate_up = op == "moe_exl3_gate_up"
+    row = plugin.row(op)
+    mirror = SimpleNamespace(n_local=E, W=W, H=H)
+    fake = 1 << 20                       # the hook reads shapes only; no pointer is dereferenced
+    for T in (1, 2, 3, 4, 6, 8, 16, 33, 64, 512, 2048):
+        rows = T * k
+        p = {"M": T, "N": 2 * W if gate_up else H, "K": H if gate_up else W, "n_expert": E, "top_k": k,
+             "dtype": "exl3k3" if gate_up else "exl3k4", "codebook": "mul1", "h_rot": 0}
+        if gate_up:
+            p["a_rot"] = 0
+        P, nP, keep = rad.make_params(p)
+        if gate_up:
+            ts = [rad.tensor(fake, rad.DT["f16"], [T, H]),
+                  rad.tensor(fake, 1970, [E, 2 * W, H], [0, H, 1]),
+                  rad.tensor(fake, rad.DT["f16"], [E, 1, H]), rad.tensor(fake, rad.DT["f16"], [E, 1, H]),
+                  rad.tensor(fake, rad.DT["f16"], [E, 2 * W, 1]), rad.RadTensor(),
+                  rad.tensor(fake, rad.DT["i32"], [rows]), rad.tensor(fake, rad.DT["i32"], [E + 1]),
+                  rad.RadTensor(), rad.RadTensor(), rad.RadTensor(), rad.RadTensor(), rad.RadTensor(),
+                  rad.tensor(fake, rad.DT["f16"], [rows, W])]
+        else:
+            ts = [rad.tensor(fake, rad.DT["f16"], [rows, W]),
+                  rad.tensor(fake, 1970, [E, H, W], [0, W, 1]),
+                  rad.tensor(fake, rad.DT["f16"], [E, 1, W]), rad.tensor(fake, rad.DT["f16"], [E, H, 1]),
+                  rad.tensor(fake, rad.DT["i32"], [rows]), rad.tensor(fake, rad.DT["i32"], [E + 1]),
+                  rad.RadTensor(), rad.RadTensor(), rad.RadTensor(),
+                  rad.tensor(fake, rad.DT["bf16"], [rows, H])]
+        arr = (rad.RadTensor * len(ts))(*ts)
+        a = rad.RadArgs()
+        a.t, a.n_t, a.p, a.n_p, a.world_size = arr, len(ts), P, nP, 1
+        need = int(row.scratch(C.byref(a)))
+        want = (rows * (2 * H if gate_up else W) * 2 + 255) // 256 * 256
+        tc = MoeLayer._tc(mirror, "gate_up" if gate_up else "down", rows)
+        assert need == (want if tc else 0), (T, need, tc)
