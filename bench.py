@@ -234,16 +234,23 @@ def bench_ours(args, rank, world, local_rank):
     plugin = load_plugin()
     T = args.tokens
     tp_mode = world > 1 and args.mode == "tp"
+    # N > 1: every rank also builds the whole 512-expert layer from the same seed (its weights are the ones the ranks
+    # hold in slices), used once after the timed region to check this rank's multi-GPU output against the one-GPU
+    # layer on the same tokens
+    full = None
+    if world > 1:
+        full = MoeLayer(plugin, n_expert=E, hidden=H, width=W, top_k=TOPK, bits_gu=KGU, bits_dn=KDN, codebook=CB,
+                        max_tokens=T, seed=1)
     if tp_mode:
         # the width split: every rank holds half (a quarter, ...) of every expert's width and serves ALL T tokens
         # (replicated), so the group's throughput is T a step (strong scaling)
         from exl3b200.tp import TpLayer
         layer = TpLayer(plugin, rank=rank, world=world, n_expert=E, hidden=H, width=W, top_k=TOPK, bits_gu=KGU,
-                        bits_dn=KDN, codebook=CB, max_tokens=T, seed=1, transport=args.transport)
+                        bits_dn=KDN, codebook=CB, max_tokens=T, seed=1, transport=args.transport, full=full)
     elif world > 1:
         from exl3b200.ep import EpLayer
         layer = EpLayer(plugin, rank=rank, world=world, n_expert=E, hidden=H, width=W, top_k=TOPK, bits_gu=KGU,
-                        bits_dn=KDN, codebook=CB, max_tokens=T, seed=1 + rank, transport=args.transport)
+                        bits_dn=KDN, codebook=CB, max_tokens=T, seed=1, transport=args.transport, full=full)
     else:
         layer = MoeLayer(plugin, n_expert=E, hidden=H, width=W, top_k=TOPK, bits_gu=KGU, bits_dn=KDN, codebook=CB,
                          max_tokens=T, seed=1)
@@ -495,8 +502,29 @@ def bench_ours(args, rank, world, local_rank):
         except Exception as exc:  # the reference library is absent on this box
             cpu = {"value": None, "unit": "tokens/s", "cores": 0, "kind": "reference", "sample": f"unavailable: {exc}"}
 
+    multi_check = None
     if world > 1:
         layer.check()
+        # this rank's output of the last step against the one-GPU layer on the same tokens and weights: expert
+        # parallelism returns every pair's own down row and sums a token's slots in the same order, so the two must
+        # be equal to the bit; the width split sums per-rank partials (each rounded to bf16 rows), so it is held to
+        # the expert-output tolerance (max |diff| <= 1e-2 max |ref|, cosine >= 0.9999)
+        full.x[:T].copy_(layer.x[:T])
+        full.logits[:T].copy_(layer.logits[:T])
+        full.forward(T, sh)
+        torch.cuda.synchronize()
+        a, b = full.out[:T].double(), layer.out[:T].double()
+        same = bool(torch.equal(full.out[:T], layer.out[:T]))
+        rel = float((a - b).abs().max() / a.abs().max().clamp_min(1e-30))
+        cos = float((a * b).sum() / (a.norm() * b.norm()).clamp_min(1e-30))
+        ok = same if not tp_mode else (rel <= 1e-2 and cos >= 0.9999)
+        v = torch.tensor([1.0 if ok else 0.0, 1.0 if same else 0.0, rel, -cos], device=dev, dtype=torch.float64)
+        torch.distributed.all_reduce(v, op=torch.distributed.ReduceOp.MIN)
+        v2 = torch.tensor([rel, -cos], device=dev, dtype=torch.float64)
+        torch.distributed.all_reduce(v2, op=torch.distributed.ReduceOp.MAX)
+        multi_check = {"ranks_ok": bool(v[0].item() == 1.0), "bit_identical_all_ranks": bool(v[1].item() == 1.0),
+                       "max_rel_err": float(v2[0].item()), "min_cosine": float(-v2[1].item()),
+                       "against": "the one-GPU layer (all 512 experts, same seed) on each rank's own tokens"}
         exch = layer.exchange_bytes(T) if tp_mode else layer.exchange_bytes()
         if ep_phases is not None:
             ep_phases["exchange_bytes_rank0"] = exch
@@ -535,6 +563,9 @@ def bench_ours(args, rank, world, local_rank):
         "e2e": e2e, "cpu_baseline": cpu, "sweep": sweep, "bitrate_sweep": bitrates, "wall_s": round(wall, 3),
         "ep_phases_ms": ep_phases,
     }
+    if multi_check is not None:
+        line["ep_bit_identical" if not tp_mode else "tp_within_tolerance"] = multi_check["ranks_ok"]
+        line["multi_gpu_check"] = multi_check
     return line
 
 

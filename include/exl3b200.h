@@ -67,7 +67,8 @@ int exl3b200_decode_what(const void* record, int64_t rows, int64_t cols, int bit
  *                 exl3b200_moe_scatter_work_bytes() bytes.
  *   moe_gather:   y f32 [n_tok][width] = sum over slots ascending of w * bf16 row of that slot's sorted row
  *                 (a dropped slot adds nothing); `rows` bf16 with row pitch `row_pitch` elements. `work` is
- *                 caller-provided device memory of exl3b200_moe_gather_work_bytes() bytes. */
+ *                 caller-provided device memory of exl3b200_moe_gather_work_bytes() bytes. Sizes whose pair
+ *                 count n_tok * top_k would pass INT32_MAX are refused (RAD_E_SHAPE) before anything is enqueued. */
 int     exl3b200_router_topk(const float* logits, int64_t n_tok, int64_t n_expert, int64_t top_k, int32_t* ids,
                              float* w, void* stream);
 int64_t exl3b200_moe_scatter_work_bytes(int64_t n_pairs, int64_t n_expert);
@@ -90,7 +91,8 @@ int     exl3b200_moe_gather(const uint16_t* rows, int64_t row_pitch, const int32
  * strict device-memory budget, code that must not grow the CUDA allocator's footprint). No counterpart in the
  * reference: it is this library's own addition. Same arguments and result as exl3b200_moe_gather without `work`:
  * the inverse pair -> row map lives in a fixed 1 MiB device array inside this library, so n_tok * top_k must be at
- * most 262,144 (RAD_E_SHAPE beyond, nothing enqueued). The first call on each device looks up the array's device
+ * most 262,144 (RAD_E_SHAPE beyond, nothing enqueued; the limit is tested factor by factor, so huge arguments
+ * whose product would wrap around are refused too). The first call on each device looks up the array's device
  * address (cudaGetSymbolAddress) with that device current; make that first call before any stream capture. The
  * call allocates nothing (no cudaMalloc, no cudaFree, no allocating library routine). Every call shares the one
  * array per device: calls that overlap on the GPU (two streams, or two threads) race and must be serialised by
@@ -149,12 +151,13 @@ int     exl3b200_ep_dedup_scan(const int32_t* ids, int64_t top_k, const int32_t*
  * peers[world] = every rank's window base as this rank maps it (its own for itself).
  *   p2p_dispatch:      after ep_dedup_scan: pair metas and the deduplicated token rows straight into the owners'
  *                      windows, then each owner's dispatch flag (epoch) with the counts.
- *   p2p_wait_dispatch: waits (at most 5 s) for every source's flag; hdr[3s .. 3s+2] = rows, pairs, base of source
- *                      s; hdr[3 world] = 0, or -1 if a wait gave up (the error word is set too).
+ *   p2p_wait_dispatch: waits (bounded: exl3b200_set_peer_wait_ns) for every source's flag; hdr[3s .. 3s+2] =
+ *                      rows, pairs, base of source s; hdr[3 world] = 0, or -1 if a wait gave up (the error word
+ *                      is set too).
  *   p2p_unpack:        the received pairs (source-major): local expert, row in the window's rows, and where the
  *                      pair's down row returns (source rank, position).
  *   p2p_combine:       each sorted down row straight into its source's yback, then each source's combine flag.
- *   p2p_wait_combine:  waits (at most 5 s) for every owner's combine flag; status[0] = 0 or -1.
+ *   p2p_wait_combine:  waits (bounded) for every owner's combine flag; status[0] = 0 or -1.
  *   The combine fused into down instead of p2p_combine: p2p_row_dst (each sorted row's destination address in
  *   its source's window), exl3b200_moe_down_rows with that table (down's epilogue stores each row straight into
  *   the source over NVLink, fenced at system scope), then p2p_signal_combine (the flags).
@@ -192,6 +195,11 @@ int     exl3b200_p2p_begin(uint32_t* epoch, void* stream);
  * [expert_offset[0], expert_offset[n_expert]) are left untouched instead of zeroed, so a caller may pass a
  * capacity-sized pass whose live count is known only on the device; down may write through row_dst. */
 int     exl3b200_moe_op_live(const RadArgs* args, int down, const uint64_t* row_dst, void* stream);
+/* moe_exl3_down with f16 output rows: the same operands (y f16 instead of bf16), checks, scratch hook and arithmetic
+ * as the moe_exl3_down row, the f32 result times svh rounded once to f16. The single EXL3 linear of [M, K] f16 rows
+ * to [M, N] f16 (n_expert 1, top_k 1, every row routed to the one expert). No counterpart in the reference, whose
+ * down writes bf16 (kernels/exl3ref/ref.c:97-102). */
+int     exl3b200_moe_down_f16(const RadArgs* args, void* stream);
 /* moe_exl3_down (same RadArgs and checks as the row's launch) writing output row i at row_dst[i] (a device table
  * of row addresses, possibly in a peer's memory) instead of y + i * pitch. No counterpart in the reference. */
 int     exl3b200_moe_down_rows(const RadArgs* args, const uint64_t* row_dst, void* stream);
@@ -208,9 +216,9 @@ int     exl3b200_ep_map(const int32_t* idx, int64_t n, const int32_t* table, int
  * Tokens are cut into world slices of s = ceil(n_tok / world) rows (s <= s_cap); rank o reduces slice o.
  *   tp_gather_rs: the gather (exl3b200_moe_gather's arithmetic over this rank's y rows), each token's partial
  *                 stored into its owner's part segment; then every owner's partials flag. status[0] = 0.
- *   tp_reduce:    waits (at most 5 s) for every source's flag; sums this rank's slice over the sources in
+ *   tp_reduce:    waits (bounded) for every source's flag; sums this rank's slice over the sources in
  *                 ascending order into red; then every rank's reduced flag (held back if a wait gave up).
- *   tp_pull:      waits (at most 5 s) for every owner's reduced flag; out[t] = the owner's red row (f32, row pitch
+ *   tp_pull:      waits (bounded) for every owner's reduced flag; out[t] = the owner's red row (f32, row pitch
  *                 out_pitch floats); status[0] = -1 if a wait gave up (the error word is set too).
  * Every rank ends with the same bits; at world 1 they are exl3b200_moe_gather's. Ranks pass the same n_tok and call
  * the steps in the same order, after exl3b200_p2p_begin on their own epoch word. */
@@ -223,6 +231,14 @@ int     exl3b200_tp_reduce(const uint64_t* peers, const int64_t* offs, int64_t s
 int     exl3b200_tp_pull(const uint64_t* peers, const int64_t* offs, int64_t self, int64_t world, int64_t n_tok,
                          int64_t width, int64_t s_cap, float* out, int64_t out_pitch, const uint32_t* epoch,
                          int32_t* status, void* stream);
+
+/* How long a kernel that waits on another rank's flag (p2p_wait_dispatch, p2p_wait_combine, tp_reduce, tp_pull)
+ * waits before it gives up, sets its status and the error word, and returns: `ns` nanoseconds, or the default 5 s
+ * for ns <= 0 (more than 600 s is refused, RAD_E_INVAL). Process-wide; each launch reads it when it is enqueued
+ * (a CUDA graph keeps the value it was captured with). A short limit lets a caller -- or a test, with a flag that
+ * nothing raises -- see the failure path without hanging a GPU. No counterpart in the reference (whose one wait,
+ * the fused kernel's, has a fixed bound). */
+int exl3b200_set_peer_wait_ns(int64_t ns);
 
 /* The device error word of the current device: nonzero once a bounded wait inside a kernel gave up (the
  * launch then finished without a valid result). Reading it synchronises the device; `clear` resets it. Not

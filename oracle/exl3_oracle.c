@@ -355,7 +355,10 @@ static int expert_rows(const OrcOp* o, int64_t e, Work* wk) {
             gemv(wk->xr, wk->what, R, C, wk->acc);
             orc_had128(wk->acc, R);
             uint16_t* y = o->y + i * o->y_pitch;
-            for (int64_t n = 0; n < R; ++n) y[n] = rad_f32_to_bf16(wk->acc[n] * h2f(svh[n]));
+            if (o->out_f16)   /* the f16-output linear (config 1): the same value rounded to f16 instead */
+                for (int64_t n = 0; n < R; ++n) y[n] = f2h(wk->acc[n] * h2f(svh[n]));
+            else
+                for (int64_t n = 0; n < R; ++n) y[n] = rad_f32_to_bf16(wk->acc[n] * h2f(svh[n]));
         }
     }
     return 0;

@@ -67,6 +67,8 @@ typedef struct OrcOp {
     const uint16_t* const* svh;
     const uint16_t* const* dn_suh;
     int            n_threads;          /* experts decoded and run in parallel; 1 = the reference's order */
+    int            out_f16;            /* down only: round the output to f16 instead of bf16 (this library's
+                                          f16-output linear; the reference's down writes bf16, ref.c:97-102) */
 } OrcOp;
 
 /* 0 ok; -1 bad arguments; -7 out of memory. Writes exactly what the op defines (zero rows, prep's

@@ -334,6 +334,23 @@ __device__ __forceinline__ void st4_bf16(uint16_t* y, const float v[4]) {
         y[0] = b0; y[1] = b1; y[2] = b2; y[3] = b3;
     }
 }
+// Four f16 values, stored the same way (the f16-output linear).
+__device__ __forceinline__ void st4_f16(uint16_t* y, const float v[4]) {
+    const uint16_t b0 = f2h(v[0]), b1 = f2h(v[1]), b2 = f2h(v[2]), b3 = f2h(v[3]);
+    if ((reinterpret_cast<uintptr_t>(y) & 7) == 0) {
+        uint2 u;
+        u.x = (uint32_t)b0 | ((uint32_t)b1 << 16);
+        u.y = (uint32_t)b2 | ((uint32_t)b3 << 16);
+        *reinterpret_cast<uint2*>(y) = u;
+    } else {
+        y[0] = b0; y[1] = b1; y[2] = b2; y[3] = b3;
+    }
+}
+// down's output row: bf16 (the op's type), or f16 for the f16-output linear
+__device__ __forceinline__ void st4_out(const Exl3bOp& op, uint16_t* y, const float v[4]) {
+    if (op.out_f16) st4_f16(y, v);
+    else st4_bf16(y, v);
+}
 // Where output row i goes: y + i * pitch, or -- when the caller gave a row table (the expert-parallel combine
 // writing straight into the sources' memory) -- row_dst[i].
 __device__ __forceinline__ uint16_t* out_row(const Exl3bOp& op, int64_t i) {

@@ -32,7 +32,7 @@ typedef struct Exl3bOp {
     int32_t        op;                  /* EXL3B_OP_* */
     int32_t        bits, codebook, h_rot, a_rot, n_class;
     int32_t        x_bf16;              /* the input rows are bf16 (token rows only) */
-    int32_t        pad0;
+    int32_t        out_f16;             /* down only: the output rows are f16 instead of bf16 */
     int64_t        T, n_expert, top_k;
     int64_t        x_pitch, x_rows;     /* elements */
     int64_t        y_pitch, y_cols;     /* elements */

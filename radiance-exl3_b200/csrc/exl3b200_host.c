@@ -70,8 +70,9 @@ static Exl3bTab tab_of(const RadTensor* t, int64_t elem_bytes) {
     return x;
 }
 
-/* gate_up / down / prep_gu (two- or four-class): the refusals, then the kernels' argument record. */
-static int build_op(const RadArgs* a, int op, Exl3bGeom* g, Exl3bOp* k) {
+/* gate_up / down / prep_gu (two- or four-class): the refusals, then the kernels' argument record. `y_f16`: down
+ * writes f16 rows instead of bf16 (the f16-output linear; the op itself writes bf16). */
+static int build_op_ex(const RadArgs* a, int op, Exl3bGeom* g, Exl3bOp* k, int y_f16) {
     const Exl3bPositions* at = exl3b_positions(op);
     if (a->n_t < at->n_opd) return RAD_E_INVAL;
     if (!rad_arg_in(a, at->x) || !rad_arg_in(a, at->sorted) || !rad_arg_in(a, at->offset) || !rad_arg_in(a, at->y))
@@ -97,7 +98,8 @@ static int build_op(const RadArgs* a, int op, Exl3bGeom* g, Exl3bOp* k) {
     const RadTensor* off = rad_arg_in(a, at->offset);
     const int token_rows = g->gate_up && !g->a_rot;
     if (token_rows ? x->dtype != RAD_F16 && x->dtype != RAD_BF16 : x->dtype != RAD_F16) return RAD_E_DTYPE;
-    if (y->dtype != (g->op == EXL3B_DOWN ? (uint32_t)RAD_BF16 : (uint32_t)RAD_F16)) return RAD_E_DTYPE;
+    if (y_f16 && g->op != EXL3B_DOWN) return RAD_E_INVAL;
+    if (y->dtype != (g->op == EXL3B_DOWN && !y_f16 ? (uint32_t)RAD_BF16 : (uint32_t)RAD_F16)) return RAD_E_DTYPE;
     if (st->dtype != RAD_I32 || off->dtype != RAD_I32) return RAD_E_DTYPE;
     if (!rad_tensor_is_contiguous(st) || !rad_tensor_is_contiguous(off)) return RAD_E_STRIDE;
     if (x->rank < 2 || y->rank < 2) return RAD_E_SHAPE;
@@ -124,6 +126,7 @@ static int build_op(const RadArgs* a, int op, Exl3bGeom* g, Exl3bOp* k) {
     k->a_rot = g->a_rot;
     k->n_class = g->n_class;
     k->x_bf16 = x->dtype == RAD_BF16;
+    k->out_f16 = y_f16 != 0;
     k->T = T;
     k->n_expert = g->n_expert;
     k->top_k = g->top_k;
@@ -150,6 +153,8 @@ static int build_op(const RadArgs* a, int op, Exl3bGeom* g, Exl3bOp* k) {
     }
     return RAD_OK;
 }
+
+static int build_op(const RadArgs* a, int op, Exl3bGeom* g, Exl3bOp* k) { return build_op_ex(a, op, g, k, 0); }
 
 /* The band choice. The tensor-core path decodes each expert's weights once for up to 64 of its rows and pays its
  * input-rotation pass (the prep kernel into scratch) once per row; the decode-band path re-rotates per output block
@@ -235,6 +240,17 @@ int exl3b200_moe_down_rows(const RadArgs* a, const uint64_t* row_dst, void* stre
     const int rc = build_op(a, EXL3B_DOWN, &g, &k);
     if (rc != RAD_OK) return rc;
     k.row_dst = row_dst;
+    return run_op(&k, a->scratch, a->scratch_bytes, stream);
+}
+
+/* moe_exl3_down with f16 output rows (config 1's single linear, [M, K] f16 -> [M, N] f16): the down row's operands,
+ * checks and arithmetic, the f32 result times svh rounded once to f16 instead of bf16. */
+int exl3b200_moe_down_f16(const RadArgs* a, void* stream) {
+    Exl3bGeom g;
+    Exl3bOp k;
+    if (!a) return RAD_E_INVAL;
+    const int rc = build_op_ex(a, EXL3B_DOWN, &g, &k, 1);
+    if (rc != RAD_OK) return rc;
     return run_op(&k, a->scratch, a->scratch_bytes, stream);
 }
 

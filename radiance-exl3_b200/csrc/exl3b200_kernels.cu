@@ -520,7 +520,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_skinny(const Exl3bOp op, i
                     float o[4];
 #pragma unroll
                     for (int q = 0; q < 4; ++q) o[q] = __fmul_rn(v[0][q], h2f(svh[n0 + q]));
-                    st4_bf16(y, o);
+                    st4_out(op, y, o);
                 }
             }
             if (op.row_dst) __threadfence_system();   // rows in another GPU's memory: visible before the kernel ends

@@ -238,7 +238,9 @@ __device__ __forceinline__ void place_chunk_fast(const int32_t* ids, int64_t c0,
 constexpr int kPlaceFastExperts = 1024;
 
 // The whole sort in one block (few pairs): histogram, scan, stable placement, tail of -1.
-__device__ __forceinline__ void scatter_block(const int32_t* __restrict__ ids, int64_t n_pairs, int n_expert,
+// `ids` carries no __restrict__: the fused router below writes the ids earlier in the same kernel, so they must not be
+// read through the read-only (non-coherent) path.
+__device__ __forceinline__ void scatter_block(const int32_t* ids, int64_t n_pairs, int n_expert,
                                               int64_t base, int32_t* __restrict__ sorted_tok,
                                               int32_t* __restrict__ off, int* sm) {
     int* cnt = sm;                 // [n_expert + 1]
@@ -279,7 +281,7 @@ __global__ void k_scatter_small(const int32_t* __restrict__ ids, int64_t n_pairs
 constexpr int kFusedTokens = 32;
 template <int RPL>
 __global__ void __launch_bounds__(1024, 1) k_route_scatter_small(const float* __restrict__ logits, int64_t n_tok, int n_route, int top_k,
-                                      int32_t* __restrict__ ids, float* __restrict__ w, int n_expert, int64_t base,
+                                      int32_t* ids, float* __restrict__ w, int n_expert, int64_t base,
                                       int32_t* __restrict__ sorted_tok, int32_t* __restrict__ off) {
     extern __shared__ int sm[];
     const int warp = threadIdx.x >> 5;
@@ -555,6 +557,9 @@ int exl3b200_moe_gather(const uint16_t* rows, int64_t row_pitch, const int32_t* 
                         const float* w, int64_t n_tok, int64_t top_k, int64_t width, float* y, void* work,
                         void* stream) {
     if (!rows || !sorted_tok || !w || !y || !work || n_tok < 0 || top_k < 1 || width < 1) return -12;
+    // the pair count n_tok * top_k indexes int32 maps and the kernels take top_k as an int: sizes whose product
+    // would not fit are refused before it is formed
+    if (top_k > INT32_MAX || n_tok > INT32_MAX / top_k || width > INT32_MAX) return -1;
     if (n_tok == 0) return 0;
     cudaStream_t st = as_stream(stream);
     const bool v8 = aligned16(rows) && row_pitch % 8 == 0 && width % 8 == 0 && aligned16(y);
@@ -585,7 +590,9 @@ static __device__ __align__(256) int32_t g_noalloc_pos[kNoAllocMaxPairs];
 int exl3b200_moe_gather_noalloc(const uint16_t* rows, int64_t row_pitch, const int32_t* sorted_tok, int64_t n_rows,
                                 const float* w, int64_t n_tok, int64_t top_k, int64_t width, float* y, void* stream) {
     if (!rows || !sorted_tok || !w || !y || n_tok < 0 || top_k < 1 || width < 1 || n_rows < 0) return -12;
-    if (n_tok * top_k > kNoAllocMaxPairs) return -1;   // past the fixed array: refused before anything is enqueued
+    // past the fixed array: refused before anything is enqueued (tested factor by factor, so that no product of
+    // huge arguments can wrap around into the allowed range)
+    if (top_k > kNoAllocMaxPairs || n_tok > kNoAllocMaxPairs / top_k || width > INT32_MAX) return -1;
     if (n_tok == 0) return 0;
     // Set-up, once per device, with that device current: the array's device address. The host-side name of a
     // __device__ array is not a device address; only cudaGetSymbolAddress gives one.

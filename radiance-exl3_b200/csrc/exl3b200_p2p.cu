@@ -26,7 +26,6 @@
 
 namespace {
 
-constexpr uint64_t kP2pWaitNs = 5000000000ull;   // a rank waits at most 5 s for its peers, then reports
 
 struct Win {
     int64_t rows, meta, yback, ctl, done, sink;   // byte offsets in every window (sink: one spare row)
@@ -95,7 +94,7 @@ __global__ void k_p2p_dispatch(const uint4* __restrict__ x, int64_t x_pitch16, c
 // Lane s waits (bounded) for source s's dispatch flag of this epoch, then hands its counts to the host:
 // hdr[3s] = rows, hdr[3s + 1] = pairs, hdr[3s + 2] = base; hdr[3 world] = 0, or -1 when a wait gave up.
 __global__ void k_p2p_wait_dispatch(uint8_t* own, Win w, int world, const uint32_t* epoch_p, int32_t* hdr,
-                                    int32_t* err) {
+                                    int32_t* err, uint64_t limit_ns) {
     const int s = threadIdx.x;
     const uint32_t epoch = *epoch_p;
     bool ok = true;
@@ -103,7 +102,7 @@ __global__ void k_p2p_wait_dispatch(uint8_t* own, Win w, int world, const uint32
         const uint32_t* ctl = reinterpret_cast<const uint32_t*>(own + w.ctl) + s * 8;
         const uint64_t t0 = gtimer();
         while ((int32_t)(ld_acquire_sys(&ctl[0]) - epoch) < 0) {
-            if (gtimer() - t0 > kP2pWaitNs) { ok = false; break; }
+            if (gtimer() - t0 > limit_ns) { ok = false; break; }
             __nanosleep(256);
         }
         hdr[3 * s] = ok ? (int32_t)ld_acquire_sys(&ctl[1]) : 0;
@@ -192,7 +191,7 @@ __global__ void k_p2p_combine(const uint4* __restrict__ y_rows, int64_t y_pitch1
 
 // Lane d waits (bounded) for owner d's combine flag of this epoch; status[0] = 0, or -1 when a wait gave up.
 __global__ void k_p2p_wait_combine(const uint8_t* own, Win w, int world, const uint32_t* epoch_p, int32_t* status,
-                                   int32_t* err) {
+                                   int32_t* err, uint64_t limit_ns) {
     const int d = threadIdx.x;
     const uint32_t epoch = *epoch_p;
     bool ok = true;
@@ -200,7 +199,7 @@ __global__ void k_p2p_wait_combine(const uint8_t* own, Win w, int world, const u
         const uint32_t* ctl = reinterpret_cast<const uint32_t*>(own + w.ctl) + d * 8;
         const uint64_t t0 = gtimer();
         while ((int32_t)(ld_acquire_sys(&ctl[4]) - epoch) < 0) {
-            if (gtimer() - t0 > kP2pWaitNs) { ok = false; break; }
+            if (gtimer() - t0 > limit_ns) { ok = false; break; }
             __nanosleep(256);
         }
     }
@@ -265,6 +264,20 @@ extern "C" {
 
 int exl3b_cuda_device_info(int* sm_count, int32_t** err_word);   // exl3b200_moe.cu
 
+// How long a kernel that waits on another rank's flag (the dispatch and combine waits here, the width split's
+// reduce and pull) waits before it gives up and reports: 5 s unless the caller set otherwise. Read at each launch
+// and passed to the kernel as an argument.
+static const int64_t kPeerWaitDefaultNs = 5000000000ll;
+static int64_t g_peer_wait_ns = kPeerWaitDefaultNs;
+
+uint64_t exl3b_peer_wait_ns(void) { return (uint64_t)__atomic_load_n(&g_peer_wait_ns, __ATOMIC_RELAXED); }
+
+int exl3b200_set_peer_wait_ns(int64_t ns) {
+    if (ns > 600ll * 1000000000ll) return -12;
+    __atomic_store_n(&g_peer_wait_ns, ns <= 0 ? kPeerWaitDefaultNs : ns, __ATOMIC_RELAXED);
+    return 0;
+}
+
 int exl3b200_ep_window_alloc(int64_t bytes, void** ptr) {
     if (!ptr || bytes <= 0) return -12;
     void* p = nullptr;
@@ -319,7 +332,7 @@ int exl3b200_p2p_wait_dispatch(void* own, const int64_t* offs, int64_t world, co
     if (exl3b_cuda_device_info(&sm, &err) != 0) return -6;
     const Win w = { offs[0], offs[1], offs[2], offs[3], offs[4], offs[5] };
     k_p2p_wait_dispatch<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(static_cast<uint8_t*>(own), w, (int)world,
-                                                                        epoch, hdr, err);
+                                                                        epoch, hdr, err, exl3b_peer_wait_ns());
     return cudaGetLastError() == cudaSuccess ? 0 : -6;
 }
 
@@ -389,7 +402,8 @@ int exl3b200_p2p_wait_combine(const void* own, const int64_t* offs, int64_t worl
     if (exl3b_cuda_device_info(&sm, &err) != 0) return -6;
     const Win w = { offs[0], offs[1], offs[2], offs[3], offs[4], offs[5] };
     k_p2p_wait_combine<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(static_cast<const uint8_t*>(own), w,
-                                                                       (int)world, epoch, status, err);
+                                                                       (int)world, epoch, status, err,
+                                                                       exl3b_peer_wait_ns());
     return cudaGetLastError() == cudaSuccess ? 0 : -6;
 }
 

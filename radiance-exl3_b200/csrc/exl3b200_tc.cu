@@ -483,8 +483,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                             lo[e] = __fmul_rn(a[e], s0[e]);
                             hi[e] = __fmul_rn(b[e], s1[e]);
                         }
-                        st4_bf16(y, lo);
-                        st4_bf16(y + 128, hi);
+                        st4_out(op, y, lo);
+                        st4_out(op, y + 128, hi);
                     }
                 }
                 asm volatile("bar.sync 2, %0;" ::"n"(kEpiWarps * 32) : "memory");

@@ -39,7 +39,6 @@ using exl3b::gtimer;
 using exl3b::ld_acquire_sys;
 using exl3b::st_release_sys;
 
-constexpr uint64_t kTpWaitNs = 5000000000ull;   // a rank waits at most 5 s for its peers, then reports
 
 struct TpWin {
     int64_t part, red, ctl, done;   // byte offsets in every window
@@ -49,13 +48,13 @@ __device__ __forceinline__ uint8_t* wbase(const uint64_t* peers, int r) {
     return reinterpret_cast<uint8_t*>(peers[r]);
 }
 
-// Thread 0 of a block: every rank's flag `slot` at this epoch or later, waiting at most kTpWaitNs in all.
-__device__ bool wait_all(const uint8_t* own, TpWin win, int world, int slot, uint32_t epoch) {
+// Thread 0 of a block: every rank's flag `slot` at this epoch or later, waiting at most limit_ns in all.
+__device__ bool wait_all(const uint8_t* own, TpWin win, int world, int slot, uint32_t epoch, uint64_t limit_ns) {
     const uint32_t* ctl = reinterpret_cast<const uint32_t*>(own + win.ctl);
     const uint64_t t0 = gtimer();
     for (int s = 0; s < world; ++s) {
         while ((int32_t)(ld_acquire_sys(&ctl[s * 8 + slot]) - epoch) < 0) {
-            if (gtimer() - t0 > kTpWaitNs) return false;
+            if (gtimer() - t0 > limit_ns) return false;
             __nanosleep(128);
         }
     }
@@ -103,11 +102,12 @@ __global__ void k_tp_gather_rs(const uint16_t* __restrict__ rows, int64_t pitch,
 // This rank's slice, summed over the sources in ascending order (source 0's partial is the start, so one rank's
 // sum is its partial exactly).
 __global__ void k_tp_reduce(const uint64_t* __restrict__ peers, TpWin win, int self, int world, int64_t n_rows,
-                            int64_t w4, int64_t s_cap, const uint32_t* __restrict__ epoch_p, int32_t* err) {
+                            int64_t w4, int64_t s_cap, const uint32_t* __restrict__ epoch_p, int32_t* err,
+                            uint64_t limit_ns) {
     uint8_t* own = wbase(peers, self);
     const uint32_t epoch = *epoch_p;
     __shared__ bool ok;
-    if (threadIdx.x == 0) ok = wait_all(own, win, world, 0, epoch);
+    if (threadIdx.x == 0) ok = wait_all(own, win, world, 0, epoch, limit_ns);
     __syncthreads();
     uint32_t* done = reinterpret_cast<uint32_t*>(own + win.done);
     if (ok) {
@@ -146,9 +146,9 @@ __global__ void k_tp_reduce(const uint64_t* __restrict__ peers, TpWin win, int s
 // Every owner's reduced slice into this rank's output (f32 [T][H], row pitch out_pitch4 float4s).
 __global__ void k_tp_pull(const uint64_t* __restrict__ peers, TpWin win, int self, int world, int64_t n_tok,
                           int64_t w4, int64_t slice, float4* __restrict__ out, int64_t out_pitch4,
-                          const uint32_t* __restrict__ epoch_p, int32_t* status, int32_t* err) {
+                          const uint32_t* __restrict__ epoch_p, int32_t* status, int32_t* err, uint64_t limit_ns) {
     __shared__ bool ok;
-    if (threadIdx.x == 0) ok = wait_all(wbase(peers, self), win, world, 1, *epoch_p);
+    if (threadIdx.x == 0) ok = wait_all(wbase(peers, self), win, world, 1, *epoch_p, limit_ns);
     __syncthreads();
     if (!ok) {
         if (threadIdx.x == 0) {
@@ -182,6 +182,7 @@ inline TpWin tp_win(const int64_t* offs) { return TpWin{ offs[0], offs[1], offs[
 extern "C" {
 
 int exl3b_cuda_device_info(int* sm_count, int32_t** err_word);   // exl3b200_moe.cu
+uint64_t exl3b_peer_wait_ns(void);                                // exl3b200_p2p.cu
 
 // The gather (exl3b200_moe_gather's arithmetic) writing each token's partial into its owner's window, then the
 // owners' partials flags. offs[4] = {part, red, ctl, done}.
@@ -224,7 +225,7 @@ int exl3b200_tp_reduce(const uint64_t* peers, const int64_t* offs, int64_t self,
     if (exl3b_cuda_device_info(&sm, &err) != 0) return -6;
     const int64_t w4 = width / 4;
     k_tp_reduce<<<grid_for(n_rows * w4, sm), 256, 0, static_cast<cudaStream_t>(stream)>>>(
-        peers, tp_win(offs), (int)self, (int)world, n_rows, w4, s_cap, epoch, err);
+        peers, tp_win(offs), (int)self, (int)world, n_rows, w4, s_cap, epoch, err, exl3b_peer_wait_ns());
     return cudaGetLastError() == cudaSuccess ? 0 : -6;
 }
 
@@ -243,7 +244,7 @@ int exl3b200_tp_pull(const uint64_t* peers, const int64_t* offs, int64_t self, i
     const int64_t w4 = width / 4;
     k_tp_pull<<<grid_for(n_tok * w4, sm), 256, 0, static_cast<cudaStream_t>(stream)>>>(
         peers, tp_win(offs), (int)self, (int)world, n_tok, w4, slice, reinterpret_cast<float4*>(out),
-        out_pitch / 4, epoch, status, err);
+        out_pitch / 4, epoch, status, err, exl3b_peer_wait_ns());
     return cudaGetLastError() == cudaSuccess ? 0 : -6;
 }
 

@@ -203,9 +203,11 @@ class Case:
         return "bf16" if self.base in ("moe_exl3_down", "moe_exl3_gate_up_down") else "f16"
 
     # -------------------------------------------------------------- running
-    def run(self, plugin, device=False, domain=None, stream=0, scratch=True):
+    def run(self, plugin, device=False, domain=None, stream=0, scratch=True, out_dtype=None, launch=None):
         """Launch this case on `plugin`'s row for the op. Returns dict(rc, y (uint16 bits [T, y_cols]) or None,
-        redzone_ok, inputs_ok, unrelayout_ok, layouts)."""
+        redzone_ok, inputs_ok, unrelayout_ok, layouts). `out_dtype` ("f16" / "bf16") overrides the output operand's
+        type and `launch(args_ptr, stream)` the row's launch: an entry point that takes the row's RadArgs with
+        another output type (exl3b200_moe_down_f16) runs through the same harness."""
         schema = {s["op"]: s for s in plugin.schemas()}[self.op]
         row = plugin.row(self.op, domain)
         if row is None:
@@ -251,7 +253,7 @@ class Case:
             pitch = self.y_cols + self.pitch_extra
             ptr = mem.alloc(self.T * pitch * 2, 0xFF)
             outputs[i] = (ptr, pitch)
-            tensors[i] = rad.tensor(ptr, rad.DT[self.out_dtype()], [self.T, self.y_cols], [pitch, 1])
+            tensors[i] = rad.tensor(ptr, rad.DT[out_dtype or self.out_dtype()], [self.T, self.y_cols], [pitch, 1])
         a = rad.RadArgs()
         a.t = tensors
         a.n_t = len(schema["operands"])
@@ -263,7 +265,7 @@ class Case:
             if need > 0:
                 a.scratch = mem.alloc(need, 0)
                 a.scratch_bytes = need
-        rc = row.launch(C.byref(a), stream)
+        rc = (launch or row.launch)(C.byref(a), stream)
         mem.sync()
         report["rc"] = rc
         ptr, pitch = next(iter(outputs.values()))

@@ -46,6 +46,8 @@ class Native:
         L.exl3b200_p2p_row_dst.argtypes = [_VP, _I64, _VP, _VP, _VP, _VP, _I64, _I64, _I64, _I64, _VP, _VP]
         L.exl3b200_p2p_signal_combine.argtypes = [_VP, _VP, _I64, _I64, _VP, _VP]
         L.exl3b200_moe_down_rows.argtypes = [_VP, _VP, _VP]
+        L.exl3b200_moe_down_f16.argtypes = [_VP, _VP]
+        L.exl3b200_set_peer_wait_ns.argtypes = [_I64]
         L.exl3b200_p2p_begin.argtypes = [_VP, _VP]
         L.exl3b200_moe_op_live.argtypes = [_VP, _I, _VP, _VP]
         L.exl3b200_tp_gather_rs.argtypes = [_VP, _I64, _VP, _I64, _VP, _I64, _I64, _I64, _VP, _VP, _VP, _I64, _I64,
@@ -187,6 +189,13 @@ class Native:
 
     def moe_down_rows(self, args_ref, row_dst, stream=0):
         self._check(self.lib.exl3b200_moe_down_rows(args_ref, row_dst, stream), "exl3b200_moe_down_rows")
+
+    def moe_down_f16(self, args_ref, stream=0):
+        """moe_exl3_down with f16 output rows (the row's RadArgs, y f16); returns the status."""
+        return int(self.lib.exl3b200_moe_down_f16(args_ref, stream))
+
+    def set_peer_wait_ns(self, ns):
+        self._check(self.lib.exl3b200_set_peer_wait_ns(ns), "exl3b200_set_peer_wait_ns")
 
     def p2p_begin(self, epoch, stream=0):
         self._check(self.lib.exl3b200_p2p_begin(epoch, stream), "exl3b200_p2p_begin")

@@ -22,7 +22,8 @@ class OrcOp(C.Structure):
                 ("x", C.c_void_p), ("x_dtype", C.c_int), ("x_rows", C.c_int64), ("x_pitch", C.c_int64),
                 ("y", C.c_void_p), ("y_pitch", C.c_int64), ("sorted_tok", C.c_void_p), ("expert_offset", C.c_void_p),
                 ("codes", C.POINTER(C.c_void_p)), ("suh", C.POINTER(C.c_void_p)), ("suh1", C.POINTER(C.c_void_p)),
-                ("svh", C.POINTER(C.c_void_p)), ("dn_suh", C.POINTER(C.c_void_p)), ("n_threads", C.c_int)]
+                ("svh", C.POINTER(C.c_void_p)), ("dn_suh", C.POINTER(C.c_void_p)), ("n_threads", C.c_int),
+                ("out_f16", C.c_int)]
 
 
 class Oracle:
@@ -105,8 +106,9 @@ class Oracle:
         op = {"moe_exl3_down": 0, "moe_exl3_gate_up": 1, "moe_exl3_prep_gu": 2}[base]
         return self._run(case, op, case.h_rot, case.a_rot, case.x, case.geom, "own", n_threads, prefill)
 
-    def _run(self, case, op, h_rot, a_rot, x, geom, which, n_threads, prefill=None):
+    def _run(self, case, op, h_rot, a_rot, x, geom, which, n_threads, prefill=None, out_f16=False):
         o = OrcOp()
+        o.out_f16 = 1 if out_f16 else 0
         o.op, o.bits, o.codebook, o.h_rot, o.a_rot = op, case.bits, CB.get(case.codebook, 0), h_rot, a_rot
         o.T, o.n_expert, o.top_k, o.n_class = case.T, case.n_expert, case.top_k, case.n_class
         for c in range(4):

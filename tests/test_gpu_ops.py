@@ -122,6 +122,24 @@ OPS = [
     dict(op="moe_exl3_down", M=200, top_k=10, n_expert=64, geom=[(2048, 512)], bits=4, codebook="mul1", h_rot=1),
     dict(op="moe_exl3_down_mod4", M=64, top_k=2, n_expert=8, geom=[(256, 128), (512, 128), (256, 256), (256, 128)],
          bits=7, codebook="mcg"),
+    # the four-class forms of the rotation op (to the bit) and of the whole chain (tests/ref/test_exl3ref.py:1168-1205
+    # runs the same four rank-width classes): classes of different widths over one hidden size
+    dict(op="moe_exl3_prep_gu_mod4", M=4, top_k=2, n_expert=6, geom=[(256, 256), (512, 256), (256, 128), (256, 256)],
+         bits=4, drop=0.2),
+    dict(op="moe_exl3_prep_gu_mod4", M=9, top_k=3, n_expert=8, geom=[(512, 256)], bits=3, x_dtype="bf16"),
+    dict(op="moe_exl3_gate_up_down_mod4", M=4, top_k=2, n_expert=8, geom=[(256, 256), (512, 256), (256, 256),
+                                                                         (512, 256)], bits=4, codebook="mul1"),
+    dict(op="moe_exl3_gate_up_down_mod4", M=6, top_k=2, n_expert=6, geom=[(512, 256), (256, 256)], bits=3,
+         codebook="mcg", drop=0.15),
+    # config 2, the expert MLP at M = 1 and 4 through the fused op (M = 8 and 32 are above)
+    dict(op="moe_exl3_gate_up_down", M=1, top_k=1, n_expert=1, geom=[(1024, 2048)], bits=4, codebook="mul1"),
+    dict(op="moe_exl3_gate_up_down", M=4, top_k=1, n_expert=1, geom=[(1024, 2048)], bits=4, codebook="mul1"),
+    dict(op="moe_exl3_gate_up_down", M=8, top_k=1, n_expert=1, geom=[(1024, 2048)], bits=4, codebook="mul1"),
+    # the other two codebooks at the config geometry, both bands
+    dict(op="moe_exl3_gate_up", M=8, top_k=10, n_expert=64, geom=[(1024, 2048)], bits=3, codebook="mcg", h_rot=1),
+    dict(op="moe_exl3_down", M=8, top_k=10, n_expert=64, geom=[(2048, 512)], bits=4, codebook="3inst", h_rot=1),
+    dict(op="moe_exl3_gate_up", M=1, top_k=10, n_expert=64, geom=[(1024, 2048)], bits=3, codebook="3inst"),
+    dict(op="moe_exl3_down", M=1, top_k=10, n_expert=64, geom=[(2048, 512)], bits=4, codebook="mcg", h_rot=1),
 ] + [
     # config 4, the bitrate sweep's linear: out 4096 x in 1536 (and the transpose), K = 2..8, one expert, every row
     # routed to it (the decode band at batch 1, the tensor-core band at batch 32 / 256)
@@ -398,3 +416,37 @@ def test_live_only_pass_leaves_padding_untouched(dev, plugin, T, pad):
     assert torch.equal(lay.y_rows[:R].view(torch.int16), y_ref.view(torch.int16))
     assert bool((lay.h[R:R + pad].view(torch.int16) == 0x1234).all())
     assert bool((lay.y_rows[R:R + pad].view(torch.int16) == 0x2345).all())
+
+
+# ---------------------------------------------------------------------------------------------- the f16-output linear
+# config 1: a single EXL3 linear, 16 rows of 2048 -> 512, f16 out (the decode band at a handful of rows, the tensor-core
+# band from 16 rows an expert); the oracle's down with its output rounded to f16 instead of bf16
+F16_OUT = [
+    dict(op="moe_exl3_down", M=16, top_k=1, n_expert=1, geom=[(512, 2048)], bits=4, codebook="mul1"),     # config 1
+    dict(op="moe_exl3_down", M=3, top_k=1, n_expert=1, geom=[(512, 2048)], bits=4, codebook="mul1"),
+    dict(op="moe_exl3_down", M=64, top_k=1, n_expert=1, geom=[(4096, 1536)], bits=3, codebook="mcg"),
+    dict(op="moe_exl3_down", M=5, top_k=2, n_expert=4, geom=[(256, 256)], bits=5, codebook="3inst", h_rot=1,
+         drop=0.2),
+]
+
+
+@pytest.mark.parametrize("spec", F16_OUT, ids=lambda s: f"M{s['M']}-{s['geom'][0][0]}x{s['geom'][0][1]}-K{s['bits']}")
+def test_down_with_f16_output_matches_the_oracle(dev, plugin, orc, native, spec):
+    case = _case(spec, seed=99)
+    got = case.run(plugin, device=True, out_dtype="f16", launch=lambda a, s: native.moe_down_f16(a, s))
+    assert got["rc"] == 0, got["rc"]
+    assert got["redzone_ok"] and got["inputs_ok"]
+    want = orc._run(case, 0, case.h_rot, 0, case.x, case.geom, "own", os.cpu_count() or 4, out_f16=True)
+    ok, detail = compare(got["y"], want, "f16", REL_TOL, COS_TOL)
+    assert ok, detail
+    # the op's own bf16 rows from the same kernels: two roundings of one f32 value, so they agree to a bf16 half-ulp
+    bf = case.run(plugin, device=True)["y"]
+    a, b = X.bits_to_f32(got["y"], "f16"), X.bits_to_f32(bf, "bf16")
+    assert np.all(np.abs(a - b) <= np.abs(a) * 2.0 ** -8 + 1e-30)
+
+
+def test_down_f16_refuses_a_bf16_output(dev, plugin, native):
+    case = _case(F16_OUT[0])
+    got = case.run(plugin, device=True, launch=lambda a, s: native.moe_down_f16(a, s))   # y declared bf16
+    assert got["rc"] == -2                                                             # RAD_E_DTYPE
+    assert (got["y"] == 0xFFFF).all()                                                  # nothing written

@@ -19,6 +19,7 @@ from exl3b200 import library_path  # noqa: E402
 
 REL_TOL, COS_TOL = 1e-2, 0.9999
 MAX_PAIRS = 1 << 18
+RAD_E_SHAPE = -1          # the shape refusal status of include/rad_types.h
 _I64, _VP = C.c_int64, C.c_void_p
 
 
@@ -100,5 +101,18 @@ def test_noalloc_gather_refuses_past_its_limit(lib):
     rc = lib.exl3b200_moe_gather_noalloc(dummy.data_ptr(), 8, dummy.data_ptr(), 0, dummy.data_ptr(), T, k, 8,
                                          y.data_ptr(), None)
     torch.cuda.synchronize()
-    assert rc != 0
+    assert rc == RAD_E_SHAPE
+    assert (y.cpu().numpy() == 7.0).all()
+
+
+@pytest.mark.parametrize("n_tok,top_k", [(1 << 40, 1 << 30), (1 << 62, 4), (3, (1 << 18) + 1), (1 << 33, 1 << 31)])
+def test_noalloc_gather_refuses_sizes_whose_product_wraps(lib, n_tok, top_k):
+    # n_tok * top_k of these would wrap around int64 (or pass the limit by one factor alone): the entry point must
+    # refuse them with the shape status before it forms the product, and write nothing
+    y = torch.full((4, 8), 7.0, dtype=torch.float32, device="cuda")
+    dummy = torch.zeros(16, dtype=torch.int32, device="cuda")
+    rc = lib.exl3b200_moe_gather_noalloc(dummy.data_ptr(), 8, dummy.data_ptr(), 0, dummy.data_ptr(), n_tok, top_k,
+                                         8, y.data_ptr(), None)
+    torch.cuda.synchronize()
+    assert rc == RAD_E_SHAPE
     assert (y.cpu().numpy() == 7.0).all()
