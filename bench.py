@@ -225,6 +225,204 @@ def bitrate_sweep(plugin, hbm, tflops):
     return res
 
 
+def bitrate_cpu_reference():
+    """The reference's exl3ref beside the config-4 sweep: one call of moe_exl3_down on the out 4096 x in 1536 linear
+    at batch 1 for every K, and at batch 256 for K = 4 (one host core, the launch alone)."""
+    out = {}
+    for K in range(2, 9):
+        t = reference_op_seconds("moe_exl3_down", reps=1, M=1, top_k=1, n_expert=1, geom=[(4096, 1536)], bits=K,
+                                 codebook="mul1")
+        out[f"K{K}_B1"] = {"us": round(t * 1e6, 1), "gbs": round((4096 * 1536 * K / 8 + 3072 + 8192) / t / 1e9, 4)}
+    t = reference_op_seconds("moe_exl3_down", reps=1, M=256, top_k=1, n_expert=1, geom=[(4096, 1536)], bits=4,
+                             codebook="mul1")
+    out["K4_B256"] = {"us": round(t * 1e6, 1), "tflops": round(2 * 256 * 4096 * 1536 / t / 1e12, 5)}
+    out["cores"], out["kind"], out["orientation"] = 1, "reference", "out 4096 x in 1536"
+    return out
+
+
+def _graph_time(run_all, reps=5):
+    """Microseconds of one replay of a CUDA graph of `run_all(stream)` (a warm-up, then `reps` replays between CUDA
+    events on the current stream)."""
+    import torch
+    run_all(torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        run_all(torch.cuda.current_stream().cuda_stream)
+    for _ in range(3):
+        g.replay()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        g.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    del g
+    return e0.elapsed_time(e1) * 1e3 / reps
+
+
+def reference_op_seconds(op, reps=3, **case_kw):
+    """The reference's own CPU implementation (kernels/exl3ref built from its sources, oracle/_ref) of one op on a
+    seeded case of the given shape: the median wall time of the row's launch alone (buffers and layout hooks set up
+    outside the timed call), single-threaded as exl3ref is."""
+    from exl3b200 import cases as X
+    from exl3b200 import rad
+    from oracle_bind import REF_SO
+    plugin = rad.Plugin(REF_SO)
+    row = plugin.row(op)
+    case = X.Case(op, 77, **case_kw)
+    times = []
+
+    def timed(a, s):
+        t0 = time.perf_counter()
+        rc = row.launch(a, s)
+        times.append(time.perf_counter() - t0)
+        return rc
+
+    for _ in range(reps):
+        r = case.run(plugin, device=False, launch=timed)
+        if r["rc"] != 0:
+            raise RuntimeError(f"exl3ref {op}: {r['rc']}")
+    return float(np.median(times))
+
+
+def single_expert_configs(plugin, hbm, with_cpu):
+    """Config 1 (one EXL3 linear, 16 rows of 2048 -> 512, K=4 mul1, f16 out: exl3b200_moe_down_f16) and config 2
+    (one expert MLP, gate/up [512, 2048] and down [2048, 512] at K=4, M = 1, 4, 8, 32 rows: the moe_exl3_gate_up_down
+    row), each timed as one call over its own copy of the weights (copies totalling over 3x the 126 MB L2, replayed
+    as one CUDA graph, so every call streams its weights from HBM). Beside each: the reference's exl3ref on one host
+    core (moe_exl3_down with bf16 rows for config 1 -- the reference has no f16-output form -- and
+    moe_exl3_gate_up_down for config 2)."""
+    from exl3b200.layer import ExpertMlps, Linears
+    res = {}
+    n1 = int(np.ceil(3 * 126e6 / 529408))
+    lin = Linears(plugin, 512, 2048, 4, 16, n1, seed=11, out_f16=True)
+    us = _graph_time(lambda s: [lin.run(i, s) for i in range(n1)]) / n1
+    c1 = {"us": round(us, 2), "gbs": round(lin.bytes_per_call() / (us / 1e6) / 1e9, 1),
+          "frac_hbm": round(lin.bytes_per_call() / (us / 1e6) / 1e9 / hbm, 3), "bytes_per_call": lin.bytes_per_call(),
+          "tokens_per_s": round(16 / (us / 1e6), 1), "copies": n1, "out": "f16", "entry": "exl3b200_moe_down_f16"}
+    if with_cpu:
+        t = reference_op_seconds("moe_exl3_down", M=16, top_k=1, n_expert=1, geom=[(512, 2048)], bits=4,
+                                 codebook="mul1")
+        c1["cpu_reference"] = {"us": round(t * 1e6, 1), "tokens_per_s": round(16 / t, 1), "cores": 1,
+                               "kind": "reference", "op": "moe_exl3_down (bf16 rows)"}
+        c1["speedup_vs_cpu"] = round(t * 1e6 / us, 1)
+    del lin
+    res["config1_linear_16x2048_to_512"] = c1
+    c2 = {}
+    n2 = int(np.ceil(3 * 126e6 / 1588224))
+    for M in (1, 4, 8, 32):
+        mlp = ExpertMlps(plugin, 2048, 512, 4, M, n2, seed=20 + M)
+        us = _graph_time(lambda s: [mlp.run(i, s) for i in range(n2)]) / n2
+        e = {"us": round(us, 2), "gbs": round(mlp.bytes_per_call() / (us / 1e6) / 1e9, 1),
+             "frac_hbm": round(mlp.bytes_per_call() / (us / 1e6) / 1e9 / hbm, 3),
+             "tokens_per_s": round(M / (us / 1e6), 1), "copies": n2}
+        if with_cpu:
+            t = reference_op_seconds("moe_exl3_gate_up_down", M=M, top_k=1, n_expert=1, geom=[(1024, 2048)], bits=4,
+                                     codebook="mul1")
+            e["cpu_reference"] = {"us": round(t * 1e6, 1), "tokens_per_s": round(M / t, 1), "cores": 1,
+                                  "kind": "reference"}
+            e["speedup_vs_cpu"] = round(t * 1e6 / us, 1)
+        c2[f"M{M}"] = e
+        del mlp
+    res["config2_expert_mlp_2048x512_K4"] = c2
+    res["bytes_per_call"] = {"config1": 529408, "config2": 1588224}
+    return res
+
+
+def _time_steps(step, sh, reps, use_graph):
+    """ms of one call of step(stream): captured once in a CUDA graph and replayed `reps` times between CUDA events
+    (or run eagerly when capture is not possible), after a warm-up."""
+    import torch
+    step(sh)
+    torch.cuda.synchronize()
+    run = None
+    if use_graph:
+        try:
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                step(torch.cuda.current_stream().cuda_stream)
+            run = g.replay
+        except Exception:
+            run = None
+    if run is None:
+        run = lambda: step(sh)  # noqa: E731
+    for _ in range(2):
+        run()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        run()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / reps
+
+
+def skewed_routing(layer, T, sh, world, rank, dev, use_graph):
+    """Config 3 under the reference's skewed draw (tools/perfmoe.cpp:50-51): expert popularity lognormal with
+    sigma 0.8 (the same draw on every rank), each token's top-10 a Gumbel-top-k sample of it -- logits = log
+    popularity + Gumbel noise, which the router's softmax top-k then selects exactly. Returns ms a step, tokens/s
+    and how uneven the experts' rows came out."""
+    import torch
+    gp = torch.Generator(device=dev)
+    gp.manual_seed(4242)
+    log_pop = torch.randn((E,), generator=gp, device=dev) * 0.8
+    gn = torch.Generator(device=dev)
+    gn.manual_seed(4343 + rank)
+    u = torch.rand((T, E), generator=gn, device=dev).clamp_(1e-12, 1 - 1e-7)
+    logits = (log_pop[None, :] - torch.log(-torch.log(u))).contiguous()
+    ms = _time_steps(lambda s: layer.forward(T, s, logits=logits), sh, 10, use_graph)
+    layer.forward(T, sh, logits=logits)
+    torch.cuda.synchronize()
+    ids = layer.ids.reshape(-1)[:T * TOPK].cpu().numpy()
+    counts = np.bincount(ids[ids >= 0], minlength=E)
+    t = torch.tensor([ms], device=dev)
+    if world > 1:
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    ms = float(t.item())
+    return {"ms": round(ms, 4), "tokens_per_s": round(T * world / (ms / 1e3), 1),
+            "rows_per_expert_max": int(counts.max()), "rows_per_expert_mean": round(float(counts.mean()), 2),
+            "live_experts_rank0_routing": int((counts > 0).sum()),
+            "draw": "log popularity ~ 0.8 N(0,1) per expert (shared), Gumbel(0,1) noise per (token, expert)"}
+
+
+def stack48(layer, world, rank, dev, sh, use_graph, n_layers=48, tokens=(2048, 8)):
+    """Config 5: a stack of 48 routed-MoE layers, each with its own weights (seeded, resident: 48 x 679 MB / N per
+    GPU) and its own routing (seeded logits per layer), run back to back over the same token rows; the weights of
+    every layer stream from HBM each step. tokens/s = tokens a GPU x N / the stack's time."""
+    import torch
+    base = layer.ops.local if world > 1 else layer
+    for i in range(1, n_layers):
+        base.add_weight_set(seed=9000 + 131 * i + 7 * rank)
+    out = {}
+    for T in tokens:
+        if T > layer.max_tokens:
+            continue
+        lgs = []
+        for i in range(n_layers):
+            g = torch.Generator(device=dev)
+            g.manual_seed(12000 + 17 * i + 1009 * rank + T)
+            lgs.append(torch.randn((T, E), generator=g, device=dev))
+
+        def step(s):
+            for i in range(n_layers):
+                base.use_weight_set(i)
+                layer.forward(T, s, logits=lgs[i])
+
+        ms = _time_steps(step, sh, 5, use_graph)
+        t = torch.tensor([ms], device=dev)
+        if world > 1:
+            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms = float(t.item())
+        out[f"T{T}"] = {"ms_per_stack_step": round(ms, 3), "ms_per_layer": round(ms / n_layers, 4),
+                        "tokens_per_s": round(T * world / (ms / 1e3), 1)}
+    base.use_weight_set(0)
+    out["layers"] = n_layers
+    out["weights_resident_gb_per_gpu"] = round(n_layers * sum(base.expert_bytes()) * base.n_local / 1e9, 2)
+    return out
+
+
 def bench_ours(args, rank, world, local_rank):
     import torch
     torch.cuda.set_device(local_rank)
@@ -487,10 +685,24 @@ def bench_ours(args, rank, world, local_rank):
             if graph_ok:
                 del gph
 
-    # ---- config 4: the bitrate sweep of one linear (1 GPU)
-    bitrates = None
+    # ---- config 4: the bitrate sweep of one linear (1 GPU), configs 1 and 2 (single expert), the reference beside
+    bitrates = singles = None
     if world == 1 and not args.no_sweep:
         bitrates = bitrate_sweep(plugin, hbm, tflops)
+        if rank == 0 and not args.no_cpu_baseline:
+            try:
+                bitrates["cpu_reference"] = bitrate_cpu_reference()
+            except Exception as exc:
+                bitrates["cpu_reference"] = {"unavailable": str(exc)}
+        singles = single_expert_configs(plugin, hbm, with_cpu=rank == 0 and not args.no_cpu_baseline)
+
+    # ---- skewed routing (config 3 under perfmoe's popularity draw) and config 5 (the 48-layer stack)
+    use_graph = (world == 1 or args.transport == "p2p") and not args.profile
+    skew = stack = None
+    if not args.no_sweep and not tp_mode:
+        skew = skewed_routing(layer, T, sh, world, rank, dev, use_graph)
+    if not args.no_stack and not tp_mode and use_graph:
+        stack = stack48(layer, world, rank, dev, sh, use_graph)
 
     # ---- the CPU baseline (rank 0, one GPU): the reference library on a bounded sample
     cpu = None
@@ -509,6 +721,7 @@ def bench_ours(args, rank, world, local_rank):
         # parallelism returns every pair's own down row and sums a token's slots in the same order, so the two must
         # be equal to the bit; the width split sums per-rank partials (each rounded to bf16 rows), so it is held to
         # the expert-output tolerance (max |diff| <= 1e-2 max |ref|, cosine >= 0.9999)
+        layer.forward(T, sh)                 # this rank's tokens again (the sections above ran other routings)
         full.x[:T].copy_(layer.x[:T])
         full.logits[:T].copy_(layer.logits[:T])
         full.forward(T, sh)
@@ -560,7 +773,8 @@ def bench_ours(args, rank, world, local_rank):
                      "other": {"gate_up_op_ms": round(gu_ms, 4), "k_prep_ms": round(prep_ms, 4),
                                "down_op_ms": round(dn_ms, 4)}},
         "clocks": clk, "gpu_launches": int(launches_per_step * args.steps),
-        "e2e": e2e, "cpu_baseline": cpu, "sweep": sweep, "bitrate_sweep": bitrates, "wall_s": round(wall, 3),
+        "e2e": e2e, "cpu_baseline": cpu, "sweep": sweep, "bitrate_sweep": bitrates, "single_expert": singles,
+        "skewed_routing": skew, "stack48": stack, "wall_s": round(wall, 3),
         "ep_phases_ms": ep_phases,
     }
     if multi_check is not None:
@@ -583,12 +797,13 @@ def main():
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-stack", action="store_true", help="skip config 5, the 48-layer stack")
     ap.add_argument("--profile", action="store_true",
                     help="for a profiler run: no clock soak, sweep, end-to-end leg or CPU baseline")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     if args.profile:
-        args.no_sweep = args.no_e2e = args.no_cpu_baseline = True
+        args.no_sweep = args.no_e2e = args.no_cpu_baseline = args.no_stack = True
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))
     local_rank = int(os.environ.get("LOCAL_RANK", 0))

@@ -86,6 +86,13 @@ int     exl3b200_moe_gather(const uint16_t* rows, int64_t row_pitch, const int32
                             const float* w, int64_t n_tok, int64_t top_k, int64_t width, float* y, void* work,
                             void* stream);
 
+/* moe_gather writing y as bf16 (the f32 sum of each element rounded to nearest even): the layer's output in the
+ * engine's hidden-state type (the MoE block adds it to a bf16 stream, rad_block_moe_exl3.h:1660-1667). Same
+ * arguments and refusals as exl3b200_moe_gather, y uint16 bf16 bits [n_tok][width]. */
+int     exl3b200_moe_gather_bf16(const uint16_t* rows, int64_t row_pitch, const int32_t* sorted_tok, int64_t n_rows,
+                                 const float* w, int64_t n_tok, int64_t top_k, int64_t width, uint16_t* y, void* work,
+                                 void* stream);
+
 /* moe_gather for a caller that cannot allocate device memory -- one whose memory is fixed up front (a serving
  * engine that owns a preallocated pool and forbids cudaMalloc on its launch path, a process running under a
  * strict device-memory budget, code that must not grow the CUDA allocator's footprint). No counterpart in the
@@ -100,6 +107,53 @@ int     exl3b200_moe_gather(const uint16_t* rows, int64_t row_pitch, const int32
 int     exl3b200_moe_gather_noalloc(const uint16_t* rows, int64_t row_pitch, const int32_t* sorted_tok,
                                     int64_t n_rows, const float* w, int64_t n_tok, int64_t top_k, int64_t width,
                                     float* y, void* stream);
+
+/* One routed-MoE layer, the sequence the engine's MoE block issues for a pass (rad_block_moe_exl3.h:1763-1900):
+ * router_topk + moe_scatter -> moe_exl3_gate_up (h_rot 1) -> moe_exl3_down (h_rot 1) -> moe_gather, the two
+ * expert ops through this library's plugin rows with RadArgs built in C. The caller holds the weights:
+ *   gu_codes, dn_codes  device tables of n_local u64 addresses, each an expert's STORED record (the layout hook's
+ *                       form: exl3b200_codes_to_record of gate's rows then up's for gate_up)
+ *   suh, suh1 f16 [n_local][hidden]; svh_gu f16 [n_local][2 width]; dn_suh f16 [n_local][width];
+ *   svh_dn f16 [n_local][hidden]   (stacked, dense)
+ * Tokens route over n_expert experts; this caller serves [expert_base, expert_base + n_local) (the rest dropped).
+ * exl3b200_moe_layer_work_bytes sizes ONE device block for up to max_tokens tokens a pass; the caller allocates it
+ * once and exl3b200_moe_layer_carve cuts it into the buffers (ids, w, sorted_tok, expert_offset, h, the bf16 down
+ * rows, the rows' scratch, the gather's map). exl3b200_moe_layer_forward then allocates, synchronises and reads
+ * nothing on the host: it enqueues the kernels on `stream` and writes out [T][hidden] as f32 (out_dtype RAD_F32) or
+ * bf16 (RAD_BF16). No counterpart in the reference (the engine drives the ops); the ops' results are the rows'. */
+typedef struct Exl3bLayerDesc {
+    int64_t     n_expert, n_local, expert_base;
+    int64_t     hidden, width, top_k;
+    int32_t     bits_gu, bits_dn, codebook;   /* codebook 0 3inst, 1 mcg, 2 mul1 */
+    int32_t     pad0;
+    const void* gu_codes;
+    const void* dn_codes;
+    const void* suh;
+    const void* suh1;
+    const void* svh_gu;
+    const void* dn_suh;
+    const void* svh_dn;
+} Exl3bLayerDesc;
+typedef struct Exl3bLayerBufs {
+    int64_t   max_tokens;
+    int32_t*  ids;            /* [max_tokens][top_k] */
+    float*    w;              /* [max_tokens][top_k] */
+    int32_t*  sorted_tok;     /* [max_tokens * top_k] */
+    int32_t*  expert_offset;  /* [n_local + 1] */
+    void*     scatter_work;
+    uint16_t* h;              /* f16 [max_tokens * top_k][width] */
+    uint16_t* y_rows;         /* bf16 [max_tokens * top_k][hidden] */
+    void*     gu_scratch;
+    int64_t   gu_scratch_bytes;
+    void*     dn_scratch;
+    int64_t   dn_scratch_bytes;
+    void*     gather_work;
+} Exl3bLayerBufs;
+int64_t exl3b200_moe_layer_work_bytes(const Exl3bLayerDesc* desc, int64_t max_tokens);
+int     exl3b200_moe_layer_carve(const Exl3bLayerDesc* desc, int64_t max_tokens, void* work, int64_t work_bytes,
+                                 Exl3bLayerBufs* bufs);
+int     exl3b200_moe_layer_forward(const Exl3bLayerDesc* desc, const Exl3bLayerBufs* bufs, const uint16_t* x,
+                                   const float* logits, int64_t n_tok, void* out, int out_dtype, void* stream);
 
 /* Expert parallelism (one process a GPU; expert e held by rank e / n_local; no counterpart in the reference,
  * which runs on one device -- the engine's EP plumbing would call these around its all-to-alls):

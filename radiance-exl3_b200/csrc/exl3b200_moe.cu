@@ -369,8 +369,28 @@ __global__ void k_scatter_place(const int32_t* __restrict__ ids, int64_t n_pairs
 
 // ------------------------------------------------------------------------------------------ gather
 // One block a token; thread columns 4 at a time; slots in ascending order.
+// The gather's output: f32, or bf16 (the f32 sum rounded to nearest even: the engine's hidden-state type).
+__device__ __forceinline__ void gst(float* y, float v) { *y = v; }
+__device__ __forceinline__ void gst(__nv_bfloat16* y, float v) { *y = __float2bfloat16_rn(v); }
+__device__ __forceinline__ void gst8(float* y, const float a[8]) {
+    float4* o = reinterpret_cast<float4*>(y);
+    o[0] = make_float4(a[0], a[1], a[2], a[3]);
+    o[1] = make_float4(a[4], a[5], a[6], a[7]);
+}
+__device__ __forceinline__ void gst8(__nv_bfloat16* y, const float a[8]) {
+    uint4 u;
+    uint32_t* w = reinterpret_cast<uint32_t*>(&u);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        const __nv_bfloat162 h = __floats2bfloat162_rn(a[2 * q], a[2 * q + 1]);
+        w[q] = *reinterpret_cast<const uint32_t*>(&h);
+    }
+    *reinterpret_cast<uint4*>(y) = u;
+}
+
+template <typename OutT>
 __global__ void k_gather(const uint16_t* __restrict__ rows, int64_t pitch, const int32_t* __restrict__ pos,
-                         const float* __restrict__ w, int top_k, int64_t width, float* __restrict__ y) {
+                         const float* __restrict__ w, int top_k, int64_t width, OutT* __restrict__ y) {
     const int64_t t = blockIdx.x;
     for (int64_t n = 4 * (int64_t)threadIdx.x; n < width; n += 4 * (int64_t)blockDim.x) {
         float acc[4] = { 0.f, 0.f, 0.f, 0.f };
@@ -385,22 +405,21 @@ __global__ void k_gather(const uint16_t* __restrict__ rows, int64_t pitch, const
         }
 #pragma unroll
         for (int q = 0; q < 4; ++q)
-            if (n + q < width) y[t * width + n + q] = acc[q];
+            if (n + q < width) gst(y + t * width + n + q, acc[q]);
     }
 }
 
 // One block a token, a thread 8 columns (16-byte loads of bf16 rows): exl3b::gather_row8, the slots summed in
 // ascending order exactly as k_gather does. rows 16-byte aligned with a pitch of a multiple of 8 elements, width a
 // multiple of 8, y 16-byte aligned (the host checks).
+template <typename OutT>
 __global__ void k_gather_v8(const uint16_t* __restrict__ rows, int64_t pitch, const int32_t* __restrict__ pos,
-                            const float* __restrict__ w, int top_k, int64_t width, float* __restrict__ y) {
+                            const float* __restrict__ w, int top_k, int64_t width, OutT* __restrict__ y) {
     const int64_t t = blockIdx.x;
     for (int64_t n = 8 * (int64_t)threadIdx.x; n < width; n += 8 * (int64_t)blockDim.x) {
         float acc[8];
         exl3b::gather_row8(rows, pitch, pos + t * top_k, w + t * top_k, top_k, n, acc);
-        float4* o = reinterpret_cast<float4*>(y + t * width + n);
-        o[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
-        o[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+        gst8(y + t * width + n, acc);
     }
 }
 
@@ -408,9 +427,10 @@ __global__ void k_gather_v8(const uint16_t* __restrict__ rows, int64_t pitch, co
 // k_invert launch), then sums them exactly as k_gather_v8 does. At most kGatherSmallSlots slots a token.
 constexpr int kGatherSmallSlots = 32;
 constexpr int64_t kGatherSmallRows = 4096;
+template <typename OutT>
 __global__ void k_gather_small(const uint16_t* __restrict__ rows, int64_t pitch, const int32_t* __restrict__ sorted_tok,
                                int64_t n_rows, const float* __restrict__ w, int top_k, int64_t width,
-                               float* __restrict__ y) {
+                               OutT* __restrict__ y) {
     __shared__ int32_t pos[kGatherSmallSlots];
     const int64_t t = blockIdx.x;
     for (int s = threadIdx.x; s < top_k; s += blockDim.x) pos[s] = -1;
@@ -424,9 +444,7 @@ __global__ void k_gather_small(const uint16_t* __restrict__ rows, int64_t pitch,
     for (int64_t n = 8 * (int64_t)threadIdx.x; n < width; n += 8 * (int64_t)blockDim.x) {
         float acc[8];
         exl3b::gather_row8(rows, pitch, pos, w + t * top_k, top_k, n, acc);
-        float4* o = reinterpret_cast<float4*>(y + t * width + n);
-        o[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
-        o[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+        gst8(y + t * width + n, acc);
     }
 }
 
@@ -553,9 +571,11 @@ int exl3b200_router_scatter(const float* logits, int64_t n_tok, int64_t n_route,
 
 int64_t exl3b200_moe_gather_work_bytes(int64_t n_tok, int64_t top_k) { return (n_tok * top_k > 0 ? n_tok * top_k : 1) * 4; }
 
-int exl3b200_moe_gather(const uint16_t* rows, int64_t row_pitch, const int32_t* sorted_tok, int64_t n_rows,
-                        const float* w, int64_t n_tok, int64_t top_k, int64_t width, float* y, void* work,
-                        void* stream) {
+extern "C++" {
+template <typename OutT>
+static int gather_impl(const uint16_t* rows, int64_t row_pitch, const int32_t* sorted_tok, int64_t n_rows,
+                       const float* w, int64_t n_tok, int64_t top_k, int64_t width, OutT* y, void* work,
+                       void* stream) {
     if (!rows || !sorted_tok || !w || !y || !work || n_tok < 0 || top_k < 1 || width < 1) return -12;
     // the pair count n_tok * top_k indexes int32 maps and the kernels take top_k as an int: sizes whose product
     // would not fit are refused before it is formed
@@ -565,7 +585,7 @@ int exl3b200_moe_gather(const uint16_t* rows, int64_t row_pitch, const int32_t* 
     const bool v8 = aligned16(rows) && row_pitch % 8 == 0 && width % 8 == 0 && aligned16(y);
     if (v8 && n_rows <= kGatherSmallRows && top_k <= kGatherSmallSlots) {
         // few rows: each token finds its own rows, one launch
-        k_gather_small<<<(unsigned)n_tok, 256, 0, st>>>(rows, row_pitch, sorted_tok, n_rows, w, (int)top_k, width, y);
+        k_gather_small<OutT><<<(unsigned)n_tok, 256, 0, st>>>(rows, row_pitch, sorted_tok, n_rows, w, (int)top_k, width, y);
         return cudaGetLastError() == cudaSuccess ? 0 : -6;
     }
     int32_t* pos = static_cast<int32_t*>(work);
@@ -573,10 +593,25 @@ int exl3b200_moe_gather(const uint16_t* rows, int64_t row_pitch, const int32_t* 
     if (n_rows > 0)
         exl3b::k_invert<<<(unsigned)((n_rows + 255) / 256), 256, 0, st>>>(sorted_tok, n_rows, n_tok * top_k, pos);
     if (v8)
-        k_gather_v8<<<(unsigned)n_tok, 256, 0, st>>>(rows, row_pitch, pos, w, (int)top_k, width, y);
+        k_gather_v8<OutT><<<(unsigned)n_tok, 256, 0, st>>>(rows, row_pitch, pos, w, (int)top_k, width, y);
     else
-        k_gather<<<(unsigned)n_tok, 256, 0, st>>>(rows, row_pitch, pos, w, (int)top_k, width, y);
+        k_gather<OutT><<<(unsigned)n_tok, 256, 0, st>>>(rows, row_pitch, pos, w, (int)top_k, width, y);
     return cudaGetLastError() == cudaSuccess ? 0 : -6;
+}
+
+}  // extern "C++"
+
+int exl3b200_moe_gather(const uint16_t* rows, int64_t row_pitch, const int32_t* sorted_tok, int64_t n_rows,
+                        const float* w, int64_t n_tok, int64_t top_k, int64_t width, float* y, void* work,
+                        void* stream) {
+    return gather_impl(rows, row_pitch, sorted_tok, n_rows, w, n_tok, top_k, width, y, work, stream);
+}
+
+int exl3b200_moe_gather_bf16(const uint16_t* rows, int64_t row_pitch, const int32_t* sorted_tok, int64_t n_rows,
+                             const float* w, int64_t n_tok, int64_t top_k, int64_t width, uint16_t* y, void* work,
+                             void* stream) {
+    return gather_impl(rows, row_pitch, sorted_tok, n_rows, w, n_tok, top_k, width,
+                       reinterpret_cast<__nv_bfloat16*>(y), work, stream);
 }
 
 // ------------------------------------------------------------------------------------------ the gather, allocating nothing
@@ -611,9 +646,9 @@ int exl3b200_moe_gather_noalloc(const uint16_t* rows, int64_t row_pitch, const i
     if (n_rows > 0)
         exl3b::k_invert<<<(unsigned)((n_rows + 255) / 256), 256, 0, st>>>(sorted_tok, n_rows, n_tok * top_k, pos);
     if (aligned16(rows) && row_pitch % 8 == 0 && width % 8 == 0 && aligned16(y))
-        k_gather_v8<<<(unsigned)n_tok, 256, 0, st>>>(rows, row_pitch, pos, w, (int)top_k, width, y);
+        k_gather_v8<float><<<(unsigned)n_tok, 256, 0, st>>>(rows, row_pitch, pos, w, (int)top_k, width, y);
     else
-        k_gather<<<(unsigned)n_tok, 256, 0, st>>>(rows, row_pitch, pos, w, (int)top_k, width, y);
+        k_gather<float><<<(unsigned)n_tok, 256, 0, st>>>(rows, row_pitch, pos, w, (int)top_k, width, y);
     return cudaGetLastError() == cudaSuccess ? 0 : -6;
 }
 

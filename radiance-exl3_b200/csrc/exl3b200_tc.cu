@@ -46,13 +46,10 @@ constexpr int kTcWarps = kDecWarp0 + kDecWarps;      // 27
 constexpr int kTcThreads = kTcWarps * 32;           // 864
 constexpr int kNT = 64;                              // sorted rows a unit (the MMA's N)
 constexpr int kBox = 64;                             // k of one TMA box = one SWIZZLE_128B atom row (128 B)
-#ifndef EXL3B_TC_KC
-#define EXL3B_TC_KC 128
-#endif
-constexpr int kKC = EXL3B_TC_KC;                     // k a pipeline chunk: one handoff between the roles
+constexpr int kKC = 128;                             // k a pipeline chunk: one handoff between the roles
 constexpr int kKT = kKC / 16;                        // k tiles a chunk
 constexpr int kNBox = kKC / kBox;                    // boxes a half of a chunk
-constexpr int kStA = kKC == 64 ? 4 : 2;              // A stages (tensor memory)
+constexpr int kStA = 2;                              // A stages (tensor memory)
 constexpr int kBTile = kNT * kBox * 2;               // one box of input rows: 8 KB
 constexpr int kBHalf = kNBox * kBTile;               // one half's input rows of a chunk
 constexpr int kEpiCols = 128 + 4;                    // staging row (f32), padded
@@ -70,7 +67,7 @@ struct TcCfg {
     // the record ring runs deep (the rows are small, latency-bound reads): 3..12 stages within 64 KB
     static constexpr int ST_R = (64 * 1024 / REC_STAGE) < 3 ? 3 : (64 * 1024 / REC_STAGE) > 12 ? 12 : (64 * 1024 / REC_STAGE);
     // input-row stages: as many as shared memory leaves beside the record ring
-    static constexpr int ST_B = kKC == 64 ? 6 : (BITS >= 6 ? 3 : 4);
+    static constexpr int ST_B = BITS >= 6 ? 3 : 4;
 };
 
 // ------------------------------------------------------------------------------------------ smem descriptors
@@ -88,16 +85,23 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t smem_addr) {
 // kind::f16, A = B = f16, D = f32, both K-major, M = 128, N = kNT.
 constexpr uint32_t kIdesc = (1u << 4) | ((uint32_t)(kNT >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
 
-// D[tmem_d] (+)= A[tmem_a] * B[bdesc]: A 128 lanes x 16 k of f16 in 8 columns (k pair 2c, 2c+1 in column c).
-// Executed by the whole MMA warp, issued by the elected lane (a warp-uniform issue runs at the tensor cores' rate).
-__device__ __forceinline__ void umma_f16_ts_el(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t accumulate) {
+// The 8 MMAs of one 128-row block over a 128-k chunk (K = 16 each): A from tensor memory at ta, ta + 8, ..., B from
+// the two 64-k boxes of the input stage (descriptors db0, db1; a 16-k step adds 32 bytes = 2 to the start address).
+// One elected lane issues all eight; the first accumulates only when `acc` is nonzero, the others always.
+__device__ __forceinline__ void umma_block8_el(uint32_t d, uint32_t ta, uint64_t db0, uint64_t db1, uint32_t acc) {
     asm volatile(
-        "{\n .reg .pred p, e;\n setp.ne.b32 p, %3, 0;\n elect.sync _|e, 0xffffffff;\n"
-        " @e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %4, p;\n}\n" ::"r"(tmem_d),
-        "r"(tmem_a), "l"(bdesc), "r"(accumulate), "r"(kIdesc));
+        "{\n .reg .pred p, e, t;\n .reg .b32 a;\n .reg .b64 b;\n"
+        " setp.ne.b32 p, %4, 0;\n setp.eq.b32 t, 0, 0;\n elect.sync _|e, 0xffffffff;\n"
+        " @e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %5, p;\n"
+        " add.u32 a, %1, 8;  add.u64 b, %2, 2;\n @e tcgen05.mma.cta_group::1.kind::f16 [%0], [a], b, %5, t;\n"
+        " add.u32 a, %1, 16; add.u64 b, %2, 4;\n @e tcgen05.mma.cta_group::1.kind::f16 [%0], [a], b, %5, t;\n"
+        " add.u32 a, %1, 24; add.u64 b, %2, 6;\n @e tcgen05.mma.cta_group::1.kind::f16 [%0], [a], b, %5, t;\n"
+        " add.u32 a, %1, 32;\n @e tcgen05.mma.cta_group::1.kind::f16 [%0], [a], %3, %5, t;\n"
+        " add.u32 a, %1, 40; add.u64 b, %3, 2;\n @e tcgen05.mma.cta_group::1.kind::f16 [%0], [a], b, %5, t;\n"
+        " add.u32 a, %1, 48; add.u64 b, %3, 4;\n @e tcgen05.mma.cta_group::1.kind::f16 [%0], [a], b, %5, t;\n"
+        " add.u32 a, %1, 56; add.u64 b, %3, 6;\n @e tcgen05.mma.cta_group::1.kind::f16 [%0], [a], b, %5, t;\n"
+        "}\n" ::"r"(d), "r"(ta), "l"(db0), "l"(db1), "r"(acc), "r"(kIdesc));
 }
-// 16 TMEM lanes x 8 columns from a warp: r0 (lane g, column t), r1 (g + 8, t), r2 (g, t + 4), r3 (g + 8, t + 4),
-// g = lane / 4, t = lane % 4.
 __device__ __forceinline__ void tmem_st_16x128b_x2(uint32_t taddr, uint32_t r0, uint32_t r1, uint32_t r2,
                                                    uint32_t r3) {
     asm volatile("tcgen05.st.sync.aligned.16x128b.x2.b32 [%0], {%1, %2, %3, %4};" ::"r"(taddr), "r"(r0), "r"(r1),
@@ -137,10 +141,14 @@ __device__ __forceinline__ void tma_tile_g2s_el(void* dst, const CUtensorMap* ma
 }
 
 // ------------------------------------------------------------------------------------------ units
-// Unit u -> (expert, row group, block pair). Units of expert e: ceil(rows_e / 64) * n_pairs.
+// Unit u -> (expert, row group, block pair). Units of expert e: ceil(rows_e / 64) * n_pairs. The record also holds
+// what every role derives from the expert (its class, its entry in the class's tables, whether the pair exists for
+// that class's width), computed once when the CTA builds its unit table, so no role divides in its loop.
 struct TcUnit {
-    int64_t e, r0;
-    int nr, pair;
+    int64_t r0;        // first sorted row
+    int32_t e, j;      // expert, entry in its class's tables
+    int16_t nr, pair;  // rows (<= 64), output block pair
+    int16_t c, live;   // class; 0: the pair lies past the class's width (its rows are zero there)
 };
 
 __device__ __forceinline__ TcUnit tc_unit(const Exl3bOp& op, const uint32_t* prefix, int64_t unit, int n_pairs) {
@@ -150,15 +158,27 @@ __device__ __forceinline__ TcUnit tc_unit(const Exl3bOp& op, const uint32_t* pre
         if ((int64_t)prefix[mid] <= unit) lo = mid; else hi = mid;
     }
     TcUnit u;
-    u.e = lo;
+    u.e = (int32_t)lo;
     const int64_t local = unit - prefix[lo];
     const int64_t grp = local / n_pairs;
-    u.pair = (int)(local % n_pairs);
+    u.pair = (int16_t)(local % n_pairs);
     u.r0 = op.expert_offset[lo] + grp * kNT;
     const int64_t rend = op.expert_offset[lo + 1];
-    u.nr = (int)(rend - u.r0 < kNT ? rend - u.r0 : kNT);
+    u.nr = (int16_t)(rend - u.r0 < kNT ? rend - u.r0 : kNT);
+    const ExpertView ev = expert_view(op, lo);
+    u.c = (int16_t)ev.c;
+    u.j = (int32_t)ev.j;
+    u.live = (int64_t)u.pair * 256 < ev.R ? 1 : 0;   // gate_up: 128 gate + 128 up rows a pair; down: 256 rows
     return u;
 }
+
+// A ring position: stage and phase advanced together (no division a chunk).
+struct Ring {
+    uint32_t s = 0, ph = 0;
+    __device__ __forceinline__ void next(uint32_t n) {
+        if (++s == n) { s = 0; ph ^= 1u; }
+    }
+};
 
 // ------------------------------------------------------------------------------------------ the kernel
 template <int BITS, int CB, bool GU>
@@ -178,7 +198,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     uint64_t* b_full = a_empty + kStA;       // producer tx -> MMA
     uint64_t* b_empty = b_full + kStB;       // MMA commit -> producer
     uint64_t* r_full = b_empty + kStB;       // producer tx -> decoders
-    uint64_t* r_empty = r_full + Cfg::ST_R;  // decoders -> producer (count kDecWarps)
+    uint64_t* r_empty = r_full + Cfg::ST_R;  // MMA warp (once every decoder has finished the stage) -> producer
     uint64_t* acc_full = r_empty + Cfg::ST_R;  // MMA commit -> epilogue [2]
     uint64_t* acc_empty = acc_full + 2;      // epilogue -> MMA [2] (count kEpiWarps)
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
@@ -193,7 +213,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     if (tid == 0) {
         for (int s = 0; s < kStA; ++s) { mbar_init(&a_full[s], kDecWarps); mbar_init(&a_empty[s], 1); }
         for (int s = 0; s < kStB; ++s) { mbar_init(&b_full[s], 1); mbar_init(&b_empty[s], 1); }
-        for (int s = 0; s < Cfg::ST_R; ++s) { mbar_init(&r_full[s], 1); mbar_init(&r_empty[s], kDecWarps); }
+        for (int s = 0; s < Cfg::ST_R; ++s) { mbar_init(&r_full[s], 1); mbar_init(&r_empty[s], 1); }
         for (int s = 0; s < 2; ++s) { mbar_init(&acc_full[s], 1); mbar_init(&acc_empty[s], kEpiWarps); }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -241,7 +261,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    const uint32_t tmem = *tmem_slot;
+    // the allocated base, read from shared memory and broadcast from lane 0: the compiler then knows it is the same in
+    // every lane, and the tensor-memory addresses and MMA operands derived from it stay warp-uniform
+    const uint32_t tmem = __shfl_sync(0xFFFFFFFFu, *tmem_slot, 0);
     auto unit_at = [&](int64_t i) -> TcUnit {
         return i < kUnitTab ? utab[i] : tc_unit(op, prefix, blockIdx.x + i * gridDim.x, n_pairs);
     };
@@ -264,86 +286,82 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         // ---------------------------------------------------------------- producers
         // warp 8 streams the record rows, warp 9 the input-row tiles: two rings, two warps, so neither producer's
         // wait holds up the other. Each warp runs its loop whole; one elected lane issues the copies.
-        uint32_t ri = 0, bi = 0;
+        Ring rr, br;
         for (int64_t ui_ = 0; ui_ < n_mine; ++ui_) {
             const TcUnit u = unit_at(ui_);
-            const ExpertView ev = expert_view(op, u.e);
-            const Exl3bClass& cl = op.cls[ev.c];
-            const int64_t wrows = GU ? ev.R / 2 : ev.R;          // rows of one record
-            if ((int64_t)u.pair * 256 >= (GU ? 2 * wrows : wrows)) continue;   // a narrower class
-            const int nck = (int)(ev.C / kKC);
+            if (!u.live) continue;                                   // a narrower class: nothing to stream
+            const Exl3bClass& cl = op.cls[u.c];
+            const int64_t wrows = GU ? cl.rows / 2 : cl.rows;       // rows of one record
+            const int nck = (int)(cl.cols / kKC);
             if (warp == kRecWarp) {
-                const uint16_t* rec = static_cast<const uint16_t*>(tab_entry(cl.codes, ev.j));
-                const int64_t mat_elems = (ev.C / 16) * (wrows / 16) * 16 * BITS;
-                for (int ck = 0; ck < nck; ++ck, ++ri) {
-                    const uint32_t s = ri % Cfg::ST_R, ph = (ri / Cfg::ST_R) & 1;
-                    mbar_wait_warp(&r_empty[s], ph ^ 1, op.err);
-                    mbar_expect_tx_el(&r_full[s], (uint32_t)Cfg::REC_STAGE);
+                const uint16_t* rec = static_cast<const uint16_t*>(tab_entry(cl.codes, u.j));
+                const int64_t mat_elems = (cl.cols / 16) * (wrows / 16) * 16 * BITS;
+                // the unit's first tile of k row 0 (per matrix); k row tk adds tk * the record's k-row stride
+                const uint16_t* src0 = rec + (int64_t)u.pair * (GU ? 8 : 16) * 16 * BITS;
+                const int64_t krow = (wrows / 16) * 16 * BITS;
+                for (int ck = 0; ck < nck; ++ck, rr.next(Cfg::ST_R)) {
+                    mbar_wait_warp(&r_empty[rr.s], rr.ph ^ 1, op.err);
+                    mbar_expect_tx_el(&r_full[rr.s], (uint32_t)Cfg::REC_STAGE);
+                    uint8_t* dst0 = r_ring + rr.s * Cfg::REC_STAGE;
+                    const uint16_t* srck = src0 + (int64_t)ck * kKT * krow;
 #pragma unroll
                     for (int q = 0; q < kKT; ++q) {
-                        const int64_t tk = (int64_t)ck * kKT + q;
-                        uint8_t* dst = r_ring + s * Cfg::REC_STAGE + q * 2 * Cfg::REC_ROW;
+                        uint8_t* dst = dst0 + q * 2 * Cfg::REC_ROW;
                         if (GU) {
-#pragma unroll
-                            for (int m = 0; m < 2; ++m) {
-                                const uint16_t* src = rec + m * mat_elems + (tk * (wrows / 16) + u.pair * 8) * 16 * BITS;
-                                tma_bulk_g2s_el(dst + m * Cfg::REC_ROW, src, Cfg::REC_ROW, &r_full[s]);
-                            }
+                            tma_bulk_g2s_el(dst, srck + q * krow, Cfg::REC_ROW, &r_full[rr.s]);
+                            tma_bulk_g2s_el(dst + Cfg::REC_ROW, srck + mat_elems + q * krow, Cfg::REC_ROW,
+                                            &r_full[rr.s]);
                         } else {
-                            const uint16_t* src = rec + (tk * (wrows / 16) + u.pair * 16) * 16 * BITS;
-                            tma_bulk_g2s_el(dst, src, 2 * Cfg::REC_ROW, &r_full[s]);
+                            tma_bulk_g2s_el(dst, srck + q * krow, 2 * Cfg::REC_ROW, &r_full[rr.s]);
                         }
                     }
                 }
             } else {
                 // input rows of each chunk (sorted rows r0 .. r0+63; zero fill past T)
-                for (int ck = 0; ck < nck; ++ck, ++bi) {
-                    const uint32_t s = bi % kStB, ph = (bi / kStB) & 1;
-                    mbar_wait_warp(&b_empty[s], ph ^ 1, op.err);
-                    mbar_expect_tx_el(&b_full[s], (uint32_t)((GU ? 2 : 1) * kBHalf));
+                for (int ck = 0; ck < nck; ++ck, br.next(kStB)) {
+                    mbar_wait_warp(&b_empty[br.s], br.ph ^ 1, op.err);
+                    mbar_expect_tx_el(&b_full[br.s], (uint32_t)((GU ? 2 : 1) * kBHalf));
 #pragma unroll
                     for (int m = 0; m < (GU ? 2 : 1); ++m)
 #pragma unroll
                         for (int bx = 0; bx < kNBox; ++bx)
-                            tma_tile_g2s_el(b_ring + (s * 2 + m) * kBHalf + bx * kBTile, &tmap,
-                                            (int)(m * ev.C + ck * kKC + bx * kBox), (int)u.r0, &b_full[s]);
+                            tma_tile_g2s_el(b_ring + (br.s * 2 + m) * kBHalf + bx * kBTile, &tmap,
+                                            (int)(m * cl.cols + ck * kKC + bx * kBox), (int)u.r0, &b_full[br.s]);
                 }
             }
         }
     } else if (warp == kMmaWarp) {
         // ---------------------------------------------------------------- MMA issuer (whole warp, elected lane)
         // the input ring's base descriptor; a stage, half and k step only add to the start-address field (the
-        // shared-memory window is below 256 KB, so the 14-bit field never carries)
+        // shared-memory window is below 256 KB, so the 14-bit field never carries). Once every decoder has filled a
+        // chunk's A stage it has also finished reading the chunk's record stage, so this warp hands that stage back
+        // to the record producer (one arrive a chunk, instead of one a decoder warp).
         const uint64_t b_desc0 = sw128_desc(smem_u32(b_ring));
-        uint32_t ai = 0, bi = 0, ui = 0;
+        Ring ar, br, rr;
+        uint32_t ui = 0;
         for (int64_t ui_ = 0; ui_ < n_mine; ++ui_) {
             const TcUnit u = unit_at(ui_);
-            const ExpertView ev = expert_view(op, u.e);
-            const int64_t wrows = GU ? ev.R / 2 : ev.R;
-            if ((int64_t)u.pair * 256 >= (GU ? 2 * wrows : wrows)) continue;
+            if (!u.live) continue;
+            const int nck = (int)(op.cls[u.c].cols / kKC);
             const uint32_t buf = ui & 1, uph = (ui >> 1) & 1;
             mbar_wait_warp(&acc_empty[buf], uph ^ 1, op.err);
             tc_fence_after();
-            const int nck = (int)(ev.C / kKC);
             const uint32_t d = tmem + buf * (2 * kNT);
-            for (int ck = 0; ck < nck; ++ck) {
-                const uint32_t sa = ai % kStA, pa = (ai / kStA) & 1;
-                const uint32_t sb = bi % kStB, pb = (bi / kStB) & 1;
-                mbar_wait2_warp(&a_full[sa], pa, &b_full[sb], pb, op.err);
+            for (int ck = 0; ck < nck; ++ck, ar.next(kStA), br.next(kStB), rr.next(Cfg::ST_R)) {
+                mbar_wait2_warp(&a_full[ar.s], ar.ph, &b_full[br.s], br.ph, op.err);
                 tc_fence_after();
-                const uint32_t ta = tmem + kAccCols + sa * kAStageCols;
-                const uint64_t db = b_desc0 + (uint64_t)((sb * 2 * kBHalf) >> 4);
+                if (lane == 0) mbar_arrive(&r_empty[rr.s]);
+                __syncwarp();
+                const uint32_t ta = tmem + kAccCols + ar.s * kAStageCols;
+                const uint64_t db = b_desc0 + (uint64_t)((br.s * 2 * kBHalf) >> 4);
 #pragma unroll
-                for (int blk = 0; blk < 2; ++blk)
-#pragma unroll
-                    for (int ks = 0; ks < kKT; ++ks)
-                        umma_f16_ts_el(d + blk * kNT, ta + blk * (kKC / 2) + ks * 8,
-                                       db + (uint64_t)(((GU ? blk : 0) * kBHalf + (ks / 4) * kBTile + (ks % 4) * 32) >> 4),
-                                       (ck | ks) ? 1u : 0u);
-                umma_commit_el(&a_empty[sa]);
-                umma_commit_el(&b_empty[sb]);
-                ++ai;
-                ++bi;
+                for (int blk = 0; blk < 2; ++blk) {
+                    const uint64_t dbb = db + (uint64_t)(((GU ? blk : 0) * kBHalf) >> 4);
+                    umma_block8_el(d + blk * kNT, ta + blk * (kKC / 2), dbb, dbb + (uint64_t)(kBTile >> 4),
+                                   ck ? 1u : 0u);
+                }
+                umma_commit_el(&a_empty[ar.s]);
+                umma_commit_el(&b_empty[br.s]);
             }
             umma_commit_el(&acc_full[buf]);
             ++ui;
@@ -357,20 +375,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const LaneDec<BITS> ld = lane_dec<BITS>(lane);
         const uint32_t tile_off = (uint32_t)(blk * Cfg::REC_ROW + tn * Cfg::TILE_BYTES);
         const uint32_t a_t0 = tmem + ((uint32_t)(16 * tn) << 16) + kAccCols + blk * (kKC / 2);
-        uint32_t ai = 0, ri = 0;
+        Ring ar, rr;
         for (int64_t ui_ = 0; ui_ < n_mine; ++ui_) {
             const TcUnit u = unit_at(ui_);
-            const ExpertView ev = expert_view(op, u.e);
-            const int64_t wrows = GU ? ev.R / 2 : ev.R;
-            if ((int64_t)u.pair * 256 >= (GU ? 2 * wrows : wrows)) continue;
-            const int nck = (int)(ev.C / kKC);
-            for (int ck = 0; ck < nck; ++ck) {
-                const uint32_t sr = ri % Cfg::ST_R, pr = (ri / Cfg::ST_R) & 1;
-                const uint32_t sa = ai % kStA, pa = (ai / kStA) & 1;
-                mbar_wait2_warp(&r_full[sr], pr, &a_empty[sa], pa ^ 1, op.err);
+            if (!u.live) continue;
+            const int nck = (int)(op.cls[u.c].cols / kKC);
+            for (int ck = 0; ck < nck; ++ck, ar.next(kStA), rr.next(Cfg::ST_R)) {
+                mbar_wait2_warp(&r_full[rr.s], rr.ph, &a_empty[ar.s], ar.ph ^ 1, op.err);
                 tc_fence_after();
-                const uint8_t* rst = r_ring + sr * Cfg::REC_STAGE + tile_off;
-                const uint32_t ta = a_t0 + sa * kAStageCols;
+                const uint8_t* rst = r_ring + rr.s * Cfg::REC_STAGE + tile_off;
+                const uint32_t ta = a_t0 + ar.s * kAStageCols;
 #pragma unroll
                 for (int tt = 0; tt < kDecTn; ++tt)
 #pragma unroll
@@ -382,12 +396,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 tmem_wait_st();
                 tc_fence_before();
                 __syncwarp();
-                if (lane == 0) {
-                    mbar_arrive(&a_full[sa]);
-                    mbar_arrive(&r_empty[sr]);
-                }
-                ++ai;
-                ++ri;
+                if (lane == 0) mbar_arrive(&a_full[ar.s]);
             }
         }
     } else {
@@ -397,10 +406,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         uint32_t ui = 0;
         for (int64_t ui_ = 0; ui_ < n_mine; ++ui_) {
             const TcUnit u = unit_at(ui_);
-            const ExpertView ev = expert_view(op, u.e);
-            const Exl3bClass& cl = op.cls[ev.c];
-            const int64_t wrows = GU ? ev.R / 2 : ev.R;
-            if ((int64_t)u.pair * 256 >= (GU ? 2 * wrows : wrows)) {
+            const Exl3bClass& cl = op.cls[u.c];
+            if (!u.live) {
                 // a narrower class: its live rows are zero across this pair's columns
                 const int64_t c0 = (int64_t)u.pair * (GU ? 128 : 256), nc = GU ? 128 : 256;
                 for (int m = 0; m < u.nr; ++m) {
@@ -412,16 +419,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 continue;
             }
             // the unit's output scales, held for all its rows: lane l owns columns 4l .. 4l+3 of each block
-            const uint16_t* svh = static_cast<const uint16_t*>(tab_entry(cl.svh, ev.j));
+            const uint16_t* svh = static_cast<const uint16_t*>(tab_entry(cl.svh, u.j));
             float s0[4], s1[4], sd[4];
             const int64_t n0 = (int64_t)u.pair * (GU ? 128 : 256) + 4 * lane;
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
                 s0[e] = h2f(svh[n0 + e]);
-                s1[e] = GU ? h2f(svh[ev.R / 2 + n0 + e]) : h2f(svh[n0 + 128 + e]);
+                s1[e] = GU ? h2f(svh[cl.rows / 2 + n0 + e]) : h2f(svh[n0 + 128 + e]);
                 sd[e] = 0.f;
             }
-            const uint16_t* dn = GU && op.h_rot ? static_cast<const uint16_t*>(tab_entry(cl.dn_suh, ev.j)) : nullptr;
+            const uint16_t* dn = GU && op.h_rot ? static_cast<const uint16_t*>(tab_entry(cl.dn_suh, u.j)) : nullptr;
             uint16_t dsuh[4] = { 0, 0, 0, 0 };
             if (dn) {
 #pragma unroll
@@ -562,7 +569,7 @@ int64_t exl3b_tc_smem_bytes(int bits) {
     const int64_t rec_stage = (int64_t)kKT * 2 * 8 * 32 * bits;
     int64_t st_r = 64 * 1024 / rec_stage;
     st_r = st_r < 3 ? 3 : st_r > 12 ? 12 : st_r;
-    const int64_t st_b = kKC == 64 ? 6 : (bits >= 6 ? 3 : 4);
+    const int64_t st_b = bits >= 6 ? 3 : 4;
     const int64_t b = st_b * 2 * kBHalf + st_r * rec_stage + 2 * 16 * kEpiCols * 4 + 512;
     return 1024 + b;   // the alignment slack; the unit prefix follows (added by the caller)
 }

@@ -59,19 +59,53 @@ class MoeLayer:
         T, R = max_tokens, self.max_rows
         self.x = torch.empty((T, H), dtype=torch.float16, device=dev)
         self.logits = torch.empty((T, n_expert), dtype=torch.float32, device=dev)
-        self.ids = torch.empty((T, top_k), dtype=torch.int32, device=dev)
-        self.w = torch.empty((T, top_k), dtype=torch.float32, device=dev)
-        self.sorted_tok = torch.empty(R, dtype=torch.int32, device=dev)
-        self.offset = torch.empty(self.n_local + 1, dtype=torch.int32, device=dev)
-        self.scatter_work = torch.empty(max(16, self.native.scatter_work_bytes(R, self.n_local)), dtype=torch.uint8,
-                                        device=dev)
-        self.h = torch.empty((R, W), dtype=torch.float16, device=dev)
-        self.y_rows = torch.empty((R, H), dtype=torch.bfloat16, device=dev)
         self.out = torch.empty((T, H), dtype=torch.float32, device=dev)
-        self.gather_work = torch.empty(max(16, self.native.gather_work_bytes(T, top_k)), dtype=torch.uint8,
-                                       device=dev)
+        self.out_bf16 = torch.empty((T, H), dtype=torch.bfloat16, device=dev)
         self.rec_dtype = self._stored_dtype()
         self._args = {}
+        # a plain layer (a pass is at most max_tokens * top_k sorted rows) runs as ONE call of the library's C layer
+        # (exl3b200_moe_layer_forward) over one device block the library carves into every buffer; the routing and
+        # row buffers below are views of that block. A layer whose passes are capacity-sized (expert parallelism's
+        # local pass) keeps buffers of its own and drives the plugin rows itself.
+        self.c_layer = R == T * top_k
+        if self.c_layer:
+            from .native import LayerDesc
+            d = self.desc = LayerDesc()
+            d.n_expert, d.n_local, d.expert_base = n_expert, self.n_local, expert_base
+            d.hidden, d.width, d.top_k = H, W, top_k
+            d.bits_gu, d.bits_dn, d.codebook = bits_gu, bits_dn, {"3inst": 0, "mcg": 1, "mul1": 2}[codebook]
+            d.gu_codes, d.dn_codes = self.gu_tab.data_ptr(), self.dn_tab.data_ptr()
+            d.suh, d.suh1, d.svh_gu = self.suh.data_ptr(), self.suh1.data_ptr(), self.svh_gu.data_ptr()
+            d.dn_suh, d.svh_dn = self.dn_suh.data_ptr(), self.svh_dn.data_ptr()
+            nbytes = self.native.layer_work_bytes(d, T)
+            self.work = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+            b = self.bufs = self.native.layer_carve(d, T, self.work.data_ptr(), nbytes)
+            base = self.work.data_ptr()
+
+            def view(ptr, n, dt, shape):
+                off = ptr - base
+                nb = n * torch.tensor([], dtype=dt).element_size()
+                return self.work[off:off + nb].view(dt).view(shape)
+
+            self.ids = view(b.ids, T * top_k, torch.int32, (T, top_k))
+            self.w = view(b.w, T * top_k, torch.float32, (T, top_k))
+            self.sorted_tok = view(b.sorted_tok, R, torch.int32, (R,))
+            self.offset = view(b.expert_offset, self.n_local + 1, torch.int32, (self.n_local + 1,))
+            self.h = view(b.h, R * W, torch.float16, (R, W))
+            self.y_rows = view(b.y_rows, R * H, torch.bfloat16, (R, H))
+            self.scatter_work = view(b.scatter_work, 16, torch.uint8, (16,))
+            self.gather_work = view(b.gather_work, 16, torch.uint8, (16,))
+        else:
+            self.ids = torch.empty((T, top_k), dtype=torch.int32, device=dev)
+            self.w = torch.empty((T, top_k), dtype=torch.float32, device=dev)
+            self.sorted_tok = torch.empty(R, dtype=torch.int32, device=dev)
+            self.offset = torch.empty(self.n_local + 1, dtype=torch.int32, device=dev)
+            self.scatter_work = torch.empty(max(16, self.native.scatter_work_bytes(R, self.n_local)),
+                                            dtype=torch.uint8, device=dev)
+            self.h = torch.empty((R, W), dtype=torch.float16, device=dev)
+            self.y_rows = torch.empty((R, H), dtype=torch.bfloat16, device=dev)
+            self.gather_work = torch.empty(max(16, self.native.gather_work_bytes(T, top_k)), dtype=torch.uint8,
+                                           device=dev)
 
     def load_experts(self, src, base):
         """Copy experts [base, base + n_local) of `src` (a layer of the same shapes holding more experts) into this
@@ -79,6 +113,45 @@ class MoeLayer:
         sl = slice(base, base + self.n_local)
         for name in ("gu_rec", "dn_rec", "suh", "suh1", "svh_gu", "dn_suh", "svh_dn"):
             getattr(self, name).copy_(getattr(src, name)[sl])
+
+    # ------------------------------------------------------------------ weight sets (a stack of layers)
+    WEIGHTS = ("gu_rec", "dn_rec", "suh", "suh1", "svh_gu", "dn_suh", "svh_dn", "gu_tab", "dn_tab")
+
+    def add_weight_set(self, seed):
+        """Another layer's weights for this layer's experts (seeded as the constructor seeds them), kept resident
+        beside the others; returns its index. A stack of layers shares one set of activation buffers and swaps
+        weights with use_weight_set."""
+        torch, dev, E, H, W = self.torch, self.dev, self.n_local, self.H, self.W
+        if not hasattr(self, "_sets"):
+            self._sets = [{n: getattr(self, n) for n in self.WEIGHTS}]
+            self._retired = []
+        g = torch.Generator(device=dev)
+        g.manual_seed(seed)
+        rnd = lambda nb: torch.randint(-32768, 32768, (E, nb // 2), generator=g, device=dev,  # noqa: E731
+                                       dtype=torch.int32).to(torch.int16)
+        sign = lambda *sh: (torch.randint(0, 2, sh, generator=g, device=dev) * 2 - 1).to(torch.float16)  # noqa: E731
+        svh = lambda *sh: (sign(*sh).float() * torch.randn(sh, generator=g, device=dev).abs() * 0.02  # noqa: E731
+                           ).to(torch.float16)
+        st = {"gu_rec": rnd(self.gu_bytes), "dn_rec": rnd(self.dn_bytes), "suh": sign(E, 1, H), "suh1": sign(E, 1, H),
+              "svh_gu": svh(E, 2 * W, 1), "dn_suh": sign(E, 1, W), "svh_dn": svh(E, H, 1)}
+        st["gu_tab"] = torch.tensor([st["gu_rec"][e].data_ptr() for e in range(E)], dtype=torch.int64, device=dev)
+        st["dn_tab"] = torch.tensor([st["dn_rec"][e].data_ptr() for e in range(E)], dtype=torch.int64, device=dev)
+        self._sets.append(st)
+        return len(self._sets) - 1
+
+    def use_weight_set(self, i):
+        """Point the layer (its C description and its per-op launch arguments) at weight set i. Launch arguments
+        built for the previous set are kept alive with their scratch, so a CUDA graph captured over several sets
+        still owns every buffer its kernels use."""
+        for n, t in self._sets[i].items():
+            setattr(self, n, t)
+        if self.c_layer:
+            d = self.desc
+            d.gu_codes, d.dn_codes = self.gu_tab.data_ptr(), self.dn_tab.data_ptr()
+            d.suh, d.suh1, d.svh_gu = self.suh.data_ptr(), self.suh1.data_ptr(), self.svh_gu.data_ptr()
+            d.dn_suh, d.svh_dn = self.dn_suh.data_ptr(), self.svh_dn.data_ptr()
+        self._retired.append(self._args)
+        self._args = {}
 
     # ------------------------------------------------------------------ the stored codes dtype
     def _stored_dtype(self):
@@ -149,13 +222,20 @@ class MoeLayer:
                 absent, absent, absent,
                 rad.tensor(self.y_rows.data_ptr(), rad.DT["bf16"], [rows, H])]
         a_gu, a_dn = args(pg, gu_t), args(pd, dn_t)
-        # the scratch each row's hook asks for (the tensor-core band's rotated input rows), allocated once per shape
+        # the scratch each row's hook asks for (the tensor-core band's rotated input rows): one buffer a row, grown to
+        # the largest pass seen and shared by every pass size and weight set (the passes run one after another on
+        # one stream); a buffer that is outgrown stays alive for the graphs that captured it
+        if not hasattr(self, "_scratch"):
+            self._scratch, self._old_scratch = {}, []
         for row_name, a in (("moe_exl3_gate_up", a_gu), ("moe_exl3_down", a_dn)):
             row = self.plugin.row(row_name)
             need = int(row.scratch(C.byref(a))) if row.scratch else 0
             if need > 0:
-                buf = self.torch.empty(need, dtype=self.torch.uint8, device=self.dev)
-                keep.append(buf)
+                buf = self._scratch.get(row_name)
+                if buf is None or buf.numel() < need:
+                    if buf is not None:
+                        self._old_scratch.append(buf)
+                    buf = self._scratch[row_name] = self.torch.empty(need, dtype=self.torch.uint8, device=self.dev)
                 a.scratch, a.scratch_bytes = buf.data_ptr(), need
         res = (a_gu, a_dn, keep)
         self._args[key] = res
@@ -271,16 +351,26 @@ class MoeLayer:
 
     def forward(self, T, stream, events=None, x=None, logits=None, out=None):
         """The whole layer over the first T tokens of self.x / self.logits into self.out (f32 [T, H]); `x`,
-        `logits`, `out` (tensors of the same shapes) replace them, e.g. for double-buffered inputs."""
+        `logits`, `out` (tensors of the same shapes) replace them, e.g. for double-buffered inputs. An `out` of
+        dtype bfloat16 receives the layer's output in bf16 (the engine's hidden-state type). A plain layer is one
+        call of the library's C layer; `events` (three CUDA events around gate_up and down) take the per-op path."""
         nat, rows = self.native, T * self.k
+        o = out if out is not None else self.out
+        if self.c_layer and not events:
+            xx = x if x is not None else self.x
+            lg = logits if logits is not None else self.logits
+            nat.layer_forward(self.desc, self.bufs, xx.data_ptr(), lg.data_ptr(), T, o.data_ptr(),
+                              3 if o.dtype == self.torch.bfloat16 else 1, stream)
+            return
         xp = x.data_ptr() if x is not None else None
         lp = (logits if logits is not None else self.logits).data_ptr()
-        op_ = (out if out is not None else self.out).data_ptr()
+        op_ = o.data_ptr()
         nat.router_scatter(lp, T, self.E, self.k, self.ids.data_ptr(), self.w.data_ptr(), self.n_local, self.base,
                            self.sorted_tok.data_ptr(), self.offset.data_ptr(), self.scatter_work.data_ptr(), stream)
         self.experts(T, rows, stream, x_ptr=xp, events=events)
-        nat.moe_gather(self.y_rows.data_ptr(), self.H, self.sorted_tok.data_ptr(), rows, self.w.data_ptr(), T, self.k,
-                       self.H, op_, self.gather_work.data_ptr(), stream)
+        gather = nat.moe_gather_bf16 if o.dtype == self.torch.bfloat16 else nat.moe_gather
+        gather(self.y_rows.data_ptr(), self.H, self.sorted_tok.data_ptr(), rows, self.w.data_ptr(), T, self.k, self.H,
+               op_, self.gather_work.data_ptr(), stream)
 
     # ------------------------------------------------------------------ accounting
     def time_prep_step(self, T, n=5):
@@ -308,9 +398,10 @@ class Linears:
     streams every call's weights from HBM rather than L2. Weights as the layer's: uniform random record words, suh
     +-1, svh +-|N(0,1)| * 0.02."""
 
-    def __init__(self, plugin, rows, cols, bits, batch, n, codebook="mul1", seed=0, device="cuda"):
+    def __init__(self, plugin, rows, cols, bits, batch, n, codebook="mul1", seed=0, device="cuda", out_f16=False):
         import torch
         self.torch, self.plugin = torch, plugin
+        self.out_f16 = out_f16
         self.rows, self.cols, self.bits, self.B, self.n, self.codebook = rows, cols, bits, batch, n, codebook
         dev = self.dev = torch.device(device)
         g = torch.Generator(device=dev)
@@ -324,10 +415,11 @@ class Linears:
         self.svh = (s2 * torch.randn((n, rows, 1), generator=g, device=dev).abs() * 0.02).to(torch.float16)
         self.tab = torch.tensor([[self.rec[i].data_ptr()] for i in range(n)], dtype=torch.int64, device=dev)
         self.x = torch.randn((batch, cols), generator=g, device=dev).to(torch.float16)
-        self.y = torch.empty((batch, rows), dtype=torch.bfloat16, device=dev)
+        self.y = torch.empty((batch, rows), dtype=torch.float16 if out_f16 else torch.bfloat16, device=dev)
         self.sorted_tok = torch.arange(batch, dtype=torch.int32, device=dev)
         self.offset = torch.tensor([0, batch], dtype=torch.int32, device=dev)
         self.row = plugin.row("moe_exl3_down")
+        self.native = Native(plugin.path) if out_f16 else None
         params = {"M": batch, "N": rows, "K": cols, "n_expert": 1, "top_k": 1, "dtype": f"exl3k{bits}",
                   "codebook": codebook, "h_rot": 0}
         P, nP, kp = rad.make_params(params)
@@ -350,7 +442,7 @@ class Linears:
                   rad.tensor(self.sorted_tok.data_ptr(), rad.DT["i32"], [batch]),
                   rad.tensor(self.offset.data_ptr(), rad.DT["i32"], [2]),
                   absent, absent, absent,
-                  rad.tensor(self.y.data_ptr(), rad.DT["bf16"], [batch, rows])]
+                  rad.tensor(self.y.data_ptr(), rad.DT["f16" if out_f16 else "bf16"], [batch, rows])]
             arr = (rad.RadTensor * len(ts))(*ts)
             a = rad.RadArgs()
             a.t, a.n_t, a.p, a.n_p, a.world_size = arr, len(ts), P, nP, 1
@@ -363,7 +455,10 @@ class Linears:
             self.args.append(a)
 
     def run(self, i, stream):
-        rc = self.row.launch(C.byref(self.args[i]), stream)
+        if self.out_f16:
+            rc = self.native.moe_down_f16(C.addressof(self.args[i]), stream)
+        else:
+            rc = self.row.launch(C.byref(self.args[i]), stream)
         if rc != 0:
             raise RuntimeError(f"moe_exl3_down launch: {rc}")
 
@@ -373,6 +468,103 @@ class Linears:
 
     def flops_per_call(self):
         return 2 * self.B * self.rows * self.cols
+
+
+class ExpertMlps:
+    """`n` independent copies of one expert MLP (config 2: gate [W, H] and up [W, H] at K bits, down [H, W]), each
+    served by one call of the moe_exl3_gate_up_down row (n_expert 1, top_k 1, every input row routed to the expert;
+    gate_up(h_rot 1) -> down(h_rot 1) inside the op, h in the row's scratch) over `batch` input rows. Weights as the
+    layer's. The copies let a timed loop stream every call's weights from HBM rather than L2; one scratch serves all
+    copies (the calls run one after another on one stream)."""
+
+    def __init__(self, plugin, hidden, width, bits, batch, n, codebook="mul1", seed=0, device="cuda"):
+        import torch
+        self.torch, self.plugin = torch, plugin
+        self.H, self.W, self.bits, self.B, self.n = hidden, width, bits, batch, n
+        dev = self.dev = torch.device(device)
+        g = torch.Generator(device=dev)
+        g.manual_seed(seed)
+        H, W = hidden, width
+        self.gu_bytes, self.dn_bytes = 2 * W * H * bits // 8, H * W * bits // 8
+        rnd = lambda nb: torch.randint(-32768, 32768, (n, nb // 2), generator=g, device=dev,  # noqa: E731
+                                       dtype=torch.int32).to(torch.int16)
+        self.gu_rec, self.dn_rec = rnd(self.gu_bytes), rnd(self.dn_bytes)
+
+        def sign(*shape):
+            return (torch.randint(0, 2, shape, generator=g, device=dev) * 2 - 1).to(torch.float16)
+
+        def svh(*shape):
+            return (sign(*shape).float() * torch.randn(shape, generator=g, device=dev).abs() * 0.02).to(torch.float16)
+
+        self.suh, self.suh1, self.svh_gu = sign(n, 1, H), sign(n, 1, H), svh(n, 2 * W, 1)
+        self.dn_suh, self.svh_dn = sign(n, 1, W), svh(n, H, 1)
+        self.gu_tab = torch.tensor([[self.gu_rec[i].data_ptr()] for i in range(n)], dtype=torch.int64, device=dev)
+        self.dn_tab = torch.tensor([[self.dn_rec[i].data_ptr()] for i in range(n)], dtype=torch.int64, device=dev)
+        self.x = torch.randn((batch, H), generator=g, device=dev).to(torch.float16)
+        self.y = torch.empty((batch, H), dtype=torch.bfloat16, device=dev)
+        self.sorted_tok = torch.arange(batch, dtype=torch.int32, device=dev)
+        self.offset = torch.tensor([0, batch], dtype=torch.int32, device=dev)
+        self.row = plugin.row("moe_exl3_gate_up_down")
+        params = {"M": batch, "N": 2 * W, "K": H, "n_expert": 1, "top_k": 1, "dtype": f"exl3k{bits}",
+                  "codebook": codebook}
+        P, nP, kp = rad.make_params(params)
+        enc = X.encoding(bits, codebook, stacked=True)
+        sel = C.c_int(0)
+        L = rad.RadLayout()
+        pt = rad.tensor(0, rad.DT_UK[bits], [2 * W, H])
+        if self.row.layout(P, nP, 1, C.byref(enc), C.byref(sel), C.byref(pt), 1, C.byref(L)) != 0:
+            raise RuntimeError("layout hook refused the gate_up codes")
+        rec_dtype = int(L.dtype)
+        schema = {s_["op"]: s_ for s_ in plugin.schemas()}["moe_exl3_gate_up_down"]
+        self._keep, self.args, scratch = [kp], [], None
+        for i in range(n):
+            P, nP, kp = rad.make_params(params)
+            ts = []
+            for name, role, optional in schema["operands"]:
+                if name == "a":
+                    ts.append(rad.tensor(self.x.data_ptr(), rad.DT["f16"], [batch, H]))
+                elif name == "codes":
+                    ts.append(rad.tensor(self.gu_tab[i].data_ptr(), rec_dtype, [1, 2 * W, H], [0, H, 1]))
+                elif name == "dn_codes":
+                    ts.append(rad.tensor(self.dn_tab[i].data_ptr(), rec_dtype, [1, H, W], [0, W, 1]))
+                elif name in ("suh", "suh1", "dn_suh"):
+                    t = {"suh": self.suh, "suh1": self.suh1, "dn_suh": self.dn_suh}[name][i]
+                    ts.append(rad.tensor(t.data_ptr(), rad.DT["f16"], [1] + list(t.shape)))
+                elif name == "svh":
+                    ts.append(rad.tensor(self.svh_gu[i].data_ptr(), rad.DT["f16"], [1, 2 * W, 1]))
+                elif name == "dn_svh":
+                    ts.append(rad.tensor(self.svh_dn[i].data_ptr(), rad.DT["f16"], [1, H, 1]))
+                elif name == "sorted_tok":
+                    ts.append(rad.tensor(self.sorted_tok.data_ptr(), rad.DT["i32"], [batch]))
+                elif name == "expert_offset":
+                    ts.append(rad.tensor(self.offset.data_ptr(), rad.DT["i32"], [2]))
+                elif name == "y":
+                    ts.append(rad.tensor(self.y.data_ptr(), rad.DT["bf16"], [batch, H]))
+                else:
+                    ts.append(rad.RadTensor())
+            arr = (rad.RadTensor * len(ts))(*ts)
+            a = rad.RadArgs()
+            a.t, a.n_t, a.p, a.n_p, a.world_size = arr, len(ts), P, nP, 1
+            need = int(self.row.scratch(C.byref(a)))
+            if scratch is None or scratch.numel() < need:
+                scratch = torch.empty(max(256, need), dtype=torch.uint8, device=dev)
+                self._keep.append(scratch)
+            a.scratch, a.scratch_bytes = scratch.data_ptr(), need
+            self._keep.extend([P, kp, arr])
+            self.args.append(a)
+
+    def run(self, i, stream):
+        rc = self.row.launch(C.byref(self.args[i]), stream)
+        if rc != 0:
+            raise RuntimeError(f"moe_exl3_gate_up_down launch: {rc}")
+
+    def bytes_per_call(self):
+        """Algorithmic bytes of one call: both records plus suh, suh.1, svh (gate_up), dn_suh and svh (down)."""
+        H, W = self.H, self.W
+        return self.gu_bytes + self.dn_bytes + 2 * H * 2 + 2 * W * 2 + W * 2 + H * 2
+
+    def flops_per_call(self):
+        return 2 * self.B * 3 * self.H * self.W
 
 
 class ClassMoeLayer(MoeLayer):
@@ -387,6 +579,7 @@ class ClassMoeLayer(MoeLayer):
         if len(widths) not in (2, 4):
             raise ValueError("classes: 2 (by parity) or 4 (by number mod 4)")
         super().__init__(plugin, width=max(widths), **kw)
+        self.c_layer = False          # its experts are the class tables below, served through the class rows
         self.widths = list(widths)
         self.n_class = len(widths)
         E, H, dev = self.n_local, self.H, self.dev

@@ -9,6 +9,21 @@ from . import library_path
 _I64, _VP, _I = C.c_int64, C.c_void_p, C.c_int
 
 
+class LayerDesc(C.Structure):
+    """Exl3bLayerDesc (include/exl3b200.h)."""
+    _fields_ = [("n_expert", _I64), ("n_local", _I64), ("expert_base", _I64), ("hidden", _I64), ("width", _I64),
+                ("top_k", _I64), ("bits_gu", C.c_int32), ("bits_dn", C.c_int32), ("codebook", C.c_int32),
+                ("pad0", C.c_int32), ("gu_codes", _VP), ("dn_codes", _VP), ("suh", _VP), ("suh1", _VP),
+                ("svh_gu", _VP), ("dn_suh", _VP), ("svh_dn", _VP)]
+
+
+class LayerBufs(C.Structure):
+    """Exl3bLayerBufs (include/exl3b200.h): device addresses inside the caller's work block."""
+    _fields_ = [("max_tokens", _I64), ("ids", _VP), ("w", _VP), ("sorted_tok", _VP), ("expert_offset", _VP),
+                ("scatter_work", _VP), ("h", _VP), ("y_rows", _VP), ("gu_scratch", _VP), ("gu_scratch_bytes", _I64),
+                ("dn_scratch", _VP), ("dn_scratch_bytes", _I64), ("gather_work", _VP)]
+
+
 class Native:
     def __init__(self, path=None):
         L = self.lib = C.CDLL(str(path or library_path()))
@@ -47,6 +62,12 @@ class Native:
         L.exl3b200_p2p_signal_combine.argtypes = [_VP, _VP, _I64, _I64, _VP, _VP]
         L.exl3b200_moe_down_rows.argtypes = [_VP, _VP, _VP]
         L.exl3b200_moe_down_f16.argtypes = [_VP, _VP]
+        L.exl3b200_moe_gather_bf16.argtypes = [_VP, _I64, _VP, _I64, _VP, _I64, _I64, _I64, _VP, _VP, _VP]
+        L.exl3b200_moe_layer_work_bytes.restype = _I64
+        L.exl3b200_moe_layer_work_bytes.argtypes = [C.POINTER(LayerDesc), _I64]
+        L.exl3b200_moe_layer_carve.argtypes = [C.POINTER(LayerDesc), _I64, _VP, _I64, C.POINTER(LayerBufs)]
+        L.exl3b200_moe_layer_forward.argtypes = [C.POINTER(LayerDesc), C.POINTER(LayerBufs), _VP, _VP, _I64, _VP,
+                                                 C.c_int, _VP]
         L.exl3b200_set_peer_wait_ns.argtypes = [_I64]
         L.exl3b200_p2p_begin.argtypes = [_VP, _VP]
         L.exl3b200_moe_op_live.argtypes = [_VP, _I, _VP, _VP]
@@ -189,6 +210,27 @@ class Native:
 
     def moe_down_rows(self, args_ref, row_dst, stream=0):
         self._check(self.lib.exl3b200_moe_down_rows(args_ref, row_dst, stream), "exl3b200_moe_down_rows")
+
+    def moe_gather_bf16(self, rows, row_pitch, sorted_tok, n_rows, w, n_tok, top_k, width, y, work, stream=0):
+        self._check(self.lib.exl3b200_moe_gather_bf16(rows, row_pitch, sorted_tok, n_rows, w, n_tok, top_k, width, y,
+                                                      work, stream), "exl3b200_moe_gather_bf16")
+
+    def layer_work_bytes(self, desc, max_tokens):
+        n = int(self.lib.exl3b200_moe_layer_work_bytes(C.byref(desc), max_tokens))
+        if n < 0:
+            raise RuntimeError("exl3b200_moe_layer_work_bytes: the layer description was refused")
+        return n
+
+    def layer_carve(self, desc, max_tokens, work, work_bytes):
+        b = LayerBufs()
+        self._check(self.lib.exl3b200_moe_layer_carve(C.byref(desc), max_tokens, work, work_bytes, C.byref(b)),
+                    "exl3b200_moe_layer_carve")
+        return b
+
+    def layer_forward(self, desc, bufs, x, logits, n_tok, out, out_dtype, stream=0):
+        """out_dtype: 1 (RAD_F32) or 3 (RAD_BF16)."""
+        self._check(self.lib.exl3b200_moe_layer_forward(C.byref(desc), C.byref(bufs), x, logits, n_tok, out, out_dtype,
+                                                        stream), "exl3b200_moe_layer_forward")
 
     def moe_down_f16(self, args_ref, stream=0):
         """moe_exl3_down with f16 output rows (the row's RadArgs, y f16); returns the status."""
