@@ -558,11 +558,14 @@ def bench_ours(args, rank, world, local_rank):
     dom_ms = gu_kernel_ms if dom == "gate_up" else dn_ms
     dom_bytes = live * (gu_b if dom == "gate_up" else dn_b)
     achieved = dom_bytes / (dom_ms / 1e3) / 1e9
-    # DRAM traffic per launch of that kernel from the committed full capture of this workload
-    # (profiles/k_gemm_tc_config3_T2048.md: dram__bytes_read.sum + dram__bytes_write.sum), where it applies
+    # DRAM traffic per launch of that kernel (dram__bytes_read.sum + dram__bytes_write.sum), as one ncu capture of this
+    # workload recorded it in the repository's traffic table, where it applies
     traffic = None
-    if world == 1 and T == 2048 and "k_gemm_tc" in layer.band_name(dom, T):
-        traffic = {"gate_up": 592.7e6, "down": 355.7e6}[dom]
+    traffic_key = f"k_gemm_tc {dom} config3 T{T}"
+    tpath = REPO / "profiles" / "traffic.json"
+    if world == 1 and "k_gemm_tc" in layer.band_name(dom, T) and tpath.exists():
+        ent = json.loads(tpath.read_text()).get(traffic_key)
+        traffic = ent["dram_bytes_per_launch"] if ent else None
     launches_per_step = layer.launches_per_step(T)
 
     # ---- end to end: pinned host inputs in, the layer, the output back, every step. Double-buffered: step i's
@@ -769,7 +772,7 @@ def bench_ours(args, rank, world, local_rank):
                                      else "of fallback: 6650 GB/s (MEASURED_PEAKS.json absent)"),
                      "bytes_per_launch": int(dom_bytes), "ms_per_launch": round(dom_ms, 4),
                      "traffic": int(traffic) if traffic else None,
-                     "traffic_source": "profiles/k_gemm_tc_config3_T2048.md" if traffic else None,
+                     "traffic_source": f"ncu capture: {traffic_key}" if traffic else None,
                      "other": {"gate_up_op_ms": round(gu_ms, 4), "k_prep_ms": round(prep_ms, 4),
                                "down_op_ms": round(dn_ms, 4)}},
         "clocks": clk, "gpu_launches": int(launches_per_step * args.steps),

@@ -249,11 +249,14 @@ int     exl3b200_p2p_begin(uint32_t* epoch, void* stream);
  * [expert_offset[0], expert_offset[n_expert]) are left untouched instead of zeroed, so a caller may pass a
  * capacity-sized pass whose live count is known only on the device; down may write through row_dst. */
 int     exl3b200_moe_op_live(const RadArgs* args, int down, const uint64_t* row_dst, void* stream);
-/* moe_exl3_down with f16 output rows: the same operands (y f16 instead of bf16), checks, scratch hook and arithmetic
- * as the moe_exl3_down row, the f32 result times svh rounded once to f16. The single EXL3 linear of [M, K] f16 rows
- * to [M, N] f16 (n_expert 1, top_k 1, every row routed to the one expert). No counterpart in the reference, whose
- * down writes bf16 (kernels/exl3ref/ref.c:97-102). */
+/* moe_exl3_down with f16 output rows: the same operands (y f16 instead of bf16), checks and arithmetic as the
+ * moe_exl3_down row, the f32 result times svh rounded once to f16. The single EXL3 linear of [M, K] f16 rows to
+ * [M, N] f16 (n_expert 1, top_k 1, every row routed to the one expert). Its scratch (args->scratch) is sized by
+ * exl3b200_moe_down_f16_scratch: the down row's own hook refuses an f16 y. Without it the launch runs the decode
+ * band whatever the row count (the two bands agree within the ops' tolerance, not bit for bit). No counterpart in
+ * the reference, whose down writes bf16 (kernels/exl3ref/ref.c:97-102). */
 int     exl3b200_moe_down_f16(const RadArgs* args, void* stream);
+int64_t exl3b200_moe_down_f16_scratch(const RadArgs* args);
 /* moe_exl3_down (same RadArgs and checks as the row's launch) writing output row i at row_dst[i] (a device table
  * of row addresses, possibly in a peer's memory) instead of y + i * pitch. No counterpart in the reference. */
 int     exl3b200_moe_down_rows(const RadArgs* args, const uint64_t* row_dst, void* stream);

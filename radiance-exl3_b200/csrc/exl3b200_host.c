@@ -254,6 +254,15 @@ int exl3b200_moe_down_f16(const RadArgs* a, void* stream) {
     return run_op(&k, a->scratch, a->scratch_bytes, stream);
 }
 
+/* The scratch exl3b200_moe_down_f16 uses for these arguments (the rotated input rows of the tensor-core band), 0 when
+ * it needs none or the arguments are refused. The down row's own scratch hook refuses an f16 y. */
+int64_t exl3b200_moe_down_f16_scratch(const RadArgs* a) {
+    Exl3bGeom g;
+    Exl3bOp k;
+    if (!a || build_op_ex(a, EXL3B_DOWN, &g, &k, 1) != RAD_OK) return 0;
+    return tc_scratch_bytes(&k);
+}
+
 /* moe_exl3_gate_up (down = 0) or moe_exl3_down (down = 1) over the live rows only: rows outside the runs are left
  * untouched instead of zeroed, so a caller may pass a capacity-sized sorted_tok whose live count is known only on the
  * device (expert_offset[n_expert]). down may also write through a row-address table (row_dst, else NULL). */

@@ -203,11 +203,13 @@ class Case:
         return "bf16" if self.base in ("moe_exl3_down", "moe_exl3_gate_up_down") else "f16"
 
     # -------------------------------------------------------------- running
-    def run(self, plugin, device=False, domain=None, stream=0, scratch=True, out_dtype=None, launch=None):
+    def run(self, plugin, device=False, domain=None, stream=0, scratch=True, out_dtype=None, launch=None,
+            scratch_fn=None):
         """Launch this case on `plugin`'s row for the op. Returns dict(rc, y (uint16 bits [T, y_cols]) or None,
         redzone_ok, inputs_ok, unrelayout_ok, layouts). `out_dtype` ("f16" / "bf16") overrides the output operand's
         type and `launch(args_ptr, stream)` the row's launch: an entry point that takes the row's RadArgs with
-        another output type (exl3b200_moe_down_f16) runs through the same harness."""
+        another output type (exl3b200_moe_down_f16) runs through the same harness; `scratch_fn(args_ptr)` then sizes
+        its scratch in place of the row's hook."""
         schema = {s["op"]: s for s in plugin.schemas()}[self.op]
         row = plugin.row(self.op, domain)
         if row is None:
@@ -260,8 +262,8 @@ class Case:
         a.p = P
         a.n_p = nP
         a.world_size = 1
-        if scratch and row.scratch:
-            need = row.scratch(C.byref(a))
+        if scratch and (scratch_fn or row.scratch):
+            need = (scratch_fn or row.scratch)(C.byref(a))
             if need > 0:
                 a.scratch = mem.alloc(need, 0)
                 a.scratch_bytes = need

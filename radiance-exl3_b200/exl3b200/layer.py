@@ -446,7 +446,10 @@ class Linears:
             arr = (rad.RadTensor * len(ts))(*ts)
             a = rad.RadArgs()
             a.t, a.n_t, a.p, a.n_p, a.world_size = arr, len(ts), P, nP, 1
-            need = int(self.row.scratch(C.byref(a))) if self.row.scratch else 0
+            if out_f16:
+                need = self.native.moe_down_f16_scratch(C.addressof(a))
+            else:
+                need = int(self.row.scratch(C.byref(a))) if self.row.scratch else 0
             if need > 0:
                 buf = torch.empty(need, dtype=torch.uint8, device=dev)
                 self._keep.append(buf)

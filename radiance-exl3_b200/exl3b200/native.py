@@ -62,6 +62,8 @@ class Native:
         L.exl3b200_p2p_signal_combine.argtypes = [_VP, _VP, _I64, _I64, _VP, _VP]
         L.exl3b200_moe_down_rows.argtypes = [_VP, _VP, _VP]
         L.exl3b200_moe_down_f16.argtypes = [_VP, _VP]
+        L.exl3b200_moe_down_f16_scratch.restype = _I64
+        L.exl3b200_moe_down_f16_scratch.argtypes = [_VP]
         L.exl3b200_moe_gather_bf16.argtypes = [_VP, _I64, _VP, _I64, _VP, _I64, _I64, _I64, _VP, _VP, _VP]
         L.exl3b200_moe_layer_work_bytes.restype = _I64
         L.exl3b200_moe_layer_work_bytes.argtypes = [C.POINTER(LayerDesc), _I64]
@@ -235,6 +237,10 @@ class Native:
     def moe_down_f16(self, args_ref, stream=0):
         """moe_exl3_down with f16 output rows (the row's RadArgs, y f16); returns the status."""
         return int(self.lib.exl3b200_moe_down_f16(args_ref, stream))
+
+    def moe_down_f16_scratch(self, args_ref):
+        """Scratch bytes moe_down_f16 uses for these RadArgs (0: none, or refused)."""
+        return int(self.lib.exl3b200_moe_down_f16_scratch(args_ref))
 
     def set_peer_wait_ns(self, ns):
         self._check(self.lib.exl3b200_set_peer_wait_ns(ns), "exl3b200_set_peer_wait_ns")

@@ -433,14 +433,16 @@ F16_OUT = [
 @pytest.mark.parametrize("spec", F16_OUT, ids=lambda s: f"M{s['M']}-{s['geom'][0][0]}x{s['geom'][0][1]}-K{s['bits']}")
 def test_down_with_f16_output_matches_the_oracle(dev, plugin, orc, native, spec):
     case = _case(spec, seed=99)
-    got = case.run(plugin, device=True, out_dtype="f16", launch=lambda a, s: native.moe_down_f16(a, s))
+    got = case.run(plugin, device=True, out_dtype="f16", launch=lambda a, s: native.moe_down_f16(a, s),
+                   scratch_fn=lambda a: native.moe_down_f16_scratch(a))
     assert got["rc"] == 0, got["rc"]
     assert got["redzone_ok"] and got["inputs_ok"]
     want = orc._run(case, 0, case.h_rot, 0, case.x, case.geom, "own", os.cpu_count() or 4, out_f16=True)
     ok, detail = compare(got["y"], want, "f16", REL_TOL, COS_TOL)
     assert ok, detail
-    # the op's own bf16 rows from the same kernels: two roundings of one f32 value v (|bf16 - v| <= 2^-8 |v|,
-    # |f16 - v| <= 2^-11 |v| in the normal range), so they agree within one bf16 ulp of the value
+    # the op's own bf16 rows from the same kernels (the f16 entry's scratch sized by its own hook, so both launches
+    # take the same band): two roundings of one f32 value v (|bf16 - v| <= 2^-8 |v|, |f16 - v| <= 2^-11 |v| in the
+    # normal range), so they agree within one bf16 ulp of the value
     bf = case.run(plugin, device=True)["y"]
     a, b = X.bits_to_f32(got["y"], "f16").astype(np.float64), X.bits_to_f32(bf, "bf16").astype(np.float64)
     bad = np.abs(a - b) > np.maximum(np.abs(a), np.abs(b)) * 2.0 ** -7 + 2.0 ** -24
