@@ -181,6 +181,23 @@ __device__ __forceinline__ void had128_warp(float v[4], int lane) {
     for (int i = 0; i < 4; ++i) v[i] = __fmul_rn(v[i], kRs);
 }
 
+// SiLU(g) * u in f32 (kernels/exl3ref/ref.c:44, 209): g / (1 + e^-g) with the exponential and the reciprocal from the
+// special-function unit (ex2.approx, rcp.approx: a few ulp of f32, far inside the ops' stated tolerance). g very
+// negative: e^-g = inf and the quotient is -0, as the reference's g * (1 / (1 + inf)).
+__device__ __forceinline__ float silu_mul(float g, float u) {
+    return __fmul_rn(__fdividef(g, __fadd_rn(1.0f, __expf(-g))), u);
+}
+// down's input scale on gate_up's h (h_rot): v = f32(f16(f16(h) * s)) for four values, as the reference's
+// f16(f32(f16 h) * f32 s) -- the product of two f16 values is exact in f32, so one HMUL2 (exact product, one
+// round-to-nearest-even to f16) gives the same bits.
+__device__ __forceinline__ void hrot_scale4(float h[4], const uint16_t s[4]) {
+    const __half2 a = __floats2half2_rn(h[0], h[1]), b = __floats2half2_rn(h[2], h[3]);
+    const __half2 sa = __halves2half2(__ushort_as_half(s[0]), __ushort_as_half(s[1]));
+    const __half2 sb = __halves2half2(__ushort_as_half(s[2]), __ushort_as_half(s[3]));
+    const float2 ra = __half22float2(__hmul2(a, sa)), rb = __half22float2(__hmul2(b, sb));
+    h[0] = ra.x; h[1] = ra.y; h[2] = rb.x; h[3] = rb.y;
+}
+
 // f16(had(f16(x * s))) of one 128-block held as above (kernels/exl3ref/ref.c:27-32).
 __device__ __forceinline__ void prologue_warp(float v[4], const uint16_t* __restrict__ s, int lane) {
 #pragma unroll

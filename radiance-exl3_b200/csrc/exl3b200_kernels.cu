@@ -500,10 +500,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_skinny(const Exl3bOp op, i
                     float h[4];
 #pragma unroll
                     for (int q = 0; q < 4; ++q) {
-                        const float gte = __fmul_rn(v[0][q], h2f(svh[n0 + q]));
-                        const float up = __fmul_rn(v[MATS - 1][q], h2f(svh[W + n0 + q]));
-                        const float sg = __fmul_rn(gte, __frcp_rn(__fadd_rn(1.0f, expf(-gte))));
-                        h[q] = __fmul_rn(sg, up);
+                        h[q] = silu_mul(__fmul_rn(v[0][q], h2f(svh[n0 + q])), __fmul_rn(v[MATS - 1][q], h2f(svh[W + n0 + q])));
                     }
                     uint16_t* y = out_row(op, i) + n0;
                     if (op.h_rot) {

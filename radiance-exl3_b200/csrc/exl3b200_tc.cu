@@ -435,6 +435,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 for (int e = 0; e < 4; ++e) dsuh[e] = dn[(int64_t)u.pair * 128 + 4 * lane + e];
             }
             (void)sd;
+            // the sorted_tok entries of this warp's rows (m = 8 l + warp, one a lane of the first eight), loaded once a
+            // unit while the accumulators are still being computed
+            int32_t tokv = -1;
+            if (lane < kNT / kEpiWarps && kEpiWarps * lane + warp < u.nr) tokv = op.sorted_tok[u.r0 + kEpiWarps * lane + warp];
             const uint32_t buf = ui & 1, uph = (ui >> 1) & 1;
             mbar_wait_warp(&acc_full[buf], uph, op.err);
             tc_fence_after();
@@ -451,9 +455,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 // rows: warp w takes rows w and w + 8 of the slice
                 for (int j = warp; j < 16; j += kEpiWarps) {
                     const int m = sl * 16 + j;
-                    if (m >= u.nr) continue;
+                    const int32_t tok = __shfl_sync(0xFFFFFFFFu, tokv, m / kEpiWarps);
+                    if (m >= u.nr || tok < 0) continue;
                     const int64_t i = u.r0 + m;
-                    if (op.sorted_tok[i] < 0) continue;
                     const float4 av = *reinterpret_cast<const float4*>(&epi[(0 * 16 + j) * kEpiCols + 4 * lane]);
                     const float4 bv = *reinterpret_cast<const float4*>(&epi[(1 * 16 + j) * kEpiCols + 4 * lane]);
                     float a[4] = { av.x, av.y, av.z, av.w }, b[4] = { bv.x, bv.y, bv.z, bv.w };
@@ -463,15 +467,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     if (GU) {
                         float h[4];
 #pragma unroll
-                        for (int e = 0; e < 4; ++e) {
-                            const float gte = __fmul_rn(a[e], s0[e]);
-                            const float up = __fmul_rn(b[e], s1[e]);
-                            const float sg = __fmul_rn(gte, __frcp_rn(__fadd_rn(1.0f, expf(-gte))));
-                            h[e] = __fmul_rn(sg, up);
-                        }
+                        for (int e = 0; e < 4; ++e) h[e] = silu_mul(__fmul_rn(a[e], s0[e]), __fmul_rn(b[e], s1[e]));
                         if (dn) {
-#pragma unroll
-                            for (int e = 0; e < 4; ++e) h[e] = h2f(f2h(__fmul_rn(h2f(f2h(h[e])), h2f(dsuh[e]))));
+                            hrot_scale4(h, dsuh);
                             had128_warp(h, lane);
                         }
                         uint2 pk;
