@@ -107,13 +107,41 @@ __device__ __forceinline__ LaneDec<BITS> lane_dec(int lane) {
     return d;
 }
 
+// The stream words a lane's windows span (BITS = 4: words L-1, L; otherwise a-1, a, a+1 and, for BITS >= 5, a+2),
+// read from a generic pointer or -- the kernels' record rings -- straight from a shared-memory address.
+struct TileWords {
+    uint32_t w0, w1, w2, w3;
+};
+template <int BITS>
+__device__ __forceinline__ TileWords tile_words(const uint8_t* __restrict__ tile, const LaneDec<BITS>& d) {
+    TileWords w;
+    w.w0 = *reinterpret_cast<const uint32_t*>(tile + d.o0);
+    w.w1 = *reinterpret_cast<const uint32_t*>(tile + d.o1);
+    w.w2 = BITS == 4 ? 0u : *reinterpret_cast<const uint32_t*>(tile + d.o2);
+    w.w3 = BITS >= 5 ? *reinterpret_cast<const uint32_t*>(tile + d.o3) : 0u;
+    return w;
+}
+__device__ __forceinline__ uint32_t lds_u32(uint32_t a) {
+    uint32_t v;
+    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a));
+    return v;
+}
+template <int BITS>
+__device__ __forceinline__ TileWords tile_words_s(uint32_t tile, const LaneDec<BITS>& d) {
+    TileWords w;
+    w.w0 = lds_u32(tile + d.o0);
+    w.w1 = lds_u32(tile + d.o1);
+    w.w2 = BITS == 4 ? 0u : lds_u32(tile + d.o2);
+    w.w3 = BITS >= 5 ? lds_u32(tile + d.o3) : 0u;
+    return w;
+}
+
 template <int BITS, int CB>
-__device__ __forceinline__ void decode_tile(const uint8_t* __restrict__ tile, const LaneDec<BITS>& d, uint32_t b[4]) {
+__device__ __forceinline__ void decode_words(const TileWords& w, const LaneDec<BITS>& d, uint32_t b[4]) {
     uint32_t st[8];
     if constexpr (BITS == 4) {
         // window of position 8L+j at offset 20 + 4j of (word L-1 : word L)
-        const uint32_t hi = *reinterpret_cast<const uint32_t*>(tile + d.o0);
-        const uint32_t lo = *reinterpret_cast<const uint32_t*>(tile + d.o1);
+        const uint32_t hi = w.w0, lo = w.w1;
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
             // the windows that lie byte-aligned inside `lo` are one PRMT; the others a funnel shift and a mask
@@ -124,17 +152,14 @@ __device__ __forceinline__ void decode_tile(const uint8_t* __restrict__ tile, co
             else st[j] = __funnelshift_r(lo, hi, sh) & 0xFFFFu;
         }
     } else {
-        const uint32_t wm1 = *reinterpret_cast<const uint32_t*>(tile + d.o0);
-        const uint32_t wa = *reinterpret_cast<const uint32_t*>(tile + d.o1);
-        const uint32_t wb = *reinterpret_cast<const uint32_t*>(tile + d.o2);
+        const uint32_t wm1 = w.w0, wa = w.w1, wb = w.w2;
         const uint32_t h = __funnelshift_r(wa, wm1, d.sh16);         // stream bits [32a - sh16, +32)
         const uint32_t m = __funnelshift_r(wb, wa, d.sh16);          // the next 32
         if constexpr (BITS <= 4) {
 #pragma unroll
             for (int j = 0; j < 8; ++j) st[j] = __funnelshift_rc(m, h, 48 - d.offp - j * BITS) & 0xFFFFu;
         } else {
-            const uint32_t wc = *reinterpret_cast<const uint32_t*>(tile + d.o3);
-            const uint32_t l = __funnelshift_r(wc, wb, d.sh16);
+            const uint32_t l = __funnelshift_r(w.w3, wb, d.sh16);
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
                 const int q = d.offp + j * BITS;
@@ -148,6 +173,16 @@ __device__ __forceinline__ void decode_tile(const uint8_t* __restrict__ tile, co
     b[1] = cb_pair<CB>(st[2], st[3]);
     b[2] = cb_pair<CB>(st[4], st[5]);
     b[3] = cb_pair<CB>(st[6], st[7]);
+}
+
+template <int BITS, int CB>
+__device__ __forceinline__ void decode_tile(const uint8_t* __restrict__ tile, const LaneDec<BITS>& d, uint32_t b[4]) {
+    decode_words<BITS, CB>(tile_words<BITS>(tile, d), d, b);
+}
+// The same, the tile at a shared-memory address (explicit shared loads).
+template <int BITS, int CB>
+__device__ __forceinline__ void decode_tile_s(uint32_t tile, const LaneDec<BITS>& d, uint32_t b[4]) {
+    decode_words<BITS, CB>(tile_words_s<BITS>(tile, d), d, b);
 }
 
 // One lane's eight positions of the tile at `w` (the per-lane setup done in place).

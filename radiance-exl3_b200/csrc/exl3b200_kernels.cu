@@ -428,6 +428,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_skinny(const Exl3bOp op, i
 #pragma unroll
                         for (int q = 0; q < 4; ++q) acc[mt][mc][nb][q] = 0.f;
             const int arow = (lane & 7) + 8 * ((lane >> 3) & 1), acol = 8 * (lane >> 4);
+            const LaneDec<BITS> ldec = lane_dec<BITS>(lane);
             for (int sidx = 0; sidx < nstages; ++sidx, ++it) {
                 const uint32_t s = it % kNst, ph = (it / kNst) & 1;
                 mbar_wait_warp(&full[s], ph, op.err);
@@ -437,10 +438,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_skinny(const Exl3bOp op, i
                     const int tkl = tk_first + q;                       // k-tile index inside this CTA's range
 #pragma unroll
                     for (int mat = 0; mat < MATS; ++mat) {
-                        const uint32_t* words = reinterpret_cast<const uint32_t*>(
-                            ring + s * Cfg::STAGE_BYTES + (q * MATS + mat) * Cfg::COPY_BYTES) + warp * Cfg::TILE_WORDS;
+                        const uint32_t words = smem_u32(ring) + s * Cfg::STAGE_BYTES +
+                                               (q * MATS + mat) * Cfg::COPY_BYTES + warp * Cfg::TILE_WORDS * 4;
                         uint32_t b[4];
-                        decode_lane<BITS, CB>(words, lane, b);
+                        decode_tile_s<BITS, CB>(words, ldec, b);
 #pragma unroll
                         for (int mc = 0; mc < MCH; ++mc) {
                             uint32_t a[4];

@@ -105,8 +105,7 @@ __device__ __forceinline__ void umma_block8_el(uint32_t d, uint32_t ta, uint64_t
 __device__ __forceinline__ void tmem_st_16x128b_x2(uint32_t taddr, uint32_t r0, uint32_t r1, uint32_t r2,
                                                    uint32_t r3) {
     asm volatile("tcgen05.st.sync.aligned.16x128b.x2.b32 [%0], {%1, %2, %3, %4};" ::"r"(taddr), "r"(r0), "r"(r1),
-                 "r"(r2), "r"(r3)
-                 : "memory");
+                 "r"(r2), "r"(r3));
 }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void umma_commit_el(uint64_t* bar) {
@@ -186,8 +185,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     k_gemm_tc(const __grid_constant__ CUtensorMap tmap, const Exl3bOp op, int n_pairs) {
     using Cfg = TcCfg<BITS>;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
-    // 1024-byte alignment of every swizzled tile
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    // 1024-byte alignment of every swizzled tile, as an offset from the shared array (the pointers stay visibly in
+    // shared memory, so every access through them is a shared-memory instruction, not a generic one)
+    uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     constexpr int kStB = Cfg::ST_B;
     uint8_t* b_ring = smem;                                        // [kStB][half 2][box kNBox][8 KB]
     uint8_t* r_ring = b_ring + kStB * 2 * kBHalf;                  // [ST_R][REC_STAGE]
@@ -383,16 +383,22 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             for (int ck = 0; ck < nck; ++ck, ar.next(kStA), rr.next(Cfg::ST_R)) {
                 mbar_wait2_warp(&r_full[rr.s], rr.ph, &a_empty[ar.s], ar.ph ^ 1, op.err);
                 tc_fence_after();
-                const uint8_t* rst = r_ring + rr.s * Cfg::REC_STAGE + tile_off;
+                const uint32_t rst = smem_u32(r_ring) + rr.s * Cfg::REC_STAGE + tile_off;
                 const uint32_t ta = a_t0 + ar.s * kAStageCols;
 #pragma unroll
-                for (int tt = 0; tt < kDecTn; ++tt)
+                for (int tt = 0; tt < kDecTn; ++tt) {
+                    // every tile's stream words of the chunk first, so no tile waits on its shared-memory loads
+                    TileWords w[kKT];
+#pragma unroll
+                    for (int tk = 0; tk < kKT; ++tk)
+                        w[tk] = tile_words_s<BITS>(rst + tk * 2 * Cfg::REC_ROW + tt * Cfg::TILE_BYTES, ld);
 #pragma unroll
                     for (int tk = 0; tk < kKT; ++tk) {
                         uint32_t b[4];
-                        decode_tile<BITS, CB>(rst + tk * 2 * Cfg::REC_ROW + tt * Cfg::TILE_BYTES, ld, b);
+                        decode_words<BITS, CB>(w[tk], ld, b);
                         tmem_st_16x128b_x2(ta + ((uint32_t)(16 * tt) << 16) + tk * 8, b[0], b[2], b[1], b[3]);
                     }
+                }
                 tmem_wait_st();
                 tc_fence_before();
                 __syncwarp();
