@@ -576,13 +576,16 @@ def bench_ours(args, rank, world, local_rank):
         nb = 2
         hx = [torch.empty(layer.x[:T].shape, dtype=layer.x.dtype, pin_memory=True) for _ in range(nb)]
         hl = [torch.empty(layer.logits[:T].shape, dtype=layer.logits.dtype, pin_memory=True) for _ in range(nb)]
-        ho = [torch.empty(layer.out[:T].shape, dtype=layer.out.dtype, pin_memory=True) for _ in range(nb)]
+        # the layer's output in the engine's hidden-state type (bf16: the MoE block adds it to a bf16 stream); the
+        # width split sums f32 partials across ranks and returns f32
+        odt = torch.float32 if tp_mode else torch.bfloat16
+        ho = [torch.empty(layer.out[:T].shape, dtype=odt, pin_memory=True) for _ in range(nb)]
         for b in range(nb):
             hx[b].copy_(layer.x[:T].cpu())
             hl[b].copy_(layer.logits[:T].cpu())
         dx = [torch.empty_like(layer.x[:T]) for _ in range(nb)]
         dl = [torch.empty_like(layer.logits[:T]) for _ in range(nb)]
-        do = [torch.empty_like(layer.out[:T]) for _ in range(nb)]
+        do = [torch.empty(layer.out[:T].shape, dtype=odt, device=dev) for _ in range(nb)]
         s_in, s_out = torch.cuda.Stream(), torch.cuda.Stream()
         in_ready = [torch.cuda.Event() for _ in range(nb)]
         comp_done = [torch.cuda.Event() for _ in range(nb)]
@@ -626,10 +629,11 @@ def bench_ours(args, rank, world, local_rank):
             e_ms = float(t.item())
         e2e = {"value": tokens_total / (e_ms / 1e3), "unit": "tokens/s", "ms_per_step": e_ms,
                "h2d_bytes_per_step": int(hx[0].numel() * 2 + hl[0].numel() * 4),
-               "d2h_bytes_per_step": int(ho[0].numel() * 4),
+               "d2h_bytes_per_step": int(ho[0].numel() * ho[0].element_size()),
                "path": "pinned host x + logits -> router/scatter kernels -> plugin rows moe_exl3_gate_up, "
-                       "moe_exl3_down (RadArgs launch) -> gather kernel -> pinned host y; copies on two streams, "
-                       "double-buffered so each step's copies overlap the neighbouring steps' layers"}
+                       f"moe_exl3_down (RadArgs launch) -> gather kernel ({'f32' if tp_mode else 'bf16'} y) -> "
+                       "pinned host y; copies on two streams, double-buffered so each step's copies overlap the "
+                       "neighbouring steps' layers"}
 
     # ---- the batch sweep (1 GPU): each T captured in a CUDA graph. Below T = 2048 a step reads only its live
     # experts' weights (13 MB at T = 1, 99 MB at T = 8), which a repeated step would find in the 126 MB L2; so the

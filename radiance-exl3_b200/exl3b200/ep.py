@@ -92,8 +92,10 @@ class DeviceOps:
 
     def gather(self, rows, sorted_pairs, n_rows, w, T, k, out, rows_ptr=None):
         work = self._work(("gather", k), self.nat.gather_work_bytes(w.numel() // k, k), out.device)
-        self.nat.moe_gather(rows_ptr or rows.data_ptr(), out.shape[1], sorted_pairs.data_ptr(), n_rows,
-                            w.data_ptr(), T, k, out.shape[1], out.data_ptr(), work.data_ptr(), self._stream())
+        import torch
+        gather = self.nat.moe_gather_bf16 if out.dtype == torch.bfloat16 else self.nat.moe_gather
+        gather(rows_ptr or rows.data_ptr(), out.shape[1], sorted_pairs.data_ptr(), n_rows, w.data_ptr(), T, k,
+               out.shape[1], out.data_ptr(), work.data_ptr(), self._stream())
 
     def kernels(self, T, k, E, R):
         """How many of the library's kernels one step launches: router, ep_dest, rank scatter, the two pack
