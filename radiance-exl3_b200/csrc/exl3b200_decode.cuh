@@ -72,15 +72,24 @@ __device__ __forceinline__ uint32_t cb_pair(uint32_t s0, uint32_t s1) {
 // n = L/4 and L/4 + 8), so the four returned half2 are: b[0], b[1] the first n8 block's fragment registers,
 // b[2], b[3] the second's.
 //
-// The lane's windows all fall in a 64-bit (K <= 4) or 96-bit (K >= 5) span that starts on a 16-bit
-// boundary with its first window at offset 16..31; each state is then one clamped funnel shift.
-// What a lane needs to find its eight windows in any tile of a given K: the byte offsets of the three or four
-// stream words they span, the 16-bit realignment and the first window's offset. Computed once a kernel.
+// The lane's eight windows span 16 + 7K bits starting at S = (8L+1)K - 16 (circular): inside two stream words from
+// word S/32 for K <= 4, three for K >= 5. The words are realigned once (funnel shifts by S % 32) so the first window
+// starts at the top bit; every window is then at a compile-time position: one shift and a mask, a single shift or
+// PRMT where it lies at the top or on a byte boundary of one word. For K = 4 and K = 8 every lane's S % 32 is the
+// same (20, 24), so no realignment is needed at all.
+template <int BITS>
+struct KDec {
+    static constexpr int NWQ = BITS <= 4 ? 2 : 3;              // stream words a lane's windows span
+    static constexpr bool FIXED = BITS == 4 || BITS == 8;      // every lane's first window at the same bit offset
+    static constexpr int OFF = BITS == 4 ? 20 : BITS == 8 ? 24 : 0;
+};
+
+// What a lane needs to find its windows in any tile of a given K: the byte offsets of its two or three stream words
+// and the first window's bit offset in the first. Computed once a kernel.
 template <int BITS>
 struct LaneDec {
-    uint32_t o0, o1, o2, o3;   // byte offsets of words a-1, a, a+1, a+2 (circular in the tile)
-    uint32_t sh16;             // 0 or 16
-    int offp;                  // the first window's offset, 16..31
+    uint32_t o0, o1, o2;       // byte offsets of words a, a+1, a+2 (circular in the tile)
+    uint32_t off;              // the first window's start bit in word a
 };
 
 template <int BITS>
@@ -88,37 +97,26 @@ __device__ __forceinline__ LaneDec<BITS> lane_dec(int lane) {
     constexpr int NW = 8 * BITS;
     constexpr int NB = 256 * BITS;
     LaneDec<BITS> d;
-    if constexpr (BITS == 4) {
-        d.o0 = (uint32_t)(((lane + NW - 1) % NW) * 4);
-        d.o1 = (uint32_t)(lane * 4);
-        d.o2 = d.o3 = 0;
-        d.sh16 = 0;
-        d.offp = 20;
-    } else {
-        const int base = ((8 * lane + 1) * BITS - 16 + NB) % NB;   // first window's start bit
-        const int a = base >> 5, off = base & 31;
-        d.sh16 = off < 16 ? 16u : 0u;
-        d.offp = off + (int)d.sh16;
-        d.o0 = (uint32_t)(((a + NW - 1) % NW) * 4);
-        d.o1 = (uint32_t)(a * 4);
-        d.o2 = (uint32_t)(((a + 1) % NW) * 4);
-        d.o3 = (uint32_t)(((a + 2) % NW) * 4);
-    }
+    const int base = ((8 * lane + 1) * BITS - 16 + NB) % NB;   // first window's start bit
+    const int a = base >> 5;
+    d.off = (uint32_t)(base & 31);
+    d.o0 = (uint32_t)(a * 4);
+    d.o1 = (uint32_t)(((a + 1) % NW) * 4);
+    d.o2 = (uint32_t)(((a + 2) % NW) * 4);
     return d;
 }
 
-// The stream words a lane's windows span (BITS = 4: words L-1, L; otherwise a-1, a, a+1 and, for BITS >= 5, a+2),
-// read from a generic pointer or -- the kernels' record rings -- straight from a shared-memory address.
+// The stream words a lane's windows span, read from a generic pointer or -- the kernels' record rings -- straight
+// from a shared-memory address.
 struct TileWords {
-    uint32_t w0, w1, w2, w3;
+    uint32_t w0, w1, w2;
 };
 template <int BITS>
 __device__ __forceinline__ TileWords tile_words(const uint8_t* __restrict__ tile, const LaneDec<BITS>& d) {
     TileWords w;
     w.w0 = *reinterpret_cast<const uint32_t*>(tile + d.o0);
     w.w1 = *reinterpret_cast<const uint32_t*>(tile + d.o1);
-    w.w2 = BITS == 4 ? 0u : *reinterpret_cast<const uint32_t*>(tile + d.o2);
-    w.w3 = BITS >= 5 ? *reinterpret_cast<const uint32_t*>(tile + d.o3) : 0u;
+    w.w2 = KDec<BITS>::NWQ == 3 ? *reinterpret_cast<const uint32_t*>(tile + d.o2) : 0u;
     return w;
 }
 __device__ __forceinline__ uint32_t lds_u32(uint32_t a) {
@@ -131,44 +129,64 @@ __device__ __forceinline__ TileWords tile_words_s(uint32_t tile, const LaneDec<B
     TileWords w;
     w.w0 = lds_u32(tile + d.o0);
     w.w1 = lds_u32(tile + d.o1);
-    w.w2 = BITS == 4 ? 0u : lds_u32(tile + d.o2);
-    w.w3 = BITS >= 5 ? lds_u32(tile + d.o3) : 0u;
+    w.w2 = KDec<BITS>::NWQ == 3 ? lds_u32(tile + d.o2) : 0u;
     return w;
+}
+
+// Bits [S, S + 16) (counted from the least significant bit) of the 32*NWQ-bit value q2:q1:q0 (q2 the top word; q0
+// unused for NWQ = 2), as a clean 16-bit value. S is a compile-time constant.
+template <int S, int NWQ>
+__device__ __forceinline__ uint32_t win16(uint32_t q2, uint32_t q1, uint32_t q0) {
+    constexpr int TOP = 32 * NWQ;
+    // the word the window's low bit falls in, and the one above it
+    constexpr int LOWW = S / 32;                               // 0 = lowest word
+    constexpr int SH = S % 32;
+    const uint32_t lo = NWQ == 3 ? (LOWW == 2 ? q2 : LOWW == 1 ? q1 : q0) : (LOWW == 1 ? q2 : q1);
+    static_assert(S + 16 <= TOP, "window inside the span");
+    if constexpr (SH <= 16) {
+        // inside one word
+        if constexpr (SH == 16) return lo >> 16;
+        else if constexpr (SH == 8) return __byte_perm(lo, 0u, 0x4421);
+        else if constexpr (SH == 0) return __byte_perm(lo, 0u, 0x4410);
+        else return (lo >> SH) & 0xFFFFu;
+    } else {
+        const uint32_t hi = NWQ == 3 ? (LOWW == 1 ? q2 : q1) : q2;
+        return __funnelshift_r(lo, hi, SH) & 0xFFFFu;
+    }
+}
+
+// The eight states of a lane's windows: window j starts (from the top of the span) at off + jK.
+template <int BITS>
+__device__ __forceinline__ void lane_states(const TileWords& w, const LaneDec<BITS>& d, uint32_t st[8]) {
+    using K = KDec<BITS>;
+    uint32_t q2, q1, q0 = 0;
+    constexpr int SHIFT0 = 32 * K::NWQ - 16 - K::OFF;          // window 0's low bit, before realignment
+    if constexpr (K::FIXED) {
+        q2 = w.w0;
+        q1 = w.w1;
+        if constexpr (K::NWQ == 3) q0 = w.w2;
+    } else if constexpr (K::NWQ == 2) {
+        q2 = __funnelshift_l(w.w1, w.w0, d.off);               // the span's first bit at the top
+        q1 = w.w1 << d.off;
+    } else {
+        q2 = __funnelshift_l(w.w1, w.w0, d.off);
+        q1 = __funnelshift_l(w.w2, w.w1, d.off);
+        q0 = w.w2 << d.off;
+    }
+    st[0] = win16<SHIFT0 - 0 * BITS, K::NWQ>(q2, q1, q0);
+    st[1] = win16<SHIFT0 - 1 * BITS, K::NWQ>(q2, q1, q0);
+    st[2] = win16<SHIFT0 - 2 * BITS, K::NWQ>(q2, q1, q0);
+    st[3] = win16<SHIFT0 - 3 * BITS, K::NWQ>(q2, q1, q0);
+    st[4] = win16<SHIFT0 - 4 * BITS, K::NWQ>(q2, q1, q0);
+    st[5] = win16<SHIFT0 - 5 * BITS, K::NWQ>(q2, q1, q0);
+    st[6] = win16<SHIFT0 - 6 * BITS, K::NWQ>(q2, q1, q0);
+    st[7] = win16<SHIFT0 - 7 * BITS, K::NWQ>(q2, q1, q0);
 }
 
 template <int BITS, int CB>
 __device__ __forceinline__ void decode_words(const TileWords& w, const LaneDec<BITS>& d, uint32_t b[4]) {
     uint32_t st[8];
-    if constexpr (BITS == 4) {
-        // window of position 8L+j at offset 20 + 4j of (word L-1 : word L)
-        const uint32_t hi = w.w0, lo = w.w1;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            // the windows that lie byte-aligned inside `lo` are one PRMT; the others a funnel shift and a mask
-            const int sh = 28 - 4 * j;
-            if (sh == 16) st[j] = __byte_perm(lo, 0u, 0x4432);
-            else if (sh == 8) st[j] = __byte_perm(lo, 0u, 0x4421);
-            else if (sh == 0) st[j] = __byte_perm(lo, 0u, 0x4410);
-            else st[j] = __funnelshift_r(lo, hi, sh) & 0xFFFFu;
-        }
-    } else {
-        const uint32_t wm1 = w.w0, wa = w.w1, wb = w.w2;
-        const uint32_t h = __funnelshift_r(wa, wm1, d.sh16);         // stream bits [32a - sh16, +32)
-        const uint32_t m = __funnelshift_r(wb, wa, d.sh16);          // the next 32
-        if constexpr (BITS <= 4) {
-#pragma unroll
-            for (int j = 0; j < 8; ++j) st[j] = __funnelshift_rc(m, h, 48 - d.offp - j * BITS) & 0xFFFFu;
-        } else {
-            const uint32_t l = __funnelshift_r(w.w3, wb, d.sh16);
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                const int q = d.offp + j * BITS;
-                const uint32_t v0 = __funnelshift_rc(m, h, 48 - q);
-                const uint32_t v1 = __funnelshift_rc(l, m, 80 - q);
-                st[j] = (q <= 48 ? v0 : v1) & 0xFFFFu;
-            }
-        }
-    }
+    lane_states<BITS>(w, d, st);
     b[0] = cb_pair<CB>(st[0], st[1]);
     b[1] = cb_pair<CB>(st[2], st[3]);
     b[2] = cb_pair<CB>(st[4], st[5]);
