@@ -159,13 +159,18 @@ static int build_op(const RadArgs* a, int op, Exl3bGeom* g, Exl3bOp* k) { return
 /* The band choice. The tensor-core path decodes each expert's weights once for up to 64 of its rows and pays its
  * input-rotation pass (the prep kernel into scratch) once per row; the decode-band path re-rotates per output block
  * and holds at most 64 rows in registers, but splits K over clusters so that a few live experts still spread over
- * the GPU. The tensor-core path is taken when the live experts average at least EXL3B_TC_MIN_ROWS rows, or when
- * they make at least EXL3B_TC_MIN_UNITS of its units (live experts x 256-row output pairs), provided every class's
- * output is a whole number of 256-row unit pairs and its input rows can be read by a 16-byte-aligned tensor map;
+ * the GPU. The tensor-core path is taken when the pass makes at least EXL3B_TC_MIN_UNITS of its units (64-row groups
+ * of each live expert's rows x 256-row output pairs, estimated as (live experts + rows / 64) x pairs), or when the live
+ * experts average at least EXL3B_TC_MIN_ROWS rows and make at least EXL3B_TC_FEW_UNITS units (fewer leave nearly every
+ * SM idle: a lone expert of 16 rows 2048 -> 512 is two units), provided every class's output is a whole number of
+ * 256-row unit pairs and its input rows can be read by a 16-byte-aligned tensor map;
  * otherwise the decode-band path serves the launch (the two agree within the ops' tolerance, not bit for bit:
  * their f32 accumulations run in different orders). */
 #ifndef EXL3B_TC_MIN_ROWS
 #define EXL3B_TC_MIN_ROWS 16
+#endif
+#ifndef EXL3B_TC_FEW_UNITS
+#define EXL3B_TC_FEW_UNITS 8
 #endif
 #ifndef EXL3B_TC_MIN_UNITS
 #define EXL3B_TC_MIN_UNITS 64
@@ -180,7 +185,8 @@ static int tc_band(const Exl3bOp* k) {
         if (k->op == EXL3B_OP_DOWN && k->cls[c].rows % 256) return 0;
         if (k->cls[c].rows / 256 > pairs) pairs = k->cls[c].rows / 256;
     }
-    if (k->T / live < EXL3B_TC_MIN_ROWS && live * pairs < EXL3B_TC_MIN_UNITS) return 0;
+    const int64_t units = (live + k->T / 64) * pairs;
+    if (units < EXL3B_TC_MIN_UNITS && (k->T / live < EXL3B_TC_MIN_ROWS || units < EXL3B_TC_FEW_UNITS)) return 0;
     if ((k->n_expert + 1) * 4 > 16384) return 0;
     /* the kernel's shared memory (rings by bitrate + the unit prefix) must fit a CTA */
     if (exl3b_tc_smem_bytes(k->bits) + ((k->n_expert + 1) * 4 + 15) / 16 * 16 + 16 + 4096 > 227 * 1024) return 0;

@@ -314,13 +314,14 @@ class MoeLayer:
         return e0.elapsed_time(e1) / n
 
     def _tc(self, op, rows):
-        """The library's band rule (exl3b200_host.c tc_band): the tensor-core band once the live experts average 16
-        rows or make 64 units (live experts x 256-row output pairs)."""
+        """The library's band rule (exl3b200_host.c tc_band): the tensor-core band once the pass makes 64 of its units
+        ((live experts + rows / 64) x 256-row output pairs), or 8 of them while the live experts average 16 rows."""
         live = min(self.n_local, rows)
         if live <= 0:
             return False
         pairs = (2 * self.W if op == "gate_up" else self.H) // 256
-        return rows // live >= 16 or live * pairs >= 64
+        units = (live + rows // 64) * pairs
+        return units >= 64 or (rows // live >= 16 and units >= 8)
 
     def band_name(self, op, T, rows=None):
         """Which kernels serve one op at T tokens, or over `rows` sorted rows (gate_up's input rotation runs once a

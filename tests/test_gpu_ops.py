@@ -106,7 +106,8 @@ OPS = [
     # the decode band at the config's shapes (fewer than 64 units: live experts x 256-row output pairs)
     dict(op="moe_exl3_gate_up", M=1, top_k=10, n_expert=64, geom=[(1024, 2048)], bits=3, codebook="mul1"),
     dict(op="moe_exl3_down", M=1, top_k=4, n_expert=64, geom=[(2048, 512)], bits=4, codebook="mul1", h_rot=1),
-    # the tensor-core band (live experts averaging >= 16 rows, or at least 64 units)
+    # the tensor-core band (at least 64 units: 64-row groups x 256-row output pairs; or 8 of them while the live experts
+    # average >= 16 rows)
     dict(op="moe_exl3_down", M=8, top_k=10, n_expert=64, geom=[(2048, 512)], bits=4, codebook="mul1",
          table_form="stacked"),
     dict(op="moe_exl3_gate_up", M=8, top_k=10, n_expert=64, geom=[(1024, 2048)], bits=3, codebook="mul1"),
@@ -114,8 +115,8 @@ OPS = [
     dict(op="moe_exl3_gate_up", M=64, top_k=2, n_expert=4, geom=[(512, 256), (256, 128)], bits=2, codebook="3inst",
          drop=0.1),
     dict(op="moe_exl3_gate_up", M=48, top_k=1, n_expert=2, geom=[(1024, 512)], bits=5, codebook="mcg", a_rot=1),
-    dict(op="moe_exl3_down", M=70, top_k=1, n_expert=1, geom=[(256, 128)], bits=8, codebook="mul1"),
-    dict(op="moe_exl3_gate_up", M=33, top_k=2, n_expert=2, geom=[(256, 256)], bits=6, codebook="mul1", h_rot=1,
+    dict(op="moe_exl3_down", M=70, top_k=1, n_expert=1, geom=[(1024, 128)], bits=8, codebook="mul1"),
+    dict(op="moe_exl3_gate_up", M=33, top_k=2, n_expert=2, geom=[(1024, 256)], bits=6, codebook="mul1", h_rot=1,
          x_dtype="bf16"),
     dict(op="moe_exl3_gate_up", M=200, top_k=10, n_expert=64, geom=[(1024, 2048)], bits=3, codebook="mul1",
          h_rot=1),
@@ -419,8 +420,8 @@ def test_live_only_pass_leaves_padding_untouched(dev, plugin, T, pad):
 
 
 # ---------------------------------------------------------------------------------------------- the f16-output linear
-# config 1: a single EXL3 linear, 16 rows of 2048 -> 512, f16 out (the decode band at a handful of rows, the tensor-core
-# band from 16 rows an expert); the oracle's down with its output rounded to f16 instead of bf16
+# config 1: a single EXL3 linear, 16 rows of 2048 -> 512, f16 out (the decode band: two units; the tensor-core band for
+# the 64-row 1536 -> 4096 case); the oracle's down with its output rounded to f16 instead of bf16
 F16_OUT = [
     dict(op="moe_exl3_down", M=16, top_k=1, n_expert=1, geom=[(512, 2048)], bits=4, codebook="mul1"),     # config 1
     dict(op="moe_exl3_down", M=3, top_k=1, n_expert=1, geom=[(512, 2048)], bits=4, codebook="mul1"),
