@@ -162,8 +162,9 @@ __global__ void __launch_bounds__(kPrepWarps * 32) k_prep(const Exl3bOp op, uint
     uint16_t* y = nullptr;
     int32_t tok = -1;
     bool svec = false;
-    for (uint32_t task = t_begin; task < t_end; ++task) {
-        const uint32_t rr = task / (uint32_t)ngrp;
+    // the task's row and its group within the row, advanced with the task (no division a task)
+    uint32_t rr = t_begin / (uint32_t)ngrp, gi = t_begin - rr * (uint32_t)ngrp;
+    for (uint32_t task = t_begin; task < t_end; ++task, (++gi == (uint32_t)ngrp ? (gi = 0, ++rr) : 0)) {
         const int64_t i = lo + rr;
         if (i != row) {
             row = i;
@@ -181,7 +182,7 @@ __global__ void __launch_bounds__(kPrepWarps * 32) k_prep(const Exl3bOp op, uint
             s1 = gu ? static_cast<const uint16_t*>(tab_entry(op.cls[ev.c].suh1, ev.j)) : s0;
             svec = al16(s0) && al16(s1);
         }
-        const int64_t blk = (int64_t)(task - rr * (uint32_t)ngrp) * 4 + bq;
+        const int64_t blk = (int64_t)gi * 4 + bq;
         const bool mine = blk * 128 < ev.C;            // lanes past the class's width idle (shuffles stay whole)
         const int64_t c = (mine ? blk : 0) * 128 + 16 * l8;
         if (tok < 0) {
@@ -484,13 +485,21 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_skinny(const Exl3bOp op, i
                 for (int mat = 0; mat < MATS; ++mat) {
                     const float* src = red + m * Cfg::RED_COLS + mat * 128 + 4 * lane;
                     float4 sum = *reinterpret_cast<const float4*>(src);
-                    for (int r = 1; r < S; ++r) {
-                        const float4 p = ld_dsmem_f4(src, (uint32_t)r);
-                        sum.x = __fadd_rn(sum.x, p.x);
-                        sum.y = __fadd_rn(sum.y, p.y);
-                        sum.z = __fadd_rn(sum.z, p.z);
-                        sum.w = __fadd_rn(sum.w, p.w);
-                    }
+                    // every rank's partial in flight at once (the plan splits K at most 8 ways), then summed in
+                    // rank order
+                    float4 part[7];
+#pragma unroll
+                    for (int r = 1; r < 8; ++r)
+                        if (r < S) part[r - 1] = ld_dsmem_f4(src, (uint32_t)r);
+#pragma unroll
+                    for (int r = 1; r < 8; ++r)
+                        if (r < S) {
+                            const float4 p = part[r - 1];
+                            sum.x = __fadd_rn(sum.x, p.x);
+                            sum.y = __fadd_rn(sum.y, p.y);
+                            sum.z = __fadd_rn(sum.z, p.z);
+                            sum.w = __fadd_rn(sum.w, p.w);
+                        }
                     v[mat][0] = sum.x; v[mat][1] = sum.y; v[mat][2] = sum.z; v[mat][3] = sum.w;
                     had128_warp(v[mat], lane);
                 }

@@ -9,10 +9,10 @@
 //   warp 8       record producer: cp.async.bulk (TMA) of the unit's record rows into a deep ring
 //   warp 9       input producer: cp.async.bulk.tensor of the input rows (xr / h, sorted order) through a
 //                128-byte-swizzled tensor map
-//   warp 10      TMEM allocator and MMA issuer: tcgen05.mma.cta_group::1.kind::f16, M=128 (weight rows), N=64
-//                (sorted rows), K=16; A (the decoded weights) from TENSOR memory, B from shared memory, D in tensor
-//                memory; tcgen05.commit frees stages
-//   warps 11..26 decoders: each lane decodes 8 trellis positions of a tile (the same bit-exact decode as the
+//   warps 10, 11 MMA issuers (warp 10 also allocates TMEM): tcgen05.mma.cta_group::1.kind::f16, M=128 (weight rows),
+//                N=64 (sorted rows), K=16, one warp a block; A (the decoded weights) from TENSOR memory, B from
+//                shared memory, D in tensor memory; tcgen05.commit frees stages
+//   warps 12..27 decoders: each lane decodes 8 trellis positions of a tile (the same bit-exact decode as the
 //                decode-band kernel) -- exactly the 16x128b.x2 tcgen05.st fragment of a 16-row x 16-k A tile
 //                (lane g: rows g, g+8; 32-bit columns t, t+4 = k pairs 2t, 2t+8) -- and stores it into tensor
 //                memory; a decoder warp writes only its own TMEM lane quadrant (warp % 4)
@@ -35,15 +35,15 @@ namespace {
 constexpr int kEpiWarps = 8;                         // two a TMEM lane quadrant (warp % 4)
 constexpr int kRecWarp = 8;
 constexpr int kBWarp = 9;
-constexpr int kMmaWarp = 10;
-constexpr int kDecWarp0 = 11;
+constexpr int kMmaWarp = 10;                         // block 0's MMAs (and the TMEM allocation); 11: block 1's
+constexpr int kDecWarp0 = 12;
 #ifndef EXL3B_TC_DEC_TN
 #define EXL3B_TC_DEC_TN 1
 #endif
 constexpr int kDecTn = EXL3B_TC_DEC_TN;              // 16-row tile rows a decoder warp takes (1 or 2)
 constexpr int kDecWarps = 16 / kDecTn;               // 16 / kDecTn: 4 / kDecTn a lane quadrant
-constexpr int kTcWarps = kDecWarp0 + kDecWarps;      // 27
-constexpr int kTcThreads = kTcWarps * 32;           // 864
+constexpr int kTcWarps = kDecWarp0 + kDecWarps;      // 28
+constexpr int kTcThreads = kTcWarps * 32;           // 896
 constexpr int kNT = 64;                              // sorted rows a unit (the MMA's N)
 constexpr int kBox = 64;                             // k of one TMA box = one SWIZZLE_128B atom row (128 B)
 constexpr int kKC = 128;                             // k a pipeline chunk: one handoff between the roles
@@ -211,10 +211,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const int64_t n_exp = op.n_expert;
 
     if (tid == 0) {
-        for (int s = 0; s < kStA; ++s) { mbar_init(&a_full[s], kDecWarps); mbar_init(&a_empty[s], 1); }
-        for (int s = 0; s < kStB; ++s) { mbar_init(&b_full[s], 1); mbar_init(&b_empty[s], 1); }
+        // the stages and accumulators are released by both MMA warps' commits (two arrivals)
+        for (int s = 0; s < kStA; ++s) { mbar_init(&a_full[s], kDecWarps); mbar_init(&a_empty[s], 2); }
+        for (int s = 0; s < kStB; ++s) { mbar_init(&b_full[s], 1); mbar_init(&b_empty[s], 2); }
         for (int s = 0; s < Cfg::ST_R; ++s) { mbar_init(&r_full[s], 1); mbar_init(&r_empty[s], 1); }
-        for (int s = 0; s < 2; ++s) { mbar_init(&acc_full[s], 1); mbar_init(&acc_empty[s], kEpiWarps); }
+        for (int s = 0; s < 2; ++s) { mbar_init(&acc_full[s], 2); mbar_init(&acc_empty[s], kEpiWarps); }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (warp == kMmaWarp) {
@@ -330,12 +331,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 }
             }
         }
-    } else if (warp == kMmaWarp) {
-        // ---------------------------------------------------------------- MMA issuer (whole warp, elected lane)
-        // the input ring's base descriptor; a stage, half and k step only add to the start-address field (the
-        // shared-memory window is below 256 KB, so the 14-bit field never carries). Once every decoder has filled a
-        // chunk's A stage it has also finished reading the chunk's record stage, so this warp hands that stage back
-        // to the record producer (one arrive a chunk, instead of one a decoder warp).
+    } else if (warp == kMmaWarp || warp == kMmaWarp + 1) {
+        // ---------------------------------------------------------------- MMA issuers (whole warp, elected lane)
+        // warp 10 issues block 0's MMAs, warp 11 block 1's: the two blocks accumulate into their own TMEM columns, so
+        // each block's k steps stay in one warp's issue order, and the issue -- which holds a warp at the tensor
+        // cores' rate -- is spread over two SM sub-partitions. Each warp commits its own MMAs to the stage and
+        // accumulator barriers (two arrivals each). The input ring's base descriptor; a stage, half and k step only
+        // add to the start-address field (the shared-memory window is below 256 KB, so the 14-bit field never
+        // carries). Once every decoder has filled a chunk's A stage it has also finished reading the chunk's record
+        // stage, so warp 10 hands that stage back to the record producer (one arrive a chunk).
+        const int blk = warp - kMmaWarp;
         const uint64_t b_desc0 = sw128_desc(smem_u32(b_ring));
         Ring ar, br, rr;
         uint32_t ui = 0;
@@ -350,16 +355,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             for (int ck = 0; ck < nck; ++ck, ar.next(kStA), br.next(kStB), rr.next(Cfg::ST_R)) {
                 mbar_wait2_warp(&a_full[ar.s], ar.ph, &b_full[br.s], br.ph, op.err);
                 tc_fence_after();
-                if (lane == 0) mbar_arrive(&r_empty[rr.s]);
+                if (blk == 0 && lane == 0) mbar_arrive(&r_empty[rr.s]);
                 __syncwarp();
                 const uint32_t ta = tmem + kAccCols + ar.s * kAStageCols;
                 const uint64_t db = b_desc0 + (uint64_t)((br.s * 2 * kBHalf) >> 4);
-#pragma unroll
-                for (int blk = 0; blk < 2; ++blk) {
-                    const uint64_t dbb = db + (uint64_t)(((GU ? blk : 0) * kBHalf) >> 4);
-                    umma_block8_el(d + blk * kNT, ta + blk * (kKC / 2), dbb, dbb + (uint64_t)(kBTile >> 4),
-                                   ck ? 1u : 0u);
-                }
+                const uint64_t dbb = db + (uint64_t)(((GU ? blk : 0) * kBHalf) >> 4);
+                umma_block8_el(d + blk * kNT, ta + blk * (kKC / 2), dbb, dbb + (uint64_t)(kBTile >> 4), ck ? 1u : 0u);
                 umma_commit_el(&a_empty[ar.s]);
                 umma_commit_el(&b_empty[br.s]);
             }
