@@ -66,50 +66,60 @@ __global__ void k_decode_what(const uint32_t* __restrict__ record, int64_t rows,
 // negative is zero across 2C (docs/OPS-exl3.md:128-142). down (h_rot 0 on the tensor-core path): row i of h rotated
 // with suh into [0, C).
 //
-// A lane holds 16 consecutive values of its block (two 16-byte loads), so the butterfly stages h = 1, 2, 4, 8 run
-// in its registers and only h = 16, 32, 64 cross lanes (a shuffle within the block's 8 lanes). Every stage pairs
+// A lane holds 16 consecutive values of its block (two 16-byte loads), so the butterfly stages h = 1 .. 8 run
+// in its registers and only h = 16, 32, 64 cross lanes (a shuffle within the block's 8 lanes); 32 values a lane
+// (two cross-lane stages) was measured slower: 80 registers, fewer warps to cover the loads. Every stage pairs
 // the same elements with the same f32 operations as the reference's loop (common/exl3_decode.c:172-189), so xr is
 // bit for bit the reference's.
 constexpr int kPrepWarps = 8;
+constexpr int kPrepV = 16;                      // values a lane
+constexpr int kPrepLpb = 128 / kPrepV;          // lanes a 128-block
+constexpr int kPrepBpw = 32 / kPrepLpb;         // blocks a warp task
 
-__device__ __forceinline__ void had128_x16(float v[16], int l8) {
+template <int V>
+__device__ __forceinline__ void had128_xv(float v[V], int lb) {
 #pragma unroll
-    for (int h = 1; h < 16; h <<= 1)
+    for (int h = 1; h < V; h <<= 1)
 #pragma unroll
-        for (int i = 0; i < 16; ++i)
+        for (int i = 0; i < V; ++i)
             if (!(i & h)) {
                 const float a = v[i], b = v[i + h];
                 v[i] = __fadd_rn(a, b);
                 v[i + h] = __fsub_rn(a, b);
             }
 #pragma unroll
-    for (int m = 1; m < 8; m <<= 1) {
-        const float sg = (l8 & m) ? -1.0f : 1.0f;       // p + (+-1) v: exact product, one rounding
+    for (int m = 1; m < 128 / V; m <<= 1) {
+        const float sg = (lb & m) ? -1.0f : 1.0f;       // p + (+-1) v: exact product, one rounding
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
+        for (int i = 0; i < V; ++i) {
             const float p = __shfl_xor_sync(0xFFFFFFFFu, v[i], m);
             v[i] = __fmaf_rn(sg, v[i], p);
         }
     }
 #pragma unroll
-    for (int i = 0; i < 16; ++i) v[i] = __fmul_rn(v[i], kRs);
+    for (int i = 0; i < V; ++i) v[i] = __fmul_rn(v[i], kRs);
 }
 
-// 16 consecutive 16-bit values as 8 packed pairs (low half = the lower index)
-__device__ __forceinline__ void ld16(const uint16_t* p, bool vec, uint32_t u[8]) {
+// V consecutive 16-bit values as V/2 packed pairs (low half = the lower index)
+template <int V>
+__device__ __forceinline__ void ldv(const uint16_t* p, bool vec, uint32_t u[V / 2]) {
     if (vec) {
-        const uint4 a = *reinterpret_cast<const uint4*>(p), b = *reinterpret_cast<const uint4*>(p + 8);
-        u[0] = a.x; u[1] = a.y; u[2] = a.z; u[3] = a.w; u[4] = b.x; u[5] = b.y; u[6] = b.z; u[7] = b.w;
+#pragma unroll
+        for (int q = 0; q < V / 8; ++q) {
+            const uint4 a = *reinterpret_cast<const uint4*>(p + 8 * q);
+            u[4 * q] = a.x; u[4 * q + 1] = a.y; u[4 * q + 2] = a.z; u[4 * q + 3] = a.w;
+        }
     } else {
 #pragma unroll
-        for (int q = 0; q < 8; ++q) u[q] = (uint32_t)p[2 * q] | ((uint32_t)p[2 * q + 1] << 16);
+        for (int q = 0; q < V / 2; ++q) u[q] = (uint32_t)p[2 * q] | ((uint32_t)p[2 * q + 1] << 16);
     }
 }
-// v = f32(f16(x * s)) for 16 values: the product rounded once to f16, as the reference's f16(f32 x * f32 s) (the
+// v = f32(f16(x * s)) for V values: the product rounded once to f16, as the reference's f16(f32 x * f32 s) (the
 // product of two f16 values is exact in f32). f16 x: one HMUL2 a pair; bf16 x: in f32, then rounded.
-__device__ __forceinline__ void scale16(const uint32_t x[8], const uint32_t s[8], bool bf, float v[16]) {
+template <int V>
+__device__ __forceinline__ void scalev(const uint32_t x[V / 2], const uint32_t s[V / 2], bool bf, float v[V]) {
 #pragma unroll
-    for (int q = 0; q < 8; ++q) {
+    for (int q = 0; q < V / 2; ++q) {
         if (!bf) {
             const __half2 r = __hmul2(*reinterpret_cast<const __half2*>(&x[q]), *reinterpret_cast<const __half2*>(&s[q]));
             const float2 f = __half22float2(r);
@@ -121,20 +131,22 @@ __device__ __forceinline__ void scale16(const uint32_t x[8], const uint32_t s[8]
         }
     }
 }
-// 16 f32 values rounded to f16 and stored (8 packed pairs)
-__device__ __forceinline__ void st16f(uint16_t* p, bool vec, const float v[16]) {
-    uint32_t u[8];
+// V f32 values rounded to f16 and stored (V/2 packed pairs)
+template <int V>
+__device__ __forceinline__ void stvf(uint16_t* p, bool vec, const float v[V]) {
+    uint32_t u[V / 2];
 #pragma unroll
-    for (int q = 0; q < 8; ++q) {
+    for (int q = 0; q < V / 2; ++q) {
         const __half2 h = __floats2half2_rn(v[2 * q], v[2 * q + 1]);
         u[q] = *reinterpret_cast<const uint32_t*>(&h);
     }
     if (vec) {
-        *reinterpret_cast<uint4*>(p) = make_uint4(u[0], u[1], u[2], u[3]);
-        *reinterpret_cast<uint4*>(p + 8) = make_uint4(u[4], u[5], u[6], u[7]);
+#pragma unroll
+        for (int q = 0; q < V / 8; ++q)
+            *reinterpret_cast<uint4*>(p + 8 * q) = make_uint4(u[4 * q], u[4 * q + 1], u[4 * q + 2], u[4 * q + 3]);
     } else {
 #pragma unroll
-        for (int q = 0; q < 8; ++q) { p[2 * q] = (uint16_t)u[q]; p[2 * q + 1] = (uint16_t)(u[q] >> 16); }
+        for (int q = 0; q < V / 2; ++q) { p[2 * q] = (uint16_t)u[q]; p[2 * q + 1] = (uint16_t)(u[q] >> 16); }
     }
 }
 __device__ __forceinline__ bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
@@ -145,7 +157,7 @@ __global__ void __launch_bounds__(kPrepWarps * 32) k_prep(const Exl3bOp op, uint
     for (int64_t e = threadIdx.x; e <= op.n_expert; e += blockDim.x) s_off[e] = op.expert_offset[e];
     __syncthreads();
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-    const int l8 = lane & 7, bq = lane >> 3;           // the lane's 16 values: block 4g + bq, elements 16 l8 ..
+    const int lb = lane % kPrepLpb, bq = lane / kPrepLpb;   // the lane's V values: block Bpw g + bq, elements V lb ..
     const bool gu = op.op != EXL3B_OP_DOWN;
     const int64_t lo = s_off[0], hi = s_off[op.n_expert] < op.T ? s_off[op.n_expert] : op.T;
     const bool bf = gu && op.x_bf16;
@@ -182,32 +194,32 @@ __global__ void __launch_bounds__(kPrepWarps * 32) k_prep(const Exl3bOp op, uint
             s1 = gu ? static_cast<const uint16_t*>(tab_entry(op.cls[ev.c].suh1, ev.j)) : s0;
             svec = al16(s0) && al16(s1);
         }
-        const int64_t blk = (int64_t)gi * 4 + bq;
+        const int64_t blk = (int64_t)gi * kPrepBpw + bq;
         const bool mine = blk * 128 < ev.C;            // lanes past the class's width idle (shuffles stay whole)
-        const int64_t c = (mine ? blk : 0) * 128 + 16 * l8;
+        const int64_t c = (mine ? blk : 0) * 128 + kPrepV * lb;
         if (tok < 0) {
-            float z[16];
+            float z[kPrepV];
 #pragma unroll
-            for (int q = 0; q < 16; ++q) z[q] = 0.f;
+            for (int q = 0; q < kPrepV; ++q) z[q] = 0.f;
             if (mine) {
-                st16f(y + c, yvec, z);
-                if (gu) st16f(y + ev.C + c, yvec, z);
+                stvf<kPrepV>(y + c, yvec, z);
+                if (gu) stvf<kPrepV>(y + ev.C + c, yvec, z);
             }
             continue;
         }
-        // the two halves one after the other: 16 values live a lane, 4 CTAs an SM
-        uint32_t hx[8], hs[8];
-        float va[16];
-        ld16(src + c, xvec, hx);
-        ld16(s0 + c, svec, hs);
-        scale16(hx, hs, bf, va);
-        had128_x16(va, l8);
-        if (mine) st16f(y + c, yvec, va);
+        // the two halves one after the other
+        uint32_t hx[kPrepV / 2], hs[kPrepV / 2];
+        float va[kPrepV];
+        ldv<kPrepV>(src + c, xvec, hx);
+        ldv<kPrepV>(s0 + c, svec, hs);
+        scalev<kPrepV>(hx, hs, bf, va);
+        had128_xv<kPrepV>(va, lb);
+        if (mine) stvf<kPrepV>(y + c, yvec, va);
         if (gu) {
-            ld16(s1 + c, svec, hs);
-            scale16(hx, hs, bf, va);
-            had128_x16(va, l8);
-            if (mine) st16f(y + ev.C + c, yvec, va);
+            ldv<kPrepV>(s1 + c, svec, hs);
+            scalev<kPrepV>(hx, hs, bf, va);
+            had128_xv<kPrepV>(va, lb);
+            if (mine) stvf<kPrepV>(y + ev.C + c, yvec, va);
         }
     }
 }
@@ -485,21 +497,13 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm_skinny(const Exl3bOp op, i
                 for (int mat = 0; mat < MATS; ++mat) {
                     const float* src = red + m * Cfg::RED_COLS + mat * 128 + 4 * lane;
                     float4 sum = *reinterpret_cast<const float4*>(src);
-                    // every rank's partial in flight at once (the plan splits K at most 8 ways), then summed in
-                    // rank order
-                    float4 part[7];
-#pragma unroll
-                    for (int r = 1; r < 8; ++r)
-                        if (r < S) part[r - 1] = ld_dsmem_f4(src, (uint32_t)r);
-#pragma unroll
-                    for (int r = 1; r < 8; ++r)
-                        if (r < S) {
-                            const float4 p = part[r - 1];
-                            sum.x = __fadd_rn(sum.x, p.x);
-                            sum.y = __fadd_rn(sum.y, p.y);
-                            sum.z = __fadd_rn(sum.z, p.z);
-                            sum.w = __fadd_rn(sum.w, p.w);
-                        }
+                    for (int r = 1; r < S; ++r) {
+                        const float4 p = ld_dsmem_f4(src, (uint32_t)r);
+                        sum.x = __fadd_rn(sum.x, p.x);
+                        sum.y = __fadd_rn(sum.y, p.y);
+                        sum.z = __fadd_rn(sum.z, p.z);
+                        sum.w = __fadd_rn(sum.w, p.w);
+                    }
                     v[mat][0] = sum.x; v[mat][1] = sum.y; v[mat][2] = sum.z; v[mat][3] = sum.w;
                     had128_warp(v[mat], lane);
                 }
@@ -654,7 +658,7 @@ int exl3b_cuda_prep(const Exl3bOp* op, void* dst, int64_t dst_pitch, void* strea
     int64_t cmax = 0;
     for (int c = 0; c < op->n_class; ++c)
         if (op->cls[c].cols > cmax) cmax = op->cls[c].cols;
-    const int ngrp = (int)((cmax / 128 + 3) / 4);     // tasks a row: groups of four 128-blocks
+    const int ngrp = (int)((cmax / 128 + kPrepBpw - 1) / kPrepBpw);   // tasks a row: groups of kPrepBpw 128-blocks
     if (op->T * ngrp >= ((int64_t)1 << 31)) return -1;
     // enough warps to keep every SM's memory pipeline full (8 CTAs of 8 warps an SM), no more than the tasks
     const int64_t want = (op->T * ngrp + kPrepWarps - 1) / kPrepWarps;
