@@ -289,6 +289,94 @@ int     exl3b200_tp_pull(const uint64_t* peers, const int64_t* offs, int64_t sel
                          int64_t width, int64_t s_cap, float* out, int64_t out_pitch, const uint32_t* epoch,
                          int32_t* status, void* stream);
 
+/* Whole multi-GPU steps driven from C (one process a GPU; every rank calls the same entries in the same order). The
+ * windows' layouts:
+ *   exl3b200_ep_window_layout: the expert-parallel window for up to t_cap tokens a rank of top_k slots (p_cap =
+ *     t_cap * top_k); offs[6] = {rows, meta, yback, ctl, done, sink}; returns the bytes to allocate (-1: refused).
+ *   exl3b200_tp_window_layout: the width split's window for up to max_tokens tokens a step (s_cap =
+ *     ceil(max_tokens / world) rows a slice); offs[4] = {part, red, ctl, done}; returns the bytes (-1: refused).
+ * The expert-parallel step: exl3b200_ep_step_work_bytes sizes ONE device block (the routing, the received pairs at
+ * capacity world * max_tokens * top_k, h, the row table, the ops' scratch, the gather's map) and
+ * exl3b200_ep_step_carve cuts it; exl3b200_ep_step_forward then enqueues the whole step on `stream` and reads nothing
+ * on the host -- p2p_begin, router_topk, ep_dest, the scatter over ranks, ep_dedup_scan, p2p_dispatch,
+ * p2p_wait_dispatch, p2p_unpack, the local scatter, ep_map, then gate_up and down over the live rows through
+ * exl3b200_moe_op_live (down writing each row into its source's window when fuse_combine, else p2p_combine),
+ * p2p_wait_combine and the gather of the returned rows into out [n_tok][hidden] (RAD_F32 or RAD_BF16) -- so the
+ * step can be captured in a CUDA graph. desc->layer describes this rank's experts: n_expert every rank's together
+ * (world * n_local), expert_base = rank * n_local, the weight tables this rank's n_local experts. `epoch` (a device
+ * u32, zero at set-up, advanced once a step) and `status` (a device i32: 0, or -1 once a combine wait gave up) are
+ * the caller's; bufs->hdr[3 world] is the dispatch wait's status. `marks`: NULL, or 10 cudaEvent_t (NULL entries
+ * skipped) recorded on the stream at the step's boundaries: 0 start, 1 after the dedup scan, 2 after the dispatch
+ * wait, 3 after the local sort, 4 after down, 5 after the combine wait, 6 after the gather; 7, 8, 9 before gate_up,
+ * between the ops, after down.
+ * The width-split step: exl3b200_tp_step_forward runs this rank's slice of every expert (desc->layer: width = the
+ * slice's columns, n_local = n_expert) over the layer buffers of exl3b200_moe_layer_carve, then sums the ranks'
+ * partials over peer memory (tp_gather_rs, tp_reduce, tp_pull) into out (f32, row pitch out_pitch floats); every
+ * rank passes the same x, logits and n_tok. marks: NULL or 7 events -- 0 start, 1 routed, 2 after down, 3 summed;
+ * 4, 5, 6 before gate_up, between the ops, after down.
+ * No counterpart in the reference (one device; the engine drives the ops and its all_reduce). */
+typedef struct Exl3bEpDesc {
+    Exl3bLayerDesc  layer;
+    int64_t         rank, world;
+    int64_t         max_tokens;     /* tokens a rank routes a step, at most (the window's t_cap) */
+    int32_t         fuse_combine;   /* 1: down stores each row straight into its source's window */
+    int32_t         pad0;
+    void*           window;         /* this rank's window (exl3b200_ep_window_alloc) */
+    const uint64_t* peers;          /* device [world]: every rank's window as this rank maps it */
+    int64_t         offs[6];        /* exl3b200_ep_window_layout */
+    uint32_t*       epoch;
+    int32_t*        status;
+} Exl3bEpDesc;
+typedef struct Exl3bEpBufs {
+    int64_t   max_tokens, cap;      /* cap = world * max_tokens * top_k: the received pairs at most */
+    int32_t*  ids;                  /* [max_tokens][top_k] */
+    float*    w;                    /* [max_tokens][top_k] */
+    int32_t*  dest;                 /* [max_tokens * top_k] owner rank of each slot */
+    int32_t*  sorted_pairs;         /* [max_tokens * top_k] slots by owner rank, token order inside */
+    int32_t*  row_tok;              /* [max_tokens * top_k] */
+    uint32_t* send_meta;            /* [max_tokens * top_k] */
+    int32_t*  dest_off;             /* [world + 1] */
+    int32_t*  counts;               /* [2 world]: rows, pairs sent to each rank */
+    int32_t*  hdr;                  /* [3 world + 1]: rows, pairs, base from each source; [3 world] wait status */
+    int32_t*  pair_e;               /* [cap] each received pair's local expert (-1 past the live count) */
+    int32_t*  pair_row;             /* [cap] its row in the window's rows */
+    int32_t*  dst_rank;             /* [cap] */
+    int32_t*  dst_pos;              /* [cap] */
+    int32_t*  sorted_pair;          /* [cap] received pairs by local expert */
+    int32_t*  sorted_row;           /* [cap] their token rows (the ops' sorted_tok) */
+    int32_t*  expert_offset;        /* [n_local + 1] */
+    uint64_t* row_dst;              /* [cap] */
+    uint16_t* h;                    /* f16 [cap][width] */
+    uint16_t* y_rows;               /* bf16 [cap][hidden] when !fuse_combine, else NULL */
+    void*     scatter_rank;
+    void*     scatter_local;
+    void*     gu_scratch;
+    int64_t   gu_scratch_bytes;
+    void*     dn_scratch;
+    int64_t   dn_scratch_bytes;
+    void*     gather_work;
+} Exl3bEpBufs;
+typedef struct Exl3bTpDesc {
+    Exl3bLayerDesc  layer;
+    int64_t         rank, world;
+    int64_t         max_tokens;     /* tokens a step, at most */
+    void*           window;
+    const uint64_t* peers;
+    int64_t         offs[4];        /* exl3b200_tp_window_layout */
+    uint32_t*       epoch;
+    int32_t*        status;         /* 0, or -1 once a wait gave up */
+} Exl3bTpDesc;
+int64_t exl3b200_ep_window_layout(int64_t world, int64_t t_cap, int64_t top_k, int64_t hidden, int64_t* offs);
+int64_t exl3b200_tp_window_layout(int64_t world, int64_t max_tokens, int64_t hidden, int64_t* offs);
+int64_t exl3b200_ep_step_work_bytes(const Exl3bEpDesc* desc);
+int     exl3b200_ep_step_carve(const Exl3bEpDesc* desc, void* work, int64_t work_bytes, Exl3bEpBufs* bufs);
+int     exl3b200_ep_step_forward(const Exl3bEpDesc* desc, const Exl3bEpBufs* bufs, const uint16_t* x,
+                                 const float* logits, int64_t n_tok, void* out, int out_dtype, void* stream,
+                                 void* const* marks);
+int     exl3b200_tp_step_forward(const Exl3bTpDesc* desc, const Exl3bLayerBufs* bufs, const uint16_t* x,
+                                 const float* logits, int64_t n_tok, float* out, int64_t out_pitch, void* stream,
+                                 void* const* marks);
+
 /* How long a kernel that waits on another rank's flag (p2p_wait_dispatch, p2p_wait_combine, tp_reduce, tp_pull)
  * waits before it gives up, sets its status and the error word, and returns: `ns` nanoseconds, or the default 5 s
  * for ns <= 0 (more than 600 s is refused, RAD_E_INVAL). Process-wide; each launch reads it when it is enqueued

@@ -264,6 +264,11 @@ extern "C" {
 
 int exl3b_cuda_device_info(int* sm_count, int32_t** err_word);   // exl3b200_moe.cu
 
+// A caller's CUDA event recorded on the stream (the step drivers' phase marks; C code has no runtime headers).
+int exl3b_cuda_mark(void* event, void* stream) {
+    return cudaEventRecord(static_cast<cudaEvent_t>(event), static_cast<cudaStream_t>(stream)) == cudaSuccess ? 0 : -6;
+}
+
 // How long a kernel that waits on another rank's flag (the dispatch and combine waits here, the width split's
 // reduce and pull) waits before it gives up and reports: 5 s unless the caller set otherwise. Read at each launch
 // and passed to the kernel as an argument.

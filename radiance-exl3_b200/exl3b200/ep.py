@@ -137,23 +137,13 @@ class IpcWindow:
         self.base = None
 
 
-def _al(n):
-    return (n + 255) // 256 * 256
-
-
 class P2pWindow(IpcWindow):
-    """The expert-parallel window. Layout (byte offsets): rows [world][t_cap][H] f16 | meta [world][p_cap] u32 |
-    yback [p_cap][H] bf16 | ctl [world][8] u32 | done [2] u32 | sink [H] bf16."""
+    """The expert-parallel window, laid out by the library (exl3b200_ep_window_layout): rows [world][t_cap][H] f16 |
+    meta [world][p_cap] u32 | yback [p_cap][H] bf16 | ctl [world][8] u32 | done [2] u32 | sink [H] bf16."""
 
-    def __init__(self, nat, dist, group, rank, world, t_cap, p_cap, hidden, device):
-        o_rows = 0
-        o_meta = _al(world * t_cap * hidden * 2)
-        o_yback = o_meta + _al(world * p_cap * 4)
-        o_ctl = o_yback + _al(p_cap * hidden * 2)
-        o_done = o_ctl + _al(world * 32)
-        o_sink = o_done + 256
-        super().__init__(nat, dist, group, rank, world, (o_rows, o_meta, o_yback, o_ctl, o_done, o_sink),
-                         o_sink + _al(hidden * 2), device)
+    def __init__(self, nat, dist, group, rank, world, t_cap, top_k, hidden, device):
+        offs, nbytes = nat.ep_window_layout(world, t_cap, top_k, hidden)
+        super().__init__(nat, dist, group, rank, world, offs, nbytes, device)
 
     def rows_ptr(self):
         return self.base + self.offs[0]
@@ -182,14 +172,25 @@ class EpLayer:
         P, H = max_tokens * top_k, hidden
         self.Rcap = world * P
         if ops is None:
+            # the weights of this rank's experts; over NCCL also the buffers of the local pass (over peer memory the
+            # C driver carves its own)
             ops = DeviceOps(plugin, n_local=self.nl, hidden=hidden, width=width, bits_gu=bits_gu, bits_dn=bits_dn,
-                            codebook=codebook, max_rows=self.Rcap, seed=seed, device=dev)
+                            codebook=codebook, max_rows=self.Rcap if transport == "nccl" else 1, seed=seed,
+                            device=dev)
             if full is not None:
                 ops.local.load_experts(full, rank * self.nl)
         self.ops = ops
         e = lambda *shape, dt: torch.empty(shape, dtype=dt, device=dev)  # noqa: E731
         f16, bf16, i32, f32 = torch.float16, torch.bfloat16, torch.int32, torch.float32
         self.x, self.logits = e(max_tokens, H, dt=f16), e(max_tokens, n_expert, dt=f32)
+        self.out = e(max_tokens, H, dt=f32)
+        self.last = {"R": 0, "sent": 0}
+        if transport not in ("nccl", "p2p"):
+            raise ValueError(f"transport {transport!r}")
+        self.transport, self.win = transport, None
+        if transport == "p2p":
+            self._init_p2p(fuse_combine, bits_gu, bits_dn, codebook, width)
+            return
         self.ids, self.w, self.dest = e(P, dt=i32), e(P, dt=f32), e(P, dt=i32)
         self.sorted_pairs, self.row_tok = e(P, dt=i32), e(P, dt=i32)
         # one host read a step: [send counts 2G | receive counts 2G | rank offsets of the sorted pairs G + 1]
@@ -201,25 +202,47 @@ class EpLayer:
         self.recv_meta, self.pair_e, self.pair_row = e(self.Rcap, dt=i32), e(self.Rcap, dt=i32), e(self.Rcap, dt=i32)
         self.sorted_pair = e(self.Rcap, dt=i32)
         self.y_recv, self.y_back = e(self.Rcap, H, dt=bf16), e(P, H, dt=bf16)
-        self.out = e(max_tokens, H, dt=f32)
         self.sorted_row, self.off_loc, self.y_rows = ops.local_buffers()
-        self.last = {"R": 0, "sent": 0}
-        if transport not in ("nccl", "p2p"):
-            raise ValueError(f"transport {transport!r}")
-        self.transport, self.win, self.epoch = transport, None, 0
-        if transport == "p2p":
-            # peer-memory exchange: rows and metas straight into the owners' windows, down rows straight back
-            self.nat = ops.nat
-            self.win = P2pWindow(self.nat, dist, group, rank, world, max_tokens, P, H, dev)
-            self.dest_off_p = e(world + 1, dt=i32)
-            self.counts_p = e(2 * world, dt=i32)
-            self.hdr_p = torch.zeros(3 * world + 1, dtype=i32, device=dev)
-            self.epoch_dev = torch.zeros(1, dtype=i32, device=dev)     # the step's epoch, bumped on the device
-            self.status_p = torch.zeros(1, dtype=i32, device=dev)
-            self.dst_rank, self.dst_pos = e(self.Rcap, dt=i32), e(self.Rcap, dt=i32)
-            # the combine fused into down: each sorted row's destination in its source's window
-            self.fuse_combine = fuse_combine
-            self.row_dst = torch.empty(self.Rcap, dtype=torch.int64, device=dev)
+
+    def _init_p2p(self, fuse_combine, bits_gu, bits_dn, codebook, width):
+        """The peer-memory step: one call of the library's C driver (exl3b200_ep_step_forward) over one device block
+        it carves; the local experts' weights stay in ops.local. The views below are what the accounting reads."""
+        import torch
+        from .native import EpDesc
+        nat = self.nat = self.ops.nat
+        G, k, H, dev = self.G, self.k, self.H, self.dev
+        self.win = P2pWindow(nat, self.dist, self.group, self.rank, G, self.max_tokens, k, H, dev)
+        self.epoch_dev = torch.zeros(1, dtype=torch.int32, device=dev)     # the step's epoch, advanced on the device
+        self.status_p = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.fuse_combine = fuse_combine
+        d = self.desc = EpDesc()
+        ld = d.layer
+        ld.n_expert, ld.n_local, ld.expert_base = self.E, self.nl, self.rank * self.nl
+        ld.hidden, ld.width, ld.top_k = H, width, k
+        ld.bits_gu, ld.bits_dn, ld.codebook = bits_gu, bits_dn, {"3inst": 0, "mcg": 1, "mul1": 2}[codebook]
+        d.rank, d.world, d.max_tokens, d.fuse_combine = self.rank, G, self.max_tokens, int(fuse_combine)
+        d.window, d.peers = self.win.base, self.win.peers.data_ptr()
+        for i, o in enumerate(self.win.offs):
+            d.offs[i] = o
+        d.epoch, d.status = self.epoch_dev.data_ptr(), self.status_p.data_ptr()
+        self._sync_weights()
+        nbytes = nat.ep_step_work_bytes(d)
+        self.work = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+        b = self.bufs = nat.ep_step_carve(d, self.work.data_ptr(), nbytes)
+        base = self.work.data_ptr()
+
+        def view(ptr, n):
+            return self.work[ptr - base:ptr - base + 4 * n].view(torch.int32)
+
+        self.hdr_p, self.counts_p = view(b.hdr, 3 * G + 1), view(b.counts, 2 * G)
+        self.off_loc, self.sorted_row = view(b.expert_offset, self.nl + 1), view(b.sorted_row, self.Rcap)
+
+    def _sync_weights(self):
+        """Point the step's layer description at ops.local's current weight set (a stack swaps sets)."""
+        L, ld = self.ops.local, self.desc.layer
+        ld.gu_codes, ld.dn_codes = L.gu_tab.data_ptr(), L.dn_tab.data_ptr()
+        ld.suh, ld.suh1, ld.svh_gu = L.suh.data_ptr(), L.suh1.data_ptr(), L.svh_gu.data_ptr()
+        ld.dn_suh, ld.svh_dn = L.dn_suh.data_ptr(), L.svh_dn.data_ptr()
 
     # ------------------------------------------------------------------ the exchange
     def _a2a(self, out, inp, out_splits, in_splits):
@@ -276,51 +299,19 @@ class EpLayer:
                      "recv_counts": pairs_r, "send_rows": rows_s, "recv_rows": rows_r}
 
     def _forward_p2p(self, T, events, phases, x, logits, out):
-        """The same step with the exchange over peer memory and no host synchronisation at all: the local pass runs
-        at capacity (world * T * top_k received pairs) with its live count on the device (entries past it are
-        dropped pairs, rows past it untouched), and the epoch lives on the device -- so the step can be captured in
-        a CUDA graph and replayed."""
-        o, nat, win, G, k, P = self.ops, self.nat, self.win, self.G, self.k, T * self.k
-        st = o._stream()
-        Q, Tc, Pc = self.Rcap, self.max_tokens, self.max_tokens * k
-        ep = self.epoch_dev.data_ptr()
-        mark = (lambda i: phases[i].record()) if phases else (lambda i: None)
-        mark(0)
-        nat.p2p_begin(ep, st)
-        o.router(logits, T, self.E, k, self.ids, self.w)
-        o.dest(self.ids, P, self.nl, G, self.dest)
-        o.scatter(self.dest, P, G, self.sorted_pairs[:P], self.dest_off_p)
-        nat.ep_dedup_scan(self.ids.data_ptr(), k, self.sorted_pairs.data_ptr(), self.dest_off_p.data_ptr(), P,
-                          self.nl, G, self.send_meta.data_ptr(), self.row_tok.data_ptr(), self.counts_p.data_ptr(), st)
-        mark(1)
-        nat.p2p_dispatch(x.data_ptr(), x.shape[1], self.row_tok.data_ptr(), self.send_meta.data_ptr(),
-                         self.dest_off_p.data_ptr(), self.counts_p.data_ptr(), P, win.peers.data_ptr(), win.offs,
-                         self.rank, G, Tc, Pc, self.H, ep, st)
-        nat.p2p_wait_dispatch(win.base, win.offs, G, ep, self.hdr_p.data_ptr(), st)
-        mark(2)
-        nat.p2p_unpack(win.base, win.offs, self.hdr_p.data_ptr(), G, Tc, Pc, Q, self.pair_e.data_ptr(),
-                       self.pair_row.data_ptr(), self.dst_rank.data_ptr(), self.dst_pos.data_ptr(), st)
-        o.scatter(self.pair_e[:Q], Q, self.nl, self.sorted_pair[:Q], self.off_loc)
-        o.map(self.sorted_pair, Q, self.pair_row, Q, self.sorted_row)
-        mark(3)
-        if self.fuse_combine:
-            # down's epilogue writes each pair's row straight into its source's window (NVLink stores overlapping
-            # the decode of the next units), then the flags
-            nat.p2p_row_dst(self.sorted_pair.data_ptr(), Q, self.dst_rank.data_ptr(), self.dst_pos.data_ptr(),
-                            win.peers.data_ptr(), win.offs, self.rank, G, Pc, self.H, self.row_dst.data_ptr(), st)
-            o.experts(None, G * Tc, Q, events, x_ptr=win.rows_ptr(), down_row_dst=self.row_dst.data_ptr(), live=True)
-            mark(4)
-            nat.p2p_signal_combine(win.peers.data_ptr(), win.offs, self.rank, G, ep, st)
-        else:
-            o.experts(None, G * Tc, Q, events, x_ptr=win.rows_ptr(), live=True)
-            mark(4)
-            nat.p2p_combine(self.y_rows.data_ptr(), self.H, self.sorted_pair.data_ptr(), Q, self.dst_rank.data_ptr(),
-                            self.dst_pos.data_ptr(), win.peers.data_ptr(), win.offs, self.rank, G, Pc, self.H, ep, st)
-        nat.p2p_wait_combine(win.base, win.offs, G, ep, self.status_p.data_ptr(), st)
-        mark(5)
-        o.gather(None, self.sorted_pairs, P, self.w, T, k, out, rows_ptr=win.yback_ptr())
-        mark(6)
-        self.last = {"p2p": True, "sent": P}
+        """The same step with the exchange over peer memory, as ONE call of the library's C driver
+        (exl3b200_ep_step_forward): no host synchronisation at all -- the local pass runs at capacity (world * T *
+        top_k received pairs) with its live count on the device, and the epoch lives on the device -- so the step
+        can be captured in a CUDA graph and replayed. `phases` and `events` become the driver's marks."""
+        from .native import marks_array
+        self._sync_weights()
+        marks = None
+        if phases or events:
+            marks = marks_array(list(phases or [None] * 7) + list(events or [None] * 3))
+        dt = 3 if out.dtype == self.torch.bfloat16 else 1
+        self.nat.ep_step_forward(self.desc, self.bufs, x.data_ptr(), logits.data_ptr(), T, out.data_ptr(), dt,
+                                 self.ops._stream(), marks)
+        self.last = {"p2p": True, "sent": T * self.k}
 
     def _p2p_counts(self):
         """The last step's received counts, read from the device (synchronises): rows and pairs from each source."""
@@ -361,7 +352,8 @@ class EpLayer:
         R = self._R()
         Rr = self.last.get("rows_recv", R)
         if self.transport == "p2p":
-            return self.ops.local.time_prep(self.G * self.max_tokens, R, x_ptr=self.win.rows_ptr(), top_k=1, n=n)
+            return self.ops.local.time_prep(self.G * self.max_tokens, R, x_ptr=self.win.rows_ptr(), top_k=1, n=n,
+                                            sorted_tok=self.sorted_row.data_ptr(), offset=self.off_loc.data_ptr())
         return self.ops.local.time_prep(Rr, R, x_ptr=self.recv_x.data_ptr(), top_k=1, n=n)
 
     def expert_flops(self, rows):

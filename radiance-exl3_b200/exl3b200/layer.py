@@ -276,10 +276,11 @@ class MoeLayer:
         if events:
             events[2].record()
 
-    def time_prep(self, T, rows, x_ptr=None, top_k=None, n=5):
+    def time_prep(self, T, rows, x_ptr=None, top_k=None, n=5, sorted_tok=None, offset=None):
         """Mean device time (ms, CUDA events on the current stream) of the gate_up input rotation alone: the
         moe_exl3_prep_gu row over the same sorted rows, i.e. the k_prep launch the tensor-core gate_up runs first.
-        The bench subtracts it from the gate_up op to time k_gemm_tc by itself."""
+        The bench subtracts it from the gate_up op to time k_gemm_tc by itself. `sorted_tok`, `offset`: the routing
+        of a pass whose buffers live elsewhere (device addresses; this layer's by default)."""
         torch = self.torch
         if rows == 0:
             return 0.0
@@ -292,8 +293,8 @@ class MoeLayer:
         ts = [rad.tensor(x_ptr or self.x.data_ptr(), rad.DT["f16"], [T, H]),
               rad.tensor(self.suh.data_ptr(), rad.DT["f16"], [E, 1, H]),
               rad.tensor(self.suh1.data_ptr(), rad.DT["f16"], [E, 1, H]),
-              rad.tensor(self.sorted_tok.data_ptr(), rad.DT["i32"], [rows]),
-              rad.tensor(self.offset.data_ptr(), rad.DT["i32"], [E + 1]),
+              rad.tensor(sorted_tok or self.sorted_tok.data_ptr(), rad.DT["i32"], [rows]),
+              rad.tensor(offset or self.offset.data_ptr(), rad.DT["i32"], [E + 1]),
               absent, absent,
               rad.tensor(self._xr.data_ptr(), rad.DT["f16"], [rows, 2 * H])]
         arr = (rad.RadTensor * len(ts))(*ts)

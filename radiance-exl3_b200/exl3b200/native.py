@@ -24,6 +24,42 @@ class LayerBufs(C.Structure):
                 ("dn_scratch", _VP), ("dn_scratch_bytes", _I64), ("gather_work", _VP)]
 
 
+class EpDesc(C.Structure):
+    """Exl3bEpDesc (include/exl3b200.h)."""
+    _fields_ = [("layer", LayerDesc), ("rank", _I64), ("world", _I64), ("max_tokens", _I64),
+                ("fuse_combine", C.c_int32), ("pad0", C.c_int32), ("window", _VP), ("peers", _VP),
+                ("offs", _I64 * 6), ("epoch", _VP), ("status", _VP)]
+
+
+class EpBufs(C.Structure):
+    """Exl3bEpBufs (include/exl3b200.h): device addresses inside the caller's work block."""
+    _fields_ = [("max_tokens", _I64), ("cap", _I64)] + [(n, _VP) for n in (
+        "ids", "w", "dest", "sorted_pairs", "row_tok", "send_meta", "dest_off", "counts", "hdr", "pair_e", "pair_row",
+        "dst_rank", "dst_pos", "sorted_pair", "sorted_row", "expert_offset", "row_dst", "h", "y_rows", "scatter_rank",
+        "scatter_local", "gu_scratch")] + [("gu_scratch_bytes", _I64), ("dn_scratch", _VP),
+                                           ("dn_scratch_bytes", _I64), ("gather_work", _VP)]
+
+
+class TpDesc(C.Structure):
+    """Exl3bTpDesc (include/exl3b200.h)."""
+    _fields_ = [("layer", LayerDesc), ("rank", _I64), ("world", _I64), ("max_tokens", _I64), ("window", _VP),
+                ("peers", _VP), ("offs", _I64 * 4), ("epoch", _VP), ("status", _VP)]
+
+
+def marks_array(events):
+    """A C array of cudaEvent_t from torch.cuda.Event objects (None entries stay NULL), or None. torch creates an
+    event's handle at its first record, so each is recorded once here before its handle is taken."""
+    if not events:
+        return None
+    arr = (_VP * len(events))()
+    for i, e in enumerate(events):
+        if e is not None:
+            if not e.cuda_event:
+                e.record()
+            arr[i] = e.cuda_event
+    return arr
+
+
 class Native:
     def __init__(self, path=None):
         L = self.lib = C.CDLL(str(path or library_path()))
@@ -71,6 +107,17 @@ class Native:
         L.exl3b200_moe_layer_forward.argtypes = [C.POINTER(LayerDesc), C.POINTER(LayerBufs), _VP, _VP, _I64, _VP,
                                                  C.c_int, _VP]
         L.exl3b200_set_peer_wait_ns.argtypes = [_I64]
+        L.exl3b200_ep_window_layout.restype = _I64
+        L.exl3b200_ep_window_layout.argtypes = [_I64, _I64, _I64, _I64, C.POINTER(_I64)]
+        L.exl3b200_tp_window_layout.restype = _I64
+        L.exl3b200_tp_window_layout.argtypes = [_I64, _I64, _I64, C.POINTER(_I64)]
+        L.exl3b200_ep_step_work_bytes.restype = _I64
+        L.exl3b200_ep_step_work_bytes.argtypes = [C.POINTER(EpDesc)]
+        L.exl3b200_ep_step_carve.argtypes = [C.POINTER(EpDesc), _VP, _I64, C.POINTER(EpBufs)]
+        L.exl3b200_ep_step_forward.argtypes = [C.POINTER(EpDesc), C.POINTER(EpBufs), _VP, _VP, _I64, _VP, C.c_int,
+                                               _VP, C.POINTER(_VP)]
+        L.exl3b200_tp_step_forward.argtypes = [C.POINTER(TpDesc), C.POINTER(LayerBufs), _VP, _VP, _I64, _VP, _I64,
+                                               _VP, C.POINTER(_VP)]
         L.exl3b200_p2p_begin.argtypes = [_VP, _VP]
         L.exl3b200_moe_op_live.argtypes = [_VP, _I, _VP, _VP]
         L.exl3b200_tp_gather_rs.argtypes = [_VP, _I64, _VP, _I64, _VP, _I64, _I64, _I64, _VP, _VP, _VP, _I64, _I64,
@@ -265,3 +312,42 @@ class Native:
     def tp_pull(self, peers, offs, rank, world, n_tok, width, s_cap, out, out_pitch, epoch, status, stream=0):
         self._check(self.lib.exl3b200_tp_pull(peers, offs, rank, world, n_tok, width, s_cap, out, out_pitch, epoch,
                                               status, stream), "exl3b200_tp_pull")
+
+    # ---- whole multi-GPU steps driven from C (exl3b200_layer.c)
+    def ep_window_layout(self, world, t_cap, top_k, hidden):
+        """(offs[6], bytes) of the expert-parallel window."""
+        offs = (_I64 * 6)()
+        n = int(self.lib.exl3b200_ep_window_layout(world, t_cap, top_k, hidden, offs))
+        if n < 0:
+            raise RuntimeError("exl3b200_ep_window_layout: refused")
+        return tuple(offs), n
+
+    def tp_window_layout(self, world, max_tokens, hidden):
+        """(offs[4], bytes) of the width split's window."""
+        offs = (_I64 * 4)()
+        n = int(self.lib.exl3b200_tp_window_layout(world, max_tokens, hidden, offs))
+        if n < 0:
+            raise RuntimeError("exl3b200_tp_window_layout: refused")
+        return tuple(offs), n
+
+    def ep_step_work_bytes(self, desc):
+        n = int(self.lib.exl3b200_ep_step_work_bytes(C.byref(desc)))
+        if n < 0:
+            raise RuntimeError("exl3b200_ep_step_work_bytes: the step description was refused")
+        return n
+
+    def ep_step_carve(self, desc, work, work_bytes):
+        b = EpBufs()
+        self._check(self.lib.exl3b200_ep_step_carve(C.byref(desc), work, work_bytes, C.byref(b)),
+                    "exl3b200_ep_step_carve")
+        return b
+
+    def ep_step_forward(self, desc, bufs, x, logits, n_tok, out, out_dtype, stream=0, marks=None):
+        """out_dtype: 1 (RAD_F32) or 3 (RAD_BF16); marks: None or marks_array() of 10 events."""
+        self._check(self.lib.exl3b200_ep_step_forward(C.byref(desc), C.byref(bufs), x, logits, n_tok, out, out_dtype,
+                                                      stream, marks), "exl3b200_ep_step_forward")
+
+    def tp_step_forward(self, desc, bufs, x, logits, n_tok, out, out_pitch, stream=0, marks=None):
+        """bufs: the slice layer's LayerBufs; out f32; marks: None or marks_array() of 7 events."""
+        self._check(self.lib.exl3b200_tp_step_forward(C.byref(desc), C.byref(bufs), x, logits, n_tok, out, out_pitch,
+                                                      stream, marks), "exl3b200_tp_step_forward")

@@ -127,20 +127,6 @@ def load_classes(dst, src, cuts):
 
 
 # ------------------------------------------------------------------------------------------ the layer
-class TpWindow:
-    """Layout of the width split's window (byte offsets): part [world][s_cap][H] f32 | red [s_cap][H] f32 |
-    ctl [world][8] u32 | done [4] u32."""
-
-    @staticmethod
-    def layout(world, s_cap, hidden):
-        al = lambda n: (n + 255) // 256 * 256  # noqa: E731
-        o_part = 0
-        o_red = al(world * s_cap * hidden * 4)
-        o_ctl = o_red + al(s_cap * hidden * 4)
-        o_done = o_ctl + al(world * 32)
-        return (o_part, o_red, o_ctl, o_done), o_done + 256
-
-
 class TpLayer:
     """The routed-MoE layer with every expert's width split over `world` ranks. Every rank builds the same seeded
     full-width experts (or takes `full`, a MoeLayer) and keeps its slice; x and logits are the same on every rank
@@ -183,12 +169,24 @@ class TpLayer:
         self.x, self.logits, self.out = L.x, L.logits, L.out
         self.win = None
         if transport == "p2p":
+            # the window laid out by the library (exl3b200_tp_window_layout): part [world][s_cap][H] f32 |
+            # red [s_cap][H] f32 | ctl [world][8] u32 | done [4] u32, s_cap = ceil(max_tokens / world)
             self.s_cap = (max_tokens + world - 1) // world
-            offs, nbytes = TpWindow.layout(world, self.s_cap, hidden)
+            offs, nbytes = self.nat.tp_window_layout(world, max_tokens, hidden)
             from .ep import IpcWindow
             self.win = IpcWindow(self.nat, dist, group, rank, world, offs, nbytes, dev)
             self.epoch_dev = torch.zeros(1, dtype=torch.int32, device=dev)
             self.status = torch.zeros(1, dtype=torch.int32, device=dev)
+            if getattr(L, "c_layer", False):
+                # the even cut: the whole step is one call of the library's C driver (exl3b200_tp_step_forward)
+                from .native import TpDesc
+                d = self.desc = TpDesc()
+                d.layer = L.desc
+                d.rank, d.world, d.max_tokens = rank, world, max_tokens
+                d.window, d.peers = self.win.base, self.win.peers.data_ptr()
+                for i, o in enumerate(offs):
+                    d.offs[i] = o
+                d.epoch, d.status = self.epoch_dev.data_ptr(), self.status.data_ptr()
 
     def forward(self, T, stream=None, events=None, phases=None, x=None, logits=None, out=None):
         """The layer over the first T tokens of x / logits (self.x / self.logits by default; the same on every
@@ -202,6 +200,16 @@ class TpLayer:
         logits = self.logits if logits is None else logits
         out = self.out if out is None else out
         rows = T * k
+        if self.win is not None and getattr(L, "c_layer", False):
+            from .native import marks_array
+            d = self.desc
+            d.layer = L.desc                      # the slice layer's current weight set
+            marks = marks_array(list(phases or [None] * 4) + list(events or [None] * 3)) \
+                if (phases or events) else None
+            nat.tp_step_forward(d, L.bufs, x.data_ptr(), logits.data_ptr(), T, out.data_ptr(), out.shape[1], st,
+                                marks)
+            return
+        # the uneven cut (class rows) or NCCL: the same steps composed here
         mark = (lambda i: phases[i].record()) if phases else (lambda i: None)
         mark(0)
         if self.win is not None:

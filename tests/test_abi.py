@@ -221,3 +221,105 @@ def test_layer_band_rule_mirrors_the_library(plugin, op, E, H, W, k):
         want = (rows * (2 * H if gate_up else W) * 2 + 255) // 256 * 256
         tc = MoeLayer._tc(mirror, "gate_up" if gate_up else "down", rows)
         assert need == (want if tc else 0), (T, need, tc)
+
+
+def _layer_desc(E, n_local, base, H=2048, W=512, k=10):
+    from exl3b200.native import LayerDesc
+    d = LayerDesc()
+    d.n_expert, d.n_local, d.expert_base, d.hidden, d.width, d.top_k = E, n_local, base, H, W, k
+    d.bits_gu, d.bits_dn, d.codebook = 3, 4, 2
+    d.gu_codes = d.dn_codes = d.suh = d.suh1 = d.svh_gu = d.dn_suh = d.svh_dn = 1 << 20
+    return d
+
+
+def _regions(bufs, sizes):
+    """(start, end) of every carved buffer named in `sizes` (bytes), checked 256-byte aligned."""
+    out = []
+    for name, n in sizes.items():
+        p = getattr(bufs, name)
+        assert p is not None and p % 256 == 0, name
+        out.append((p, p + n, name))
+    return sorted(out)
+
+
+@pytest.mark.parametrize("world,rank,T,fuse", [(1, 0, 192, True), (2, 1, 2048, True), (8, 5, 2048, True),
+                                               (4, 3, 8, False)])
+def test_ep_step_carve_is_disjoint_and_in_bounds(world, rank, T, fuse):
+    """The expert-parallel step's C driver carves one caller block (pure host arithmetic: no device address is
+    touched): every buffer 256-byte aligned, inside the block, none overlapping another; the window layout puts its
+    six regions in order with room for the sizes the exchange kernels write."""
+    from exl3b200.native import EpDesc, Native
+    nat = Native()
+    E, H, W, k = 512, 2048, 512, 10
+    nl = E // world
+    offs, wbytes = nat.ep_window_layout(world, T, k, H)
+    P = T * k
+    need = [world * T * H * 2, world * P * 4, P * H * 2, world * 32, 8, H * 2]
+    for i in range(6):
+        end = offs[i + 1] if i < 5 else wbytes
+        assert offs[i] % 256 == 0 and end - offs[i] >= need[i], (i, offs)
+    d = EpDesc()
+    d.layer = _layer_desc(E, nl, rank * nl, H, W, k)
+    d.rank, d.world, d.max_tokens, d.fuse_combine = rank, world, T, int(fuse)
+    d.window, d.peers, d.epoch, d.status = 1 << 30, 1 << 30, 1 << 30, 1 << 30
+    for i, o in enumerate(offs):
+        d.offs[i] = o
+    nbytes = nat.ep_step_work_bytes(d)
+    base = 1 << 40
+    b = nat.ep_step_carve(d, base, nbytes)
+    Q = world * P
+    assert b.cap == Q and b.max_tokens == T
+    sizes = {"ids": P * 4, "w": P * 4, "dest": P * 4, "sorted_pairs": P * 4, "row_tok": P * 4, "send_meta": P * 4,
+             "dest_off": (world + 1) * 4, "counts": 2 * world * 4, "hdr": (3 * world + 1) * 4, "pair_e": Q * 4,
+             "pair_row": Q * 4, "dst_rank": Q * 4, "dst_pos": Q * 4, "sorted_pair": Q * 4, "sorted_row": Q * 4,
+             "expert_offset": (nl + 1) * 4, "row_dst": Q * 8, "h": Q * W * 2,
+             "scatter_rank": max(1, nat.scatter_work_bytes(P, world)),
+             "scatter_local": max(1, nat.scatter_work_bytes(Q, nl)),
+             "gather_work": max(1, nat.gather_work_bytes(T, k))}
+    if not fuse:
+        sizes["y_rows"] = Q * H * 2
+    else:
+        assert not b.y_rows
+    if b.gu_scratch:
+        sizes["gu_scratch"] = b.gu_scratch_bytes
+    if b.dn_scratch:
+        sizes["dn_scratch"] = b.dn_scratch_bytes
+    # gate_up at capacity runs the tensor-core band: its rotated input rows are carved
+    assert b.gu_scratch_bytes >= Q * 2 * H * 2
+    regs = _regions(b, sizes)
+    assert regs[0][0] >= base and regs[-1][1] <= base + nbytes
+    for (s0, e0, n0), (s1, e1, n1) in zip(regs, regs[1:]):
+        assert e0 <= s1, (n0, n1)
+
+
+def test_step_descriptions_are_refused_before_any_device_work():
+    """The drivers check their descriptions on the host: a rank outside the world, an expert base that is not the
+    rank's block, an expert count the world does not divide, a missing window or epoch -- refused (-1 bytes; a
+    carve or forward returns an error) with nothing enqueued."""
+    from exl3b200.native import EpDesc, Native, TpDesc
+    nat = Native()
+
+    def ep(world=2, rank=1, nl=256, base=256, window=1 << 30, epoch=1 << 30):
+        d = EpDesc()
+        d.layer = _layer_desc(world * nl if nl else 512, nl or 1, base)
+        d.rank, d.world, d.max_tokens, d.fuse_combine = rank, world, 64, 1
+        d.window, d.peers, d.epoch, d.status = window, 1 << 30, epoch, 1 << 30
+        return d
+
+    assert nat.lib.exl3b200_ep_step_work_bytes(C.byref(ep())) > 0
+    for bad in (ep(rank=2), ep(base=0), ep(world=33, rank=0, base=0), ep(window=None), ep(epoch=None)):
+        assert nat.lib.exl3b200_ep_step_work_bytes(C.byref(bad)) == -1
+    d = ep()
+    d.layer.n_expert = 511                      # the world does not divide the experts
+    assert nat.lib.exl3b200_ep_step_work_bytes(C.byref(d)) == -1
+    assert nat.lib.exl3b200_ep_window_layout(0, 64, 10, 2048, (C.c_int64 * 6)()) == -1
+    assert nat.lib.exl3b200_tp_window_layout(2, 0, 2048, (C.c_int64 * 4)()) == -1
+    # the width-split driver refuses a slice layer that does not hold every expert, before any launch
+    from exl3b200.native import LayerBufs
+    t = TpDesc()
+    t.layer = _layer_desc(512, 256, 0)
+    t.rank, t.world, t.max_tokens = 0, 2, 64
+    t.window, t.peers, t.epoch, t.status = 1 << 30, 1 << 30, 1 << 30, 1 << 30
+    rc = nat.lib.exl3b200_tp_step_forward(C.byref(t), C.byref(LayerBufs()), 1 << 30, 1 << 30, 8, 1 << 30, 2048,
+                                          None, None)
+    assert rc == -1

@@ -433,6 +433,33 @@ def _ep_single_rank(port, q):
             torch.cuda.synchronize()
             ep.check()
             res.append(bool(torch.equal(full.out[:T], ep.out[:T])))
+            if fuse:
+                # the C driver's phase marks (the step's 7 boundaries and the 3 around the ops), the bf16 output,
+                # and the step captured in a CUDA graph and replayed: the same bits every time
+                ph = [torch.cuda.Event(enable_timing=True) for _ in range(7)]
+                ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+                ep.out.zero_()
+                ep.forward(T, s, events=ev, phases=ph)
+                torch.cuda.synchronize()
+                times = [ph[i].elapsed_time(ph[i + 1]) for i in range(6)] + [ev[0].elapsed_time(ev[2])]
+                res.append(all(t >= 0 for t in times) and ev[0].elapsed_time(ev[2]) <= ph[0].elapsed_time(ph[6]))
+                res.append(bool(torch.equal(full.out[:T], ep.out[:T])))
+                yb_full = torch.empty((T, H), dtype=torch.bfloat16, device=dev)
+                yb_ep = torch.zeros((T, H), dtype=torch.bfloat16, device=dev)
+                full.forward(T, s, out=yb_full)
+                ep.forward(T, s, out=yb_ep)
+                torch.cuda.synchronize()
+                res.append(bool(torch.equal(yb_full, yb_ep)))
+                ep.out.zero_()
+                gph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(gph):
+                    ep.forward(T, torch.cuda.current_stream().cuda_stream)
+                for _ in range(3):
+                    gph.replay()
+                torch.cuda.synchronize()
+                ep.check()
+                res.append(bool(torch.equal(full.out[:T], ep.out[:T])))
+                del gph
             ep.close()
         q.put(res)
     except Exception as exc:
@@ -451,4 +478,4 @@ def test_ep_single_rank_over_peer_memory_equals_the_layer():
     p.start()
     r = q.get(timeout=600)
     p.join(timeout=120)
-    assert r == [True, True], r
+    assert r == [True] * 6, r
