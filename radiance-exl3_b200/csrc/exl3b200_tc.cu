@@ -2,7 +2,10 @@
 // GEMM with its accumulators in tensor memory. sm_100a only.
 //
 // One persistent CTA an SM walks the unit list -- unit = (expert, up to 64 of its sorted rows, two 128-row output
-// blocks: gate block b with up block b for gate_up, blocks 2q and 2q+1 for down) -- with warp-specialised roles:
+// blocks: gate block b with up block b for gate_up, blocks 2q and 2q+1 for down) -- with warp-specialised roles.
+// The WIDE form takes up to 128 rows a unit: a unit of more than 64 rows decodes its weights once and multiplies
+// both 64-row halves, each half into its own accumulator buffer (two MMA sets a chunk), so an expert's weights are
+// decoded once a 128 rows (the host picks it for passes of many rows an expert and many units).
 //
 //   warps 0..7   epilogue: tcgen05.ld of a finished unit's accumulators (lane quadrant = warp % 4, block = warp / 4),
 //                the rotation over n (transposed through shared memory), svh, SiLU(gate)*up and h_rot / bf16, stores
@@ -17,8 +20,8 @@
 //                (lane g: rows g, g+8; 32-bit columns t, t+4 = k pairs 2t, 2t+8) -- and stores it into tensor
 //                memory; a decoder warp writes only its own TMEM lane quadrant (warp % 4)
 //
-// Tensor memory (512 columns): two accumulator buffers (2 units x 2 blocks x 64 columns, so the epilogue of one
-// unit runs while the next is computed) and kStA A stages of 2 blocks x kKC / 2 columns (128 lanes x kKC k of f16).
+// Tensor memory (512 columns): two accumulator buffers (2 x 2 blocks x 64 columns, so the epilogue of one 64-row
+// half runs while the next is computed; a wide unit takes both) and kStA A stages of 2 blocks x kKC / 2 columns (128 lanes x kKC k of f16).
 // Shared memory holds only the input-row ring, the record ring and the epilogue's staging. Every wait is bounded
 // (then the error word is set); TMEM is freed by the allocating warp before the CTA exits on every path.
 #include <cuda.h>
@@ -44,7 +47,10 @@ constexpr int kDecTn = EXL3B_TC_DEC_TN;              // 16-row tile rows a decod
 constexpr int kDecWarps = 16 / kDecTn;               // 16 / kDecTn: 4 / kDecTn a lane quadrant
 constexpr int kTcWarps = kDecWarp0 + kDecWarps;      // 28
 constexpr int kTcThreads = kTcWarps * 32;           // 896
-constexpr int kNT = 64;                              // sorted rows a unit (the MMA's N)
+constexpr int kNT = 64;                              // sorted rows a half unit (the MMA's N; one accumulator buffer)
+constexpr int kUG = 2 * kNT;                         // sorted rows a wide unit at most (two halves)
+constexpr int kWideUnitsPerSm = 4;                   // wide units are chosen only with at least this many an SM
+constexpr int kWideMinCols = 1024;                   // ... and an input at least this wide (16+ chunks a unit)
 constexpr int kBox = 64;                             // k of one TMA box = one SWIZZLE_128B atom row (128 B)
 constexpr int kKC = 128;                             // k a pipeline chunk: one handoff between the roles
 constexpr int kKT = kKC / 16;                        // k tiles a chunk
@@ -140,16 +146,17 @@ __device__ __forceinline__ void tma_tile_g2s_el(void* dst, const CUtensorMap* ma
 }
 
 // ------------------------------------------------------------------------------------------ units
-// Unit u -> (expert, row group, block pair). Units of expert e: ceil(rows_e / 64) * n_pairs. The record also holds
+// Unit u -> (expert, row group, block pair). Units of expert e: ceil(rows_e / 128) * n_pairs. The record also holds
 // what every role derives from the expert (its class, its entry in the class's tables, whether the pair exists for
 // that class's width), computed once when the CTA builds its unit table, so no role divides in its loop.
 struct TcUnit {
     int64_t r0;        // first sorted row
     int32_t e, j;      // expert, entry in its class's tables
-    int16_t nr, pair;  // rows (<= 64), output block pair
+    int16_t nr, pair;  // rows (<= 128: more than 64 makes a wide unit), output block pair
     int16_t c, live;   // class; 0: the pair lies past the class's width (its rows are zero there)
 };
 
+template <int UG>
 __device__ __forceinline__ TcUnit tc_unit(const Exl3bOp& op, const uint32_t* prefix, int64_t unit, int n_pairs) {
     int64_t lo = 0, hi = op.n_expert;
     while (hi - lo > 1) {
@@ -161,9 +168,9 @@ __device__ __forceinline__ TcUnit tc_unit(const Exl3bOp& op, const uint32_t* pre
     const int64_t local = unit - prefix[lo];
     const int64_t grp = local / n_pairs;
     u.pair = (int16_t)(local % n_pairs);
-    u.r0 = op.expert_offset[lo] + grp * kNT;
+    u.r0 = op.expert_offset[lo] + grp * UG;
     const int64_t rend = op.expert_offset[lo + 1];
-    u.nr = (int16_t)(rend - u.r0 < kNT ? rend - u.r0 : kNT);
+    u.nr = (int16_t)(rend - u.r0 < UG ? rend - u.r0 : UG);
     const ExpertView ev = expert_view(op, lo);
     u.c = (int16_t)ev.c;
     u.j = (int32_t)ev.j;
@@ -180,10 +187,11 @@ struct Ring {
 };
 
 // ------------------------------------------------------------------------------------------ the kernel
-template <int BITS, int CB, bool GU>
+template <int BITS, int CB, bool GU, bool WIDE>
 __global__ void __launch_bounds__(kTcThreads, 1)
     k_gemm_tc(const __grid_constant__ CUtensorMap tmap, const Exl3bOp op, int n_pairs) {
     using Cfg = TcCfg<BITS>;
+    constexpr int UG = WIDE ? kUG : kNT;                // sorted rows a unit at most
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     // 1024-byte alignment of every swizzled tile, as an offset from the shared array (the pointers stay visibly in
     // shared memory, so every access through them is a shared-memory instruction, not a generic one)
@@ -224,7 +232,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
-    // the unit list: ceil(rows_e / 64) * n_pairs units an expert, expert-major. prefix[e] = the first unit of
+    // the unit list: ceil(rows_e / 128) * n_pairs units an expert, expert-major. prefix[e] = the first unit of
     // expert e (a block-wide exclusive scan of the per-expert counts, each thread a run of experts)
     {
         __shared__ uint32_t wsum[kTcWarps];
@@ -233,7 +241,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         uint32_t sum = 0;
         for (int64_t e = e0; e < e1; ++e) {
             const int64_t r = op.expert_offset[e + 1] - op.expert_offset[e];
-            sum += r > 0 ? (uint32_t)(((r + kNT - 1) / kNT) * n_pairs) : 0u;
+            sum += r > 0 ? (uint32_t)(((r + UG - 1) / UG) * n_pairs) : 0u;
         }
         uint32_t incl = sum;                                   // inclusive scan within the warp
 #pragma unroll
@@ -249,7 +257,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         for (int64_t e = e0; e < e1; ++e) {
             prefix[e] = acc;
             const int64_t r = op.expert_offset[e + 1] - op.expert_offset[e];
-            acc += r > 0 ? (uint32_t)(((r + kNT - 1) / kNT) * n_pairs) : 0u;
+            acc += r > 0 ? (uint32_t)(((r + UG - 1) / UG) * n_pairs) : 0u;
         }
         if (tid == kTcThreads - 1) prefix[n_exp] = acc;
     }
@@ -258,7 +266,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const int64_t n_units = prefix[n_exp];
     const int64_t n_mine = n_units > blockIdx.x ? (n_units - blockIdx.x + gridDim.x - 1) / gridDim.x : 0;
     for (int64_t i = tid; i < n_mine && i < kUnitTab; i += kTcThreads)
-        utab[i] = tc_unit(op, prefix, blockIdx.x + i * gridDim.x, n_pairs);
+        utab[i] = tc_unit<UG>(op, prefix, blockIdx.x + i * gridDim.x, n_pairs);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -266,7 +274,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     // every lane, and the tensor-memory addresses and MMA operands derived from it stay warp-uniform
     const uint32_t tmem = __shfl_sync(0xFFFFFFFFu, *tmem_slot, 0);
     auto unit_at = [&](int64_t i) -> TcUnit {
-        return i < kUnitTab ? utab[i] : tc_unit(op, prefix, blockIdx.x + i * gridDim.x, n_pairs);
+        return i < kUnitTab ? utab[i] : tc_unit<UG>(op, prefix, blockIdx.x + i * gridDim.x, n_pairs);
     };
 
     // rows no unit writes are zeroed (outside the runs, dropped slots): the grid's threads test the rows in
@@ -318,16 +326,21 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     }
                 }
             } else {
-                // input rows of each chunk (sorted rows r0 .. r0+63; zero fill past T)
-                for (int ck = 0; ck < nck; ++ck, br.next(kStB)) {
-                    mbar_wait_warp(&b_empty[br.s], br.ph ^ 1, op.err);
-                    mbar_expect_tx_el(&b_full[br.s], (uint32_t)((GU ? 2 : 1) * kBHalf));
+                // input rows of each chunk, a stage a 64-row half (rows r0 .. r0+63, then r0+64 .. for a wide unit;
+                // zero fill past T)
+                const int nh = WIDE && u.nr > kNT ? 2 : 1;
+                for (int ck = 0; ck < nck; ++ck) {
+                    for (int hh = 0; hh < nh; ++hh, br.next(kStB)) {
+                        mbar_wait_warp(&b_empty[br.s], br.ph ^ 1, op.err);
+                        mbar_expect_tx_el(&b_full[br.s], (uint32_t)((GU ? 2 : 1) * kBHalf));
 #pragma unroll
-                    for (int m = 0; m < (GU ? 2 : 1); ++m)
+                        for (int m = 0; m < (GU ? 2 : 1); ++m)
 #pragma unroll
-                        for (int bx = 0; bx < kNBox; ++bx)
-                            tma_tile_g2s_el(b_ring + (br.s * 2 + m) * kBHalf + bx * kBTile, &tmap,
-                                            (int)(m * cl.cols + ck * kKC + bx * kBox), (int)u.r0, &b_full[br.s]);
+                            for (int bx = 0; bx < kNBox; ++bx)
+                                tma_tile_g2s_el(b_ring + (br.s * 2 + m) * kBHalf + bx * kBTile, &tmap,
+                                                (int)(m * cl.cols + ck * kKC + bx * kBox), (int)(u.r0 + hh * kNT),
+                                                &b_full[br.s]);
+                    }
                 }
             }
         }
@@ -340,32 +353,42 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         // add to the start-address field (the shared-memory window is below 256 KB, so the 14-bit field never
         // carries). Once every decoder has filled a chunk's A stage it has also finished reading the chunk's record
         // stage, so warp 10 hands that stage back to the record producer (one arrive a chunk).
+        // A wide unit multiplies each chunk's A stage by both of its input stages, half h into accumulator buffer
+        // (ab + h) & 1: the buffers are taken in sequence (ab counts the halves so far), so the epilogue of one half
+        // overlaps the next half's MMAs whatever the mix of wide and narrow units.
         const int blk = warp - kMmaWarp;
         const uint64_t b_desc0 = sw128_desc(smem_u32(b_ring));
         Ring ar, br, rr;
-        uint32_t ui = 0;
+        uint32_t ab = 0;
         for (int64_t ui_ = 0; ui_ < n_mine; ++ui_) {
             const TcUnit u = unit_at(ui_);
             if (!u.live) continue;
             const int nck = (int)(op.cls[u.c].cols / kKC);
-            const uint32_t buf = ui & 1, uph = (ui >> 1) & 1;
-            mbar_wait_warp(&acc_empty[buf], uph ^ 1, op.err);
+            const int nh = WIDE && u.nr > kNT ? 2 : 1;
+            for (int hh = 0; hh < nh; ++hh)
+                mbar_wait_warp(&acc_empty[(ab + hh) & 1], (((ab + hh) >> 1) & 1) ^ 1, op.err);
             tc_fence_after();
-            const uint32_t d = tmem + buf * (2 * kNT);
-            for (int ck = 0; ck < nck; ++ck, ar.next(kStA), br.next(kStB), rr.next(Cfg::ST_R)) {
+            for (int ck = 0; ck < nck; ++ck, ar.next(kStA), rr.next(Cfg::ST_R)) {
                 mbar_wait2_warp(&a_full[ar.s], ar.ph, &b_full[br.s], br.ph, op.err);
+                Ring b2 = br;
+                if (nh == 2) {
+                    b2.next(kStB);
+                    mbar_wait_warp(&b_full[b2.s], b2.ph, op.err);
+                }
                 tc_fence_after();
                 if (blk == 0 && lane == 0) mbar_arrive(&r_empty[rr.s]);
                 __syncwarp();
-                const uint32_t ta = tmem + kAccCols + ar.s * kAStageCols;
-                const uint64_t db = b_desc0 + (uint64_t)((br.s * 2 * kBHalf) >> 4);
-                const uint64_t dbb = db + (uint64_t)(((GU ? blk : 0) * kBHalf) >> 4);
-                umma_block8_el(d + blk * kNT, ta + blk * (kKC / 2), dbb, dbb + (uint64_t)(kBTile >> 4), ck ? 1u : 0u);
+                const uint32_t ta = tmem + kAccCols + ar.s * kAStageCols + blk * (kKC / 2);
+                for (int hh = 0; hh < nh; ++hh, br.next(kStB)) {
+                    const uint32_t d = tmem + ((ab + hh) & 1) * (2 * kNT) + blk * kNT;
+                    const uint64_t dbb = b_desc0 + (uint64_t)((br.s * 2 * kBHalf + (GU ? blk : 0) * kBHalf) >> 4);
+                    umma_block8_el(d, ta, dbb, dbb + (uint64_t)(kBTile >> 4), ck ? 1u : 0u);
+                    umma_commit_el(&b_empty[br.s]);
+                }
                 umma_commit_el(&a_empty[ar.s]);
-                umma_commit_el(&b_empty[br.s]);
             }
-            umma_commit_el(&acc_full[buf]);
-            ++ui;
+            for (int hh = 0; hh < nh; ++hh) umma_commit_el(&acc_full[(ab + hh) & 1]);
+            ab += nh;
         }
     } else if (warp >= kDecWarp0) {
         // ---------------------------------------------------------------- decoders
@@ -410,7 +433,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         // ---------------------------------------------------------------- epilogue (warps 0..7)
         const int q = warp & 3;                      // TMEM lanes 32q .. 32q+31 = weight rows of a block
         const int eb = warp >> 2;                    // the block this warp moves out of TMEM
-        uint32_t ui = 0;
+        uint32_t ab = 0;                             // accumulator halves taken so far (the MMA warps' sequence)
         for (int64_t ui_ = 0; ui_ < n_mine; ++ui_) {
             const TcUnit u = unit_at(ui_);
             const Exl3bClass& cl = op.cls[u.c];
@@ -442,69 +465,75 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 for (int e = 0; e < 4; ++e) dsuh[e] = dn[(int64_t)u.pair * 128 + 4 * lane + e];
             }
             (void)sd;
-            // the sorted_tok entries of this warp's rows (m = 8 l + warp, one a lane of the first eight), loaded once a
-            // unit while the accumulators are still being computed
-            int32_t tokv = -1;
-            if (lane < kNT / kEpiWarps && kEpiWarps * lane + warp < u.nr) tokv = op.sorted_tok[u.r0 + kEpiWarps * lane + warp];
-            const uint32_t buf = ui & 1, uph = (ui >> 1) & 1;
-            mbar_wait_warp(&acc_full[buf], uph, op.err);
-            tc_fence_after();
-            for (int sl = 0; sl < kNT / 16; ++sl) {
-                if (sl * 16 >= u.nr) break;
-                // TMEM -> staging [blk][16 rows][n]: this warp's block, its 32 weight rows
-                {
-                    float v[16];
-                    tmem_ld16(tmem + ((uint32_t)(32 * q) << 16) + buf * (2 * kNT) + eb * kNT + sl * 16, v);
+            // the unit's halves in turn (one for a narrow unit), each out of its accumulator buffer
+            const int nh = WIDE && u.nr > kNT ? 2 : 1;
+            for (int hh = 0; hh < nh; ++hh) {
+                const int64_t r0 = u.r0 + hh * kNT;
+                const int nr = hh ? u.nr - kNT : (u.nr < kNT ? u.nr : kNT);
+                // the sorted_tok entries of this warp's rows (m = 8 l + warp, one a lane of the first eight), loaded
+                // once a half while the accumulators are still being computed
+                int32_t tokv = -1;
+                if (lane < kNT / kEpiWarps && kEpiWarps * lane + warp < nr) tokv = op.sorted_tok[r0 + kEpiWarps * lane + warp];
+                const uint32_t buf = ab & 1, uph = (ab >> 1) & 1;
+                mbar_wait_warp(&acc_full[buf], uph, op.err);
+                tc_fence_after();
+                for (int sl = 0; sl < kNT / 16; ++sl) {
+                    if (sl * 16 >= nr) break;
+                    // TMEM -> staging [blk][16 rows][n]: this warp's block, its 32 weight rows
+                    {
+                        float v[16];
+                        tmem_ld16(tmem + ((uint32_t)(32 * q) << 16) + buf * (2 * kNT) + eb * kNT + sl * 16, v);
 #pragma unroll
-                    for (int j = 0; j < 16; ++j) epi[(eb * 16 + j) * kEpiCols + 32 * q + lane] = v[j];
-                }
-                asm volatile("bar.sync 2, %0;" ::"n"(kEpiWarps * 32) : "memory");
-                // rows: warp w takes rows w and w + 8 of the slice
-                for (int j = warp; j < 16; j += kEpiWarps) {
-                    const int m = sl * 16 + j;
-                    const int32_t tok = __shfl_sync(0xFFFFFFFFu, tokv, m / kEpiWarps);
-                    if (m >= u.nr || tok < 0) continue;
-                    const int64_t i = u.r0 + m;
-                    const float4 av = *reinterpret_cast<const float4*>(&epi[(0 * 16 + j) * kEpiCols + 4 * lane]);
-                    const float4 bv = *reinterpret_cast<const float4*>(&epi[(1 * 16 + j) * kEpiCols + 4 * lane]);
-                    float a[4] = { av.x, av.y, av.z, av.w }, b[4] = { bv.x, bv.y, bv.z, bv.w };
-                    had128_warp(a, lane);
-                    had128_warp(b, lane);
-                    uint16_t* y = out_row(op, i) + n0;
-                    if (GU) {
-                        float h[4];
-#pragma unroll
-                        for (int e = 0; e < 4; ++e) h[e] = silu_mul(__fmul_rn(a[e], s0[e]), __fmul_rn(b[e], s1[e]));
-                        if (dn) {
-                            hrot_scale4(h, dsuh);
-                            had128_warp(h, lane);
-                        }
-                        uint2 pk;
-                        pk.x = (uint32_t)f2h(h[0]) | ((uint32_t)f2h(h[1]) << 16);
-                        pk.y = (uint32_t)f2h(h[2]) | ((uint32_t)f2h(h[3]) << 16);
-                        if ((reinterpret_cast<uintptr_t>(y) & 7) == 0) {
-                            *reinterpret_cast<uint2*>(y) = pk;
-                        } else {
-#pragma unroll
-                            for (int e = 0; e < 4; ++e) y[e] = f2h(h[e]);
-                        }
-                    } else {
-                        float lo[4], hi[4];
-#pragma unroll
-                        for (int e = 0; e < 4; ++e) {
-                            lo[e] = __fmul_rn(a[e], s0[e]);
-                            hi[e] = __fmul_rn(b[e], s1[e]);
-                        }
-                        st4_out(op, y, lo);
-                        st4_out(op, y + 128, hi);
+                        for (int j = 0; j < 16; ++j) epi[(eb * 16 + j) * kEpiCols + 32 * q + lane] = v[j];
                     }
+                    asm volatile("bar.sync 2, %0;" ::"n"(kEpiWarps * 32) : "memory");
+                    // rows: warp w takes rows w and w + 8 of the slice
+                    for (int j = warp; j < 16; j += kEpiWarps) {
+                        const int m = sl * 16 + j;
+                        const int32_t tok = __shfl_sync(0xFFFFFFFFu, tokv, m / kEpiWarps);
+                        if (m >= nr || tok < 0) continue;
+                        const int64_t i = r0 + m;
+                        const float4 av = *reinterpret_cast<const float4*>(&epi[(0 * 16 + j) * kEpiCols + 4 * lane]);
+                        const float4 bv = *reinterpret_cast<const float4*>(&epi[(1 * 16 + j) * kEpiCols + 4 * lane]);
+                        float a[4] = { av.x, av.y, av.z, av.w }, b[4] = { bv.x, bv.y, bv.z, bv.w };
+                        had128_warp(a, lane);
+                        had128_warp(b, lane);
+                        uint16_t* y = out_row(op, i) + n0;
+                        if (GU) {
+                            float h[4];
+#pragma unroll
+                            for (int e = 0; e < 4; ++e) h[e] = silu_mul(__fmul_rn(a[e], s0[e]), __fmul_rn(b[e], s1[e]));
+                            if (dn) {
+                                hrot_scale4(h, dsuh);
+                                had128_warp(h, lane);
+                            }
+                            uint2 pk;
+                            pk.x = (uint32_t)f2h(h[0]) | ((uint32_t)f2h(h[1]) << 16);
+                            pk.y = (uint32_t)f2h(h[2]) | ((uint32_t)f2h(h[3]) << 16);
+                            if ((reinterpret_cast<uintptr_t>(y) & 7) == 0) {
+                                *reinterpret_cast<uint2*>(y) = pk;
+                            } else {
+#pragma unroll
+                                for (int e = 0; e < 4; ++e) y[e] = f2h(h[e]);
+                            }
+                        } else {
+                            float lo[4], hi[4];
+#pragma unroll
+                            for (int e = 0; e < 4; ++e) {
+                                lo[e] = __fmul_rn(a[e], s0[e]);
+                                hi[e] = __fmul_rn(b[e], s1[e]);
+                            }
+                            st4_out(op, y, lo);
+                            st4_out(op, y + 128, hi);
+                        }
+                    }
+                    asm volatile("bar.sync 2, %0;" ::"n"(kEpiWarps * 32) : "memory");
                 }
-                asm volatile("bar.sync 2, %0;" ::"n"(kEpiWarps * 32) : "memory");
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&acc_empty[buf]);
+                ++ab;
             }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&acc_empty[buf]);
-            ++ui;
         }
         // rows written through a row table may live in another GPU's memory: make them visible system-wide before
         // this thread (and so the kernel) completes, ahead of whatever flag the caller raises next
@@ -520,20 +549,20 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 }
 
 template <int BITS, int CB, bool GU>
-int launch_tc_t(const CUtensorMap& map, const Exl3bOp* op, int n_pairs, int grid, int smem, cudaStream_t st) {
-    auto kern = k_gemm_tc<BITS, CB, GU>;
+int launch_tc_t(const CUtensorMap& map, const Exl3bOp* op, int n_pairs, int grid, int smem, bool wide, cudaStream_t st) {
+    auto kern = wide ? k_gemm_tc<BITS, CB, GU, true> : k_gemm_tc<BITS, CB, GU, false>;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) return -6;
     kern<<<grid, kTcThreads, smem, st>>>(map, *op, n_pairs);
     return cudaGetLastError() == cudaSuccess ? 0 : -6;
 }
 
 template <bool GU>
-int launch_tc_b(const CUtensorMap& map, const Exl3bOp* op, int n_pairs, int grid, int smem, cudaStream_t st) {
-#define EXL3B_TC_CB(B)                                                          \
-    switch (op->codebook) {                                                     \
-    case 0: return launch_tc_t<B, 0, GU>(map, op, n_pairs, grid, smem, st);     \
-    case 1: return launch_tc_t<B, 1, GU>(map, op, n_pairs, grid, smem, st);     \
-    case 2: return launch_tc_t<B, 2, GU>(map, op, n_pairs, grid, smem, st);     \
+int launch_tc_b(const CUtensorMap& map, const Exl3bOp* op, int n_pairs, int grid, int smem, bool wide, cudaStream_t st) {
+#define EXL3B_TC_CB(B)                                                              \
+    switch (op->codebook) {                                                         \
+    case 0: return launch_tc_t<B, 0, GU>(map, op, n_pairs, grid, smem, wide, st);   \
+    case 1: return launch_tc_t<B, 1, GU>(map, op, n_pairs, grid, smem, wide, st);   \
+    case 2: return launch_tc_t<B, 2, GU>(map, op, n_pairs, grid, smem, wide, st);   \
     default: return -1;                                                         \
     }
     switch (op->bits) {
@@ -613,9 +642,17 @@ int exl3b_cuda_gemm_tc(const Exl3bOp* op, const void* xin, int64_t xin_pitch, in
     const int64_t smem = exl3b_tc_smem_bytes(op->bits) + ((op->n_expert + 1) * 4 + 15) / 16 * 16 + 16;
     if (smem > 227 * 1024) return -1;
     int grid = sm_count;
+    // wide units (decode once a 128 rows) where experts hold many rows, the wide units still outnumber the SMs
+    // several times over, and a unit's decode is long against its epilogue (an input of >= 1024 columns: gate_up's
+    // 2048, not down's 512, where the doubled epilogue cost more than the decode saved): expert parallelism's
+    // received passes, prefill over few experts. Elsewhere -- few rows an expert, or a pass whose units would leave
+    // SMs idle (one large expert) -- the 64-row units, whose kernel carries no wide-unit code.
+    const int64_t n_exp = op->n_expert > 0 ? op->n_expert : 1;
+    const bool wide = op->x_cols >= kWideMinCols && op->T >= (int64_t)kUG * n_exp &&
+                      (op->T / kUG) * n_pairs >= (int64_t)kWideUnitsPerSm * sm_count;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    return gu ? launch_tc_b<true>(map, op, n_pairs, grid, (int)smem, st)
-              : launch_tc_b<false>(map, op, n_pairs, grid, (int)smem, st);
+    return gu ? launch_tc_b<true>(map, op, n_pairs, grid, (int)smem, wide, st)
+              : launch_tc_b<false>(map, op, n_pairs, grid, (int)smem, wide, st);
 }
 
 }  // extern "C"

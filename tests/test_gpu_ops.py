@@ -236,6 +236,31 @@ def test_gate_up_down_equals_its_pair(dev, plugin):
     assert np.array_equal(y, dn.run(plugin, device=True)["y"])
 
 
+@pytest.mark.parametrize("op", ["moe_exl3_down", "moe_exl3_gate_up"])
+def test_wide_units_equal_the_64_row_units(dev, plugin, op):
+    """Passes of many rows an expert over a wide input run the tensor-core kernel's wide form (a unit of up to 128
+    rows decodes its weights once for both 64-row halves). Its output equals, bit for bit, the same rows run as
+    passes small enough for the 64-row units (each output row depends only on its input row and its expert; the
+    64-row units are the ones the oracle tests pin): two experts, one slot a token, the sorted rows cut in two
+    halves. The down case (a 1024-column input: down of a 1024-wide expert) takes the same path."""
+    gate_up = op == "moe_exl3_gate_up"
+    # the wide form needs >= 128 rows an expert, 4 units an SM of the pass and an input of >= 1024 columns
+    M = 19200 if gate_up else 9600
+    geom = [(1024, 2048)] if gate_up else [(2048, 1024)]
+    full = X.Case(op, 123, M=M, top_k=1, n_expert=2, geom=geom, bits=3 if gate_up else 4, codebook="mul1", h_rot=1)
+    y = full.run(plugin, device=True)["y"]
+    off = full.expert_offset.astype(np.int64)
+    half = M // 2
+    for a, b in ((0, half), (half, M)):
+        n = b - a
+        x = full.x[full.sorted_tok[a:b]] if gate_up else full.x[a:b]
+        part = X.Case(op, 0, M=n, top_k=1, n_expert=2, geom=geom, bits=full.bits, codebook="mul1", h_rot=1,
+                      planes=full.planes, x=x, sorted_tok=np.arange(n, dtype=np.int32),
+                      expert_offset=np.clip(off - a, 0, n).astype(np.int32))
+        assert np.array_equal(y[a:b], part.run(plugin, device=True)["y"]), (op, a, b)
+    assert Native().read_error() == 0
+
+
 def test_refusals_write_nothing(dev, plugin):
     case = _case(OPS[0])
     case.bits = 9          # a dtype no row serves
