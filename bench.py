@@ -359,6 +359,31 @@ def _time_steps(step, sh, reps, use_graph):
     return e0.elapsed_time(e1) / reps
 
 
+def moe_block(plugin, dev, sh, T=2048, shared_width=512):
+    """The MoE block pass (one GPU): config 3's routed layer beside a shared EXL3 expert (width 512, K = 4) whose
+    output the gather folds in through its sigmoid gate, one call of exl3b200_moe_block_forward, against the routed
+    layer alone over the same tokens. Every step reads all 512 experts' weights (679 MB, over 5x the L2)."""
+    import torch
+    from exl3b200.layer import MoeBlock
+    blk = MoeBlock(plugin, n_expert=E, hidden=H, width=W, top_k=TOPK, bits_gu=KGU, bits_dn=KDN,
+                   shared_width=shared_width, shared_bits=4, codebook=CB, max_tokens=T, seed=23, device=dev)
+    g = torch.Generator(device=dev)
+    g.manual_seed(4242)
+    blk.x[:T] = torch.randn((T, H), generator=g, device=dev).to(torch.float16)
+    blk.logits[:T] = torch.randn((T, E), generator=g, device=dev)
+    ms = _time_steps(lambda s: blk.forward(T, s), sh, 10, True)
+    ms_layer = _time_steps(lambda s: blk.routed.forward(T, s), sh, 10, True)
+    gu, dn = blk.routed.expert_bytes()
+    shared_bytes = blk.expert_bytes()
+    res = {"tokens": T, "shared_width": shared_width, "ms": round(ms, 4), "tokens_per_s": round(T / (ms / 1e3), 1),
+           "routed_layer_ms": round(ms_layer, 4), "shared_arm_ms": round(ms - ms_layer, 4),
+           "launches": blk.launches_per_step(T),
+           "packed_weight_gbs": round((E * (gu + dn) + shared_bytes) / (ms / 1e3) / 1e9, 1)}
+    del blk
+    torch.cuda.empty_cache()
+    return res
+
+
 def skewed_routing(layer, T, sh, world, rank, dev, use_graph):
     """Config 3 under the reference's skewed draw (tools/perfmoe.cpp:50-51): expert popularity lognormal with
     sigma 0.8 (the same draw on every rank), each token's top-10 a Gumbel-top-k sample of it -- logits = log
@@ -705,9 +730,11 @@ def bench_ours(args, rank, world, local_rank):
 
     # ---- skewed routing (config 3 under perfmoe's popularity draw) and config 5 (the 48-layer stack)
     use_graph = (world == 1 or args.transport == "p2p") and not args.profile
-    skew = stack = None
+    skew = stack = block = None
     if not args.no_sweep and not tp_mode:
         skew = skewed_routing(layer, T, sh, world, rank, dev, use_graph)
+    if not args.no_sweep and world == 1:
+        block = moe_block(plugin, dev, sh, T=T)
     if not args.no_stack and not tp_mode and use_graph:
         stack = stack48(layer, world, rank, dev, sh, use_graph)
 
@@ -781,7 +808,7 @@ def bench_ours(args, rank, world, local_rank):
                                "down_op_ms": round(dn_ms, 4)}},
         "clocks": clk, "gpu_launches": int(launches_per_step * args.steps),
         "e2e": e2e, "cpu_baseline": cpu, "sweep": sweep, "bitrate_sweep": bitrates, "single_expert": singles,
-        "skewed_routing": skew, "stack48": stack, "wall_s": round(wall, 3),
+        "skewed_routing": skew, "moe_block": block, "stack48": stack, "wall_s": round(wall, 3),
         "ep_phases_ms": ep_phases,
     }
     if multi_check is not None:

@@ -155,6 +155,41 @@ int     exl3b200_moe_layer_carve(const Exl3bLayerDesc* desc, int64_t max_tokens,
 int     exl3b200_moe_layer_forward(const Exl3bLayerDesc* desc, const Exl3bLayerBufs* bufs, const uint16_t* x,
                                    const float* logits, int64_t n_tok, void* out, int out_dtype, void* stream);
 
+/* The MoE block pass without the engine (architectures/qwen4exp_exl3/rad_block_moe_exl3.h:1763-1967): the routed
+ * layer beside the shared expert, the gather folding the shared arm in through its one-column sigmoid gate, as the
+ * engine's moe_gather with act "sigmoid" does (rad_block_moe_exl3.h:1535-1548, 1961-1965):
+ *   out[t] = sum over t's routed slots, ascending, of w * down row  +  sigmoid(g[t]) * shared(x[t]),
+ *   g[t] = sum over h of x[t][h] * sgate_w[h] (f32),
+ * the shared term added as one more weighted row (product, then sum, each rounded in f32). shared = the shared
+ * expert's gate_up (h_rot 1) then down (h_rot 1) through the same plugin rows (n_expert 1, every token its own sorted
+ * row). desc->shared: n_expert = n_local = 1, expert_base 0, top_k 1, hidden = desc->routed.hidden, its own width and
+ * bitrates; sgate_w f16 [hidden], 16-byte aligned. Buffers: one device block (exl3b200_moe_block_work_bytes), cut by
+ * exl3b200_moe_block_carve into the routed layer's and the shared expert's Exl3bLayerBufs (shared.y_rows is the
+ * shared arm's bf16 output). The forward enqueues only. Not built here: the protected experts (the reference serves
+ * them with FP8 grouped GEMMs over the trailing run of the offsets) and the norm and residual add around the block.
+ *   exl3b200_moe_gather_fold: the fold alone (rows, sout, x, gate_w, y 16-byte aligned; row_pitch, width, x_cols
+ *     multiples of 8; y_dtype RAD_F32 or RAD_BF16; work as exl3b200_moe_gather's).
+ *   exl3b200_identity_routing: sorted_tok[i] = i for i < n_tok, expert_offset = {0, n_tok} (the shared expert's). */
+typedef struct Exl3bBlockDesc {
+    Exl3bLayerDesc  routed;
+    Exl3bLayerDesc  shared;
+    const void*     sgate_w;
+} Exl3bBlockDesc;
+typedef struct Exl3bBlockBufs {
+    Exl3bLayerBufs  routed;
+    Exl3bLayerBufs  shared;
+} Exl3bBlockBufs;
+int64_t exl3b200_moe_block_work_bytes(const Exl3bBlockDesc* desc, int64_t max_tokens);
+int     exl3b200_moe_block_carve(const Exl3bBlockDesc* desc, int64_t max_tokens, void* work, int64_t work_bytes,
+                                 Exl3bBlockBufs* bufs);
+int     exl3b200_moe_block_forward(const Exl3bBlockDesc* desc, const Exl3bBlockBufs* bufs, const uint16_t* x,
+                                   const float* logits, int64_t n_tok, void* out, int out_dtype, void* stream);
+int     exl3b200_moe_gather_fold(const uint16_t* rows, int64_t row_pitch, const int32_t* sorted_tok, int64_t n_rows,
+                                 const float* w, int64_t n_tok, int64_t top_k, int64_t width, const uint16_t* sout,
+                                 const uint16_t* x, int64_t x_cols, const uint16_t* gate_w, void* y, int y_dtype,
+                                 void* work, void* stream);
+int     exl3b200_identity_routing(int64_t n_tok, int32_t* sorted_tok, int32_t* expert_offset, void* stream);
+
 /* Expert parallelism (one process a GPU; expert e held by rank e / n_local; no counterpart in the reference,
  * which runs on one device -- the engine's EP plumbing would call these around its all-to-alls):
  *   ep_pack:      after moe_scatter over ALL n_local * world experts (sorted_pairs, expert_offset), for sorted

@@ -255,6 +255,65 @@ int exl3b200_moe_layer_forward(const Exl3bLayerDesc* d, const Exl3bLayerBufs* b,
 }
 
 /* ------------------------------------------------------------------------------------------------------------------
+ * The MoE block: the routed layer, the shared expert over every token, the gather folding the shared arm in. */
+
+static int check_block(const Exl3bBlockDesc* d) {
+    if (!d) return RAD_E_INVAL;
+    int rc = check_desc(&d->routed);
+    if (rc == RAD_OK) rc = check_desc(&d->shared);
+    if (rc != RAD_OK) return rc;
+    const Exl3bLayerDesc* s = &d->shared;
+    if (s->n_expert != 1 || s->n_local != 1 || s->expert_base != 0 || s->top_k != 1 || s->hidden != d->routed.hidden)
+        return RAD_E_SHAPE;
+    if (!d->sgate_w || ((uintptr_t)d->sgate_w & 15)) return RAD_E_INVAL;
+    return RAD_OK;
+}
+
+int64_t exl3b200_moe_block_work_bytes(const Exl3bBlockDesc* d, int64_t max_tokens) {
+    if (check_block(d) != RAD_OK || max_tokens < 1) return -1;
+    const int64_t r = exl3b200_moe_layer_work_bytes(&d->routed, max_tokens);
+    const int64_t s = exl3b200_moe_layer_work_bytes(&d->shared, max_tokens);
+    return r < 0 || s < 0 ? -1 : up256(r) + s + 256;
+}
+
+int exl3b200_moe_block_carve(const Exl3bBlockDesc* d, int64_t max_tokens, void* work, int64_t work_bytes,
+                             Exl3bBlockBufs* b) {
+    if (!b || !work || check_block(d) != RAD_OK || max_tokens < 1) return RAD_E_INVAL;
+    const int64_t need = exl3b200_moe_block_work_bytes(d, max_tokens);
+    if (need < 0 || work_bytes < need) return RAD_E_SCRATCH;
+    const int64_t r = exl3b200_moe_layer_work_bytes(&d->routed, max_tokens);
+    uint8_t* p = (uint8_t*)(((uintptr_t)work + 255) / 256 * 256);
+    int rc = exl3b200_moe_layer_carve(&d->routed, max_tokens, p, r, &b->routed);
+    if (rc != RAD_OK) return rc;
+    p += up256(r);
+    return exl3b200_moe_layer_carve(&d->shared, max_tokens, p, need - (p - (uint8_t*)work),
+                                    &b->shared);
+}
+
+int exl3b200_moe_block_forward(const Exl3bBlockDesc* d, const Exl3bBlockBufs* b, const uint16_t* x,
+                               const float* logits, int64_t T, void* out, int out_dtype, void* stream) {
+    int rc = check_block(d);
+    if (rc != RAD_OK) return rc;
+    if (!b || !x || !logits || !out || T < 0 || T > b->routed.max_tokens || T > b->shared.max_tokens)
+        return RAD_E_INVAL;
+    if (out_dtype != RAD_F32 && out_dtype != RAD_BF16) return RAD_E_DTYPE;
+    if (T == 0) return RAD_OK;
+    const Exl3bLayerDesc* r = &d->routed;
+    /* the routed chain, then the shared arm over the same input (every token one row of its one expert) */
+    rc = layer_experts(r, &b->routed, x, logits, T, 0, stream);
+    if (rc != RAD_OK) return rc;
+    rc = exl3b200_identity_routing(T, b->shared.sorted_tok, b->shared.expert_offset, stream);
+    if (rc != 0) return rc;
+    const Pass s = layer_pass(&d->shared, &b->shared, x, T);
+    rc = run_ops(&d->shared, &s, b->shared.gu_scratch, b->shared.gu_scratch_bytes, b->shared.dn_scratch,
+                 b->shared.dn_scratch_bytes, 0, 0, 0, stream);
+    if (rc != RAD_OK) return rc;
+    return exl3b200_moe_gather_fold(b->routed.y_rows, r->hidden, b->routed.sorted_tok, T * r->top_k, b->routed.w, T,
+                                    r->top_k, r->hidden, b->shared.y_rows, x, r->hidden, d->sgate_w, out, out_dtype,
+                                    b->routed.gather_work, stream);
+}
+
+/* ------------------------------------------------------------------------------------------------------------------
  * Expert parallelism over peer memory: the whole step of one rank. Rank r serves experts [r n_local, (r+1) n_local)
  * and routes its own tokens; the window layout and the exchange kernels are exl3b200_p2p.cu's. */
 

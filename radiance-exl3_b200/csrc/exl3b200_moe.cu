@@ -6,6 +6,7 @@
 //                     contract of include/exl3_abi.h:96-158 (sorted_tok, expert_offset, -1 past the live count)
 //   k_gather          y[t] = sum over slots ascending of w[t,s] * row of (t,s), f32 (docs/OPS-exl3.md:195-196)
 #include <cuda_runtime.h>
+#include <cuda_fp16.h>
 #include <cuda_bf16.h>
 #include <stdint.h>
 
@@ -448,6 +449,70 @@ __global__ void k_gather_small(const uint16_t* __restrict__ rows, int64_t pitch,
     }
 }
 
+// The gather with the shared expert folded in (the engine's moe_gather with act "sigmoid" over the routed rows, the
+// shared arm's output and its one-column gate: architectures/qwen4exp_exl3/rad_block_moe_exl3.h:1535-1548, 1961-1965):
+// y[t] = (the routed sum of k_gather_v8, slots in ascending order) + sigmoid(g[t]) * sout[t], the shared term added
+// as one more weighted row (product then sum, each rounded in f32), g[t] = sum over h of x[t][h] * gate_w[h] (f16
+// operands, f32 products and sums), sigmoid(g) = 1 / (1 + exp(-g)) in f32. One block a token; SMALL: the token's
+// slots found in sorted_tok (k_gather_small's way), else through the inverse map pos.
+template <typename OutT, bool SMALL>
+__global__ void __launch_bounds__(256) k_gather_fold(const uint16_t* __restrict__ rows, int64_t pitch,
+                                                     const int32_t* __restrict__ map, int64_t n_rows,
+                                                     const float* __restrict__ w, int top_k, int64_t width,
+                                                     const uint16_t* __restrict__ sout, const uint16_t* __restrict__ x,
+                                                     int64_t x_cols, const uint16_t* __restrict__ gate_w,
+                                                     OutT* __restrict__ y) {
+    __shared__ int32_t spos[kGatherSmallSlots];
+    __shared__ float part[8];
+    const int64_t t = blockIdx.x;
+    const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+    // the shared gate: each thread 8 columns at a time, then the warps' sums, then the block's (fixed order)
+    float g = 0.f;
+    for (int64_t h = 8 * (int64_t)tid; h < x_cols; h += 8 * (int64_t)blockDim.x) {
+        const uint4 xv = *reinterpret_cast<const uint4*>(x + t * x_cols + h);
+        const uint4 gv = *reinterpret_cast<const uint4*>(gate_w + h);
+        const uint32_t xa[4] = { xv.x, xv.y, xv.z, xv.w }, ga[4] = { gv.x, gv.y, gv.z, gv.w };
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const float xf = __half2float(__ushort_as_half((uint16_t)(xa[j >> 1] >> (16 * (j & 1)))));
+            const float gf = __half2float(__ushort_as_half((uint16_t)(ga[j >> 1] >> (16 * (j & 1)))));
+            g = __fadd_rn(g, __fmul_rn(xf, gf));
+        }
+    }
+#pragma unroll
+    for (int d = 16; d > 0; d >>= 1) g = __fadd_rn(g, __shfl_xor_sync(0xFFFFFFFFu, g, d));
+    if (lane == 0) part[wid] = g;
+    if (SMALL) {
+        for (int s = tid; s < top_k; s += blockDim.x) spos[s] = -1;
+    }
+    __syncthreads();
+    g = 0.f;
+    for (int i = 0; i < (int)(blockDim.x >> 5); ++i) g = __fadd_rn(g, part[i]);
+    const float sig = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-g)));
+    const int32_t* pos_t = map + t * top_k;
+    if (SMALL) {
+        const int64_t f0 = t * top_k;
+        for (int64_t i = tid; i < n_rows; i += blockDim.x) {
+            const int32_t f = map[i];
+            if (f >= f0 && f < f0 + top_k) spos[f - f0] = (int32_t)i;
+        }
+        __syncthreads();
+        pos_t = spos;
+    }
+    for (int64_t n = 8 * (int64_t)tid; n < width; n += 8 * (int64_t)blockDim.x) {
+        float acc[8];
+        exl3b::gather_row8(rows, pitch, pos_t, w + t * top_k, top_k, n, acc);
+        const uint4 sv = *reinterpret_cast<const uint4*>(sout + t * width + n);
+        const uint32_t su[4] = { sv.x, sv.y, sv.z, sv.w };
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const float b = __bfloat162float(__ushort_as_bfloat16((uint16_t)(su[j >> 1] >> (16 * (j & 1)))));
+            acc[j] = __fadd_rn(acc[j], __fmul_rn(sig, b));
+        }
+        gst8(y + t * width + n, acc);
+    }
+}
+
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
 }  // namespace
@@ -612,6 +677,56 @@ int exl3b200_moe_gather_bf16(const uint16_t* rows, int64_t row_pitch, const int3
                              void* stream) {
     return gather_impl(rows, row_pitch, sorted_tok, n_rows, w, n_tok, top_k, width,
                        reinterpret_cast<__nv_bfloat16*>(y), work, stream);
+}
+
+// The gather with the shared arm folded in (k_gather_fold). rows, sout, x, gate_w and y 16-byte aligned; row_pitch,
+// width and x_cols multiples of 8; y f32 (y_dtype RAD_F32 = 1) or bf16 (RAD_BF16 = 3); work as exl3b200_moe_gather's.
+int exl3b200_moe_gather_fold(const uint16_t* rows, int64_t row_pitch, const int32_t* sorted_tok, int64_t n_rows,
+                             const float* w, int64_t n_tok, int64_t top_k, int64_t width, const uint16_t* sout,
+                             const uint16_t* x, int64_t x_cols, const uint16_t* gate_w, void* y, int y_dtype,
+                             void* work, void* stream) {
+    if (!rows || !sorted_tok || !w || !sout || !x || !gate_w || !y || !work || n_tok < 0 || n_rows < 0 || top_k < 1 ||
+        width < 8 || x_cols < 8)
+        return -12;
+    if (top_k > INT32_MAX || n_tok > INT32_MAX / top_k || width > INT32_MAX) return -1;
+    if (y_dtype != 1 && y_dtype != 3) return -2;
+    if (!aligned16(rows) || !aligned16(sout) || !aligned16(x) || !aligned16(gate_w) || !aligned16(y) ||
+        row_pitch % 8 || width % 8 || x_cols % 8)
+        return -3;
+    if (n_tok == 0) return 0;
+    cudaStream_t st = as_stream(stream);
+#define EXL3B_FOLD(OUT, SMALL, MAP)                                                                                   \
+    k_gather_fold<OUT, SMALL><<<(unsigned)n_tok, 256, 0, st>>>(rows, row_pitch, MAP, n_rows, w, (int)top_k, width,     \
+                                                              sout, x, x_cols, gate_w, static_cast<OUT*>(y))
+    if (n_rows <= kGatherSmallRows && top_k <= kGatherSmallSlots) {
+        if (y_dtype == 1) EXL3B_FOLD(float, true, sorted_tok);
+        else EXL3B_FOLD(__nv_bfloat16, true, sorted_tok);
+        return cudaGetLastError() == cudaSuccess ? 0 : -6;
+    }
+    int32_t* pos = static_cast<int32_t*>(work);
+    if (cudaMemsetAsync(pos, 0xFF, (size_t)(n_tok * top_k) * 4, st) != cudaSuccess) return -6;
+    if (n_rows > 0)
+        exl3b::k_invert<<<(unsigned)((n_rows + 255) / 256), 256, 0, st>>>(sorted_tok, n_rows, n_tok * top_k, pos);
+    if (y_dtype == 1) EXL3B_FOLD(float, false, pos);
+    else EXL3B_FOLD(__nv_bfloat16, false, pos);
+#undef EXL3B_FOLD
+    return cudaGetLastError() == cudaSuccess ? 0 : -6;
+}
+
+// The shared expert's routing: every token its own sorted row (sorted_tok[i] = i), one expert holding all n_tok.
+__global__ void k_identity_routing(int64_t n_tok, int32_t* __restrict__ sorted_tok, int32_t* __restrict__ offset) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n_tok) sorted_tok[i] = (int32_t)i;
+    if (i == 0) {
+        offset[0] = 0;
+        offset[1] = (int32_t)n_tok;
+    }
+}
+int exl3b200_identity_routing(int64_t n_tok, int32_t* sorted_tok, int32_t* expert_offset, void* stream) {
+    if (!sorted_tok || !expert_offset || n_tok < 0 || n_tok > INT32_MAX) return -12;
+    k_identity_routing<<<(unsigned)((n_tok + 255) / 256 > 0 ? (n_tok + 255) / 256 : 1), 256, 0, as_stream(stream)>>>(
+        n_tok, sorted_tok, expert_offset);
+    return cudaGetLastError() == cudaSuccess ? 0 : -6;
 }
 
 // ------------------------------------------------------------------------------------------ the gather, allocating nothing

@@ -393,6 +393,60 @@ class MoeLayer:
         return int((np.diff(off) > 0).sum())
 
 
+class MoeBlock:
+    """The MoE block pass (architectures/qwen4exp_exl3/rad_block_moe_exl3.h:1763-1967) through the library's C driver,
+    exl3b200_moe_block_forward: the routed layer beside a shared EXL3 expert over every token, the gather folding the
+    shared arm in through its one-column sigmoid gate, out[t] = routed[t] + sigmoid(x[t] . sgate_w) * shared(x[t]).
+    `routed` is a MoeLayer (its weights and buffers), `shared` a one-expert MoeLayer (top_k 1) of width
+    `shared_width`; sgate_w f16 [hidden], seeded N(0, 1/hidden). The protected experts and the norm / residual add
+    around the block are not part of it."""
+
+    def __init__(self, plugin, *, n_expert=512, hidden=2048, width=512, top_k=10, bits_gu=3, bits_dn=4,
+                 shared_width=512, shared_bits=4, codebook="mul1", max_tokens=2048, seed=0, device="cuda"):
+        import torch
+        from .native import BlockBufs, BlockDesc
+        self.torch = torch
+        self.routed = MoeLayer(plugin, n_expert=n_expert, hidden=hidden, width=width, top_k=top_k, bits_gu=bits_gu,
+                               bits_dn=bits_dn, codebook=codebook, max_tokens=max_tokens, seed=seed, device=device)
+        self.shared = MoeLayer(plugin, n_expert=1, hidden=hidden, width=shared_width, top_k=1, bits_gu=shared_bits,
+                               bits_dn=shared_bits, codebook=codebook, max_tokens=max_tokens, seed=seed + 104729,
+                               device=device)
+        self.native, self.H, self.max_tokens = self.routed.native, hidden, max_tokens
+        dev = self.routed.dev
+        g = torch.Generator(device=dev)
+        g.manual_seed(seed + 7)
+        self.sgate_w = (torch.randn(hidden, generator=g, device=dev) / hidden ** 0.5).to(torch.float16)
+        self.x, self.logits = self.routed.x, self.routed.logits
+        self.out = torch.empty((max_tokens, hidden), dtype=torch.float32, device=dev)
+        d = self.desc = BlockDesc()
+        d.routed, d.shared, d.sgate_w = self.routed.desc, self.shared.desc, self.sgate_w.data_ptr()
+        b = self.bufs = BlockBufs()
+        b.routed, b.shared = self.routed.bufs, self.shared.bufs
+
+    def forward(self, T, stream, x=None, logits=None, out=None):
+        """The block over the first T tokens of x / logits (self.x / self.logits by default) into out (f32 or bf16
+        [T, hidden]; self.out by default)."""
+        o = self.out if out is None else out
+        xx = self.x if x is None else x
+        lg = self.logits if logits is None else logits
+        self.desc.routed, self.desc.shared = self.routed.desc, self.shared.desc     # the current weight sets
+        self.native.block_forward(self.desc, self.bufs, xx.data_ptr(), lg.data_ptr(), T, o.data_ptr(),
+                                  3 if o.dtype == self.torch.bfloat16 else 1, stream)
+
+    def launches_per_step(self, T):
+        """The routed layer's launches less its gather, the shared expert's identity routing, its gate_up (+ prep)
+        and down, and the fold (one launch up to 4096 routed rows; else the map's memset aside, two)."""
+        r, s = self.routed, self.shared
+        fold = 1 if T * r.k <= 4096 and r.k <= 32 else 2
+        return r.route_launches(T) + r.expert_launches(T) + 1 + s.expert_launches(T) + fold
+
+    def expert_bytes(self):
+        """Algorithmic bytes of a step: every live routed expert's (as MoeLayer) plus the shared expert's and the
+        gate column."""
+        gu, dn = self.shared.expert_bytes()
+        return gu + dn + 2 * self.H
+
+
 class Linears:
     """`n` independent EXL3 linears of one shape (config 4: out `rows`, in `cols`, K bits), each served by one call of
     the moe_exl3_down row as the engine issues a single linear (n_expert 1, top_k 1, every input row routed to it,

@@ -24,6 +24,16 @@ class LayerBufs(C.Structure):
                 ("dn_scratch", _VP), ("dn_scratch_bytes", _I64), ("gather_work", _VP)]
 
 
+class BlockDesc(C.Structure):
+    """Exl3bBlockDesc (include/exl3b200.h)."""
+    _fields_ = [("routed", LayerDesc), ("shared", LayerDesc), ("sgate_w", _VP)]
+
+
+class BlockBufs(C.Structure):
+    """Exl3bBlockBufs (include/exl3b200.h)."""
+    _fields_ = [("routed", LayerBufs), ("shared", LayerBufs)]
+
+
 class EpDesc(C.Structure):
     """Exl3bEpDesc (include/exl3b200.h)."""
     _fields_ = [("layer", LayerDesc), ("rank", _I64), ("world", _I64), ("max_tokens", _I64),
@@ -107,6 +117,14 @@ class Native:
         L.exl3b200_moe_layer_forward.argtypes = [C.POINTER(LayerDesc), C.POINTER(LayerBufs), _VP, _VP, _I64, _VP,
                                                  C.c_int, _VP]
         L.exl3b200_set_peer_wait_ns.argtypes = [_I64]
+        L.exl3b200_moe_block_work_bytes.restype = _I64
+        L.exl3b200_moe_block_work_bytes.argtypes = [C.POINTER(BlockDesc), _I64]
+        L.exl3b200_moe_block_carve.argtypes = [C.POINTER(BlockDesc), _I64, _VP, _I64, C.POINTER(BlockBufs)]
+        L.exl3b200_moe_block_forward.argtypes = [C.POINTER(BlockDesc), C.POINTER(BlockBufs), _VP, _VP, _I64, _VP,
+                                                 C.c_int, _VP]
+        L.exl3b200_moe_gather_fold.argtypes = [_VP, _I64, _VP, _I64, _VP, _I64, _I64, _I64, _VP, _VP, _I64, _VP, _VP,
+                                               C.c_int, _VP, _VP]
+        L.exl3b200_identity_routing.argtypes = [_I64, _VP, _VP, _VP]
         L.exl3b200_ep_window_layout.restype = _I64
         L.exl3b200_ep_window_layout.argtypes = [_I64, _I64, _I64, _I64, C.POINTER(_I64)]
         L.exl3b200_tp_window_layout.restype = _I64
@@ -351,3 +369,21 @@ class Native:
         """bufs: the slice layer's LayerBufs; out f32; marks: None or marks_array() of 7 events."""
         self._check(self.lib.exl3b200_tp_step_forward(C.byref(desc), C.byref(bufs), x, logits, n_tok, out, out_pitch,
                                                       stream, marks), "exl3b200_tp_step_forward")
+
+    # ---- the MoE block (routed layer + shared expert, the fold; exl3b200_layer.c)
+    def block_work_bytes(self, desc, max_tokens):
+        n = int(self.lib.exl3b200_moe_block_work_bytes(C.byref(desc), max_tokens))
+        if n < 0:
+            raise RuntimeError("exl3b200_moe_block_work_bytes: the block description was refused")
+        return n
+
+    def block_carve(self, desc, max_tokens, work, work_bytes):
+        b = BlockBufs()
+        self._check(self.lib.exl3b200_moe_block_carve(C.byref(desc), max_tokens, work, work_bytes, C.byref(b)),
+                    "exl3b200_moe_block_carve")
+        return b
+
+    def block_forward(self, desc, bufs, x, logits, n_tok, out, out_dtype, stream=0):
+        """out_dtype: 1 (RAD_F32) or 3 (RAD_BF16)."""
+        self._check(self.lib.exl3b200_moe_block_forward(C.byref(desc), C.byref(bufs), x, logits, n_tok, out, out_dtype,
+                                                        stream), "exl3b200_moe_block_forward")

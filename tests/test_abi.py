@@ -323,3 +323,39 @@ def test_step_descriptions_are_refused_before_any_device_work():
     rc = nat.lib.exl3b200_tp_step_forward(C.byref(t), C.byref(LayerBufs()), 1 << 30, 1 << 30, 8, 1 << 30, 2048,
                                           None, None)
     assert rc == -1
+
+
+def test_block_carve_and_refusals():
+    """The MoE block's C driver carves one caller block into the routed layer's and the shared expert's buffers
+    (host arithmetic only: fake addresses), each buffer inside the block and no two overlapping; a shared expert that
+    is not one expert of top-1 over the routed hidden size, or a misaligned gate column, is refused."""
+    from exl3b200.native import BlockDesc, Native
+    nat = Native()
+
+    def desc(sh_experts=1, sh_k=1, sh_hidden=2048, gate=1 << 20):
+        d = BlockDesc()
+        d.routed = _layer_desc(512, 512, 0)
+        d.shared = _layer_desc(sh_experts, sh_experts, 0, H=sh_hidden, W=1024, k=sh_k)
+        d.sgate_w = gate
+        return d
+
+    d = desc()
+    n = nat.block_work_bytes(d, 2048)
+    base = 1 << 40
+    b = nat.block_carve(d, 2048, base, n)
+    P, H = 2048 * 10, 2048
+    sizes = {}
+    for part, rows, W in (("routed", P, 512), ("shared", 2048, 1024)):
+        lb = getattr(b, part)
+        for name, nb in (("ids", rows * 4), ("w", rows * 4), ("sorted_tok", rows * 4), ("h", rows * W * 2),
+                         ("y_rows", rows * H * 2)):
+            sizes[(part, name)] = (getattr(lb, name), nb)
+        for name in ("gu_scratch", "dn_scratch"):
+            if getattr(lb, name):
+                sizes[(part, name)] = (getattr(lb, name), getattr(lb, name + "_bytes"))
+    regs = sorted((p, p + nb, k) for k, (p, nb) in sizes.items())
+    assert regs[0][0] >= base and regs[-1][1] <= base + n
+    for (s0, e0, n0), (s1, e1, n1) in zip(regs, regs[1:]):
+        assert e0 <= s1, (n0, n1)
+    for bad in (desc(sh_experts=2), desc(sh_k=2), desc(sh_hidden=1024), desc(gate=(1 << 20) + 8), desc(gate=None)):
+        assert nat.lib.exl3b200_moe_block_work_bytes(C.byref(bad), 2048) == -1
