@@ -76,28 +76,101 @@ constexpr int kPrepV = 16;                      // values a lane
 constexpr int kPrepLpb = 128 / kPrepV;          // lanes a 128-block
 constexpr int kPrepBpw = 32 / kPrepLpb;         // blocks a warp task
 
-template <int V>
-__device__ __forceinline__ void had128_xv(float v[V], int lb) {
+// Packed f32 pairs (sm_100's f32x2 arithmetic: two IEEE round-to-nearest operations an instruction).
+__device__ __forceinline__ uint64_t f2pk(float a, float b) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+    return r;
+}
+__device__ __forceinline__ void f2upk(uint64_t r, float& a, float& b) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(r));
+}
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+    uint64_t r;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ uint64_t sub2(uint64_t a, uint64_t b) {
+    uint64_t r;
+    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t r;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+    return r;
+}
+__device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
+    uint64_t r;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+
+// The 16-value form on packed pairs (v[q], v[q + 8]): stages h = 1, 2, 4 pair two packed registers element by
+// element, h = 8 the two halves of one, the cross-lane stages one f32x2 FMA a pair -- every element through the same
+// operations in the same order as the scalar form below, so the same bits.
+__device__ __forceinline__ void had128_x16_pk(float v[16], int lb) {
+    uint64_t P[8];
 #pragma unroll
-    for (int h = 1; h < V; h <<= 1)
+    for (int q = 0; q < 8; ++q) P[q] = f2pk(v[q], v[q + 8]);
 #pragma unroll
-        for (int i = 0; i < V; ++i)
-            if (!(i & h)) {
-                const float a = v[i], b = v[i + h];
-                v[i] = __fadd_rn(a, b);
-                v[i + h] = __fsub_rn(a, b);
+    for (int h = 1; h < 8; h <<= 1)
+#pragma unroll
+        for (int q = 0; q < 8; ++q)
+            if (!(q & h)) {
+                const uint64_t a = P[q], b = P[q + h];
+                P[q] = add2(a, b);
+                P[q + h] = sub2(a, b);
             }
 #pragma unroll
-    for (int m = 1; m < 128 / V; m <<= 1) {
-        const float sg = (lb & m) ? -1.0f : 1.0f;       // p + (+-1) v: exact product, one rounding
-#pragma unroll
-        for (int i = 0; i < V; ++i) {
-            const float p = __shfl_xor_sync(0xFFFFFFFFu, v[i], m);
-            v[i] = __fmaf_rn(sg, v[i], p);
-        }
+    for (int q = 0; q < 8; ++q) {
+        float a, b;
+        f2upk(P[q], a, b);
+        P[q] = f2pk(__fadd_rn(a, b), __fsub_rn(a, b));
     }
 #pragma unroll
-    for (int i = 0; i < V; ++i) v[i] = __fmul_rn(v[i], kRs);
+    for (int m = 1; m < 8; m <<= 1) {
+        const float sg = (lb & m) ? -1.0f : 1.0f;       // p + (+-1) v: exact product, one rounding
+        const uint64_t sg2 = f2pk(sg, sg);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+            float lo, hi;
+            f2upk(P[q], lo, hi);
+            const float pl = __shfl_xor_sync(0xFFFFFFFFu, lo, m), ph = __shfl_xor_sync(0xFFFFFFFFu, hi, m);
+            P[q] = fma2(sg2, P[q], f2pk(pl, ph));
+        }
+    }
+    const uint64_t rs2 = f2pk(kRs, kRs);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) f2upk(mul2(P[q], rs2), v[q], v[q + 8]);
+}
+
+template <int V>
+__device__ __forceinline__ void had128_xv(float v[V], int lb) {
+    if constexpr (V == 16) {
+        had128_x16_pk(v, lb);
+    } else {
+#pragma unroll
+        for (int h = 1; h < V; h <<= 1)
+#pragma unroll
+            for (int i = 0; i < V; ++i)
+                if (!(i & h)) {
+                    const float a = v[i], b = v[i + h];
+                    v[i] = __fadd_rn(a, b);
+                    v[i + h] = __fsub_rn(a, b);
+                }
+#pragma unroll
+        for (int m = 1; m < 128 / V; m <<= 1) {
+            const float sg = (lb & m) ? -1.0f : 1.0f;       // p + (+-1) v: exact product, one rounding
+#pragma unroll
+            for (int i = 0; i < V; ++i) {
+                const float p = __shfl_xor_sync(0xFFFFFFFFu, v[i], m);
+                v[i] = __fmaf_rn(sg, v[i], p);
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < V; ++i) v[i] = __fmul_rn(v[i], kRs);
+    }
 }
 
 // V consecutive 16-bit values as V/2 packed pairs (low half = the lower index)
