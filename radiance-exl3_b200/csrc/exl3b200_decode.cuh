@@ -211,6 +211,37 @@ __device__ __forceinline__ void decode_lane(const uint32_t* __restrict__ w, int 
 }
 
 // ------------------------------------------------------------------------------------------ 128-point rotation
+// Packed f32 pairs (sm_100's f32x2 arithmetic: two IEEE round-to-nearest operations an instruction), used by k_prep's
+// 16-value rotation. (The 4-value rotation below stays scalar: packed, the epilogues measured 1-5 % slower.)
+__device__ __forceinline__ uint64_t f2pk(float a, float b) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+    return r;
+}
+__device__ __forceinline__ void f2upk(uint64_t r, float& a, float& b) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(r));
+}
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+    uint64_t r;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ uint64_t sub2(uint64_t a, uint64_t b) {
+    uint64_t r;
+    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t r;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+    return r;
+}
+__device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
+    uint64_t r;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+
 // A warp holds one 128-vector, lane l the elements 4l .. 4l+3. Stages h = 1, 2 inside the lane, h = 4 .. 64
 // across lanes; a+b stays low, a-b goes high, exactly as common/exl3_decode.c:179-185; then x (float)(1/sqrt(128)).
 __device__ __forceinline__ void had128_warp(float v[4], int lane) {

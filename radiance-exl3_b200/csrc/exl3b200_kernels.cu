@@ -76,36 +76,6 @@ constexpr int kPrepV = 16;                      // values a lane
 constexpr int kPrepLpb = 128 / kPrepV;          // lanes a 128-block
 constexpr int kPrepBpw = 32 / kPrepLpb;         // blocks a warp task
 
-// Packed f32 pairs (sm_100's f32x2 arithmetic: two IEEE round-to-nearest operations an instruction).
-__device__ __forceinline__ uint64_t f2pk(float a, float b) {
-    uint64_t r;
-    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
-    return r;
-}
-__device__ __forceinline__ void f2upk(uint64_t r, float& a, float& b) {
-    asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(r));
-}
-__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
-    uint64_t r;
-    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
-    return r;
-}
-__device__ __forceinline__ uint64_t sub2(uint64_t a, uint64_t b) {
-    uint64_t r;
-    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
-    return r;
-}
-__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
-    uint64_t r;
-    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
-    return r;
-}
-__device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
-    uint64_t r;
-    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
-    return r;
-}
-
 // The 16-value form on packed pairs (v[q], v[q + 8]): stages h = 1, 2, 4 pair two packed registers element by
 // element, h = 8 the two halves of one, the cross-lane stages one f32x2 FMA a pair -- every element through the same
 // operations in the same order as the scalar form below, so the same bits.
